@@ -1,0 +1,445 @@
+"""Benchmark of the hybrid AdamW + Newton-Schulz Muon optimizer step on B200.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (synthetic, seeded; shapes from the reference model family):
+  hybrid_1b   (default) d_model 2048, 24 layers, FFN 8192, vocab 32000, untied lm_head;
+              Muon on the block matrices, AdamW on embed / lm_head / LayerNorm; fp32.
+  hybrid_8b   d_model 4096, 32 layers, GQA k/v [1024, 4096], FFN 14336, vocab 32000;
+              bf16 grads with fp32 master params, loss scale 2^16, bf16 param copies.
+  adamw_arena isolated fused AdamW over 2^28 fp32 params (t = 10, wd 0.1, divisor 4).
+  ns_batch    isolated Newton-Schulz on 64 x [4096, 4096] + 32 x [4096, 14336].
+  chatbot     the Chatbot(vocab 512, 2 layers, d_model 64) step (latency-bound).
+
+Rank 0 prints one JSON line. Multi-GPU runs use torchrun (one process per GPU):
+Muon matrices are owned whole by one rank, the AdamW arena is split evenly, and
+the updated params are all-gathered (NCCL) inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "hybrid AdamW+Muon step params/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ workloads
+def hybrid_model(d, n_layer, ffn, vocab, kv_dim=None):
+    """(name, shape, route) in optimizer call order (lm_head; blocks last..first:
+    ffn2, ffn, out, q, k, v, ln2.gamma, ln2.beta, ln1.gamma, ln1.beta; embed),
+    routed the tagged way: block matrices -> Muon, embed / lm_head / LN -> AdamW."""
+    kv = kv_dim or d
+    out = [("lm_head", (vocab, d), "adamw")]
+    for layer in reversed(range(n_layer)):
+        b = f"blocks.{layer}."
+        out += [(b + "ffn2", (d, ffn), "muon"), (b + "ffn", (ffn, d), "muon"),
+                (b + "out", (d, d), "muon"), (b + "q", (d, d), "muon"),
+                (b + "k", (kv, d), "muon"), (b + "v", (kv, d), "muon"),
+                (b + "ln2.gamma", (d,), "adamw"), (b + "ln2.beta", (d,), "adamw"),
+                (b + "ln1.gamma", (d,), "adamw"), (b + "ln1.beta", (d,), "adamw")]
+    out.append(("embed", (vocab, d), "adamw"))
+    return out
+
+
+WORKLOADS = {
+    "hybrid_1b": dict(model=lambda: hybrid_model(2048, 24, 8192, 32000), grad="f32",
+                      desc="hybrid step, d_model 2048, 24 layers, FFN 8192, vocab 32000"),
+    "hybrid_8b": dict(model=lambda: hybrid_model(4096, 32, 14336, 32000, kv_dim=1024),
+                      grad="bf16",
+                      desc="hybrid step, d_model 4096, 32 layers, GQA kv 1024, FFN 14336, "
+                           "vocab 32000, bf16 grads + fp32 master, loss scale 2^16"),
+    "chatbot": dict(model=lambda: [(n, s, "auto") for n, s in
+                                   __import__("magicmindnet_b200").chatbot_param_order(512, 2, 64)],
+                    grad="f32", desc="Chatbot(vocab 512, n_layer 2, d_model 64) hybrid step"),
+    "adamw_arena": dict(model=lambda: [("arena", (1 << 28,), "adamw")], grad="f32",
+                        desc="fused AdamW over 2^28 fp32 params, t=10, wd 0.1, divisor 4"),
+    "ns_batch": dict(model=lambda: [(f"sq{i}", (4096, 4096), "muon") for i in range(64)] +
+                     [(f"ffn{i}", (4096, 14336), "muon") for i in range(32)], grad="f32",
+                     desc="Newton-Schulz on 64 x [4096,4096] + 32 x [4096,14336]"),
+}
+
+
+def count_params(model):
+    n = 0
+    for _, s, _ in model:
+        k = 1
+        for d in s:
+            k *= d
+        n += k
+    return n
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i - 5] for r in self.rows if len(r) > 8 for i in range(5, 9)
+                          if r[i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(workload: str, model, sample_s: float = 15.0):
+    """The oracle (a C port of the reference's CPU step) timed on this host's
+    cores on a bounded sample of the workload, extrapolated to one full step
+    by the sample's share of the step's work. Returns a dict for the JSON line."""
+    import numpy as np
+
+    from oracle import reference_optim as R
+
+    cores = R.lib().ref_max_threads()
+    rng = np.random.default_rng(0)
+    n_total = count_params(model)
+    muon = [s for _, s, r in model if r == "muon" or (r == "auto" and R.classify_param(s) == R.MATRIX)]
+    adamw_n = n_total - sum(s[0] * s[1] for s in muon)
+    t_full = 0.0
+    parts = []
+    # AdamW: time a slice, scale by element count.
+    if adamw_n:
+        k = min(adamw_n, 1 << 24)
+        p = rng.normal(0, 0.02, k).astype(np.float32)
+        g = rng.normal(0, 1e-3, k).astype(np.float32)
+        m = np.zeros(k, np.float32)
+        v = np.zeros(k, np.float32)
+        dt = min(R.lib().ref_adamw_step_timed(R._ptr(p), R._ptr(m), R._ptr(v), R._ptr(g), k, 3e-4,
+                                               0.9, 0.95, 1e-8, 0.01, 10, 1.0, 0)
+                 for _ in range(3))
+        t_full += dt * adamw_n / k
+        parts.append(f"AdamW {k} elems x{adamw_n / k:.1f}")
+    # Newton-Schulz: one matrix per shape class, scaled down so the sample stays
+    # bounded, extrapolated by flop count.
+    classes = {}
+    for s in muon:
+        n, mm = min(s), max(s)
+        classes[(n, mm)] = classes.get((n, mm), 0) + 1
+    budget = sample_s / max(len(classes), 1)
+    for (n, mm), cnt in classes.items():
+        f_full = 5 * (4.0 * n * n * mm + 2.0 * n ** 3)
+        sn, sm = n, mm
+        while 5 * (4.0 * sn * sn * sm + 2.0 * sn ** 3) > 5e10 and sn > 64:
+            sn //= 2
+            sm //= 2
+        g = rng.normal(0, 1e-2, (sn, sm)).astype(np.float32)
+        t0 = time.perf_counter()
+        R.newton_schulz5(g, 5, order=R.GEMM_F32_FMA)
+        dt = time.perf_counter() - t0
+        f_s = 5 * (4.0 * sn * sn * sm + 2.0 * sn ** 3)
+        t_full += dt * (f_full / f_s) * cnt
+        parts.append(f"NS [{sn},{sm}] for {cnt} x [{n},{mm}] (flop-scaled)")
+        if dt > budget:
+            break
+    return {"value": n_total / t_full if t_full else None, "unit": "params/s", "cores": cores,
+            "kind": "port", "sample": "; ".join(parts), "step_s_extrapolated": t_full}
+
+
+# --------------------------------------------------------------------- ours
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    import magicmindnet_b200 as mmn
+
+    torch.cuda.set_device(local_rank)
+    dev = local_rank
+    spec = WORKLOADS[args.workload]
+    model = spec["model"]()
+    n_total = count_params(model)
+    is_8b = args.workload == "hybrid_8b"
+    if args.workload == "adamw_arena":
+        adamw = mmn.AdamWConfig(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    elif args.workload == "chatbot":
+        adamw = mmn.AdamWConfig(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    else:
+        adamw = mmn.AdamWConfig()
+    cfg = mmn.StepConfig(adamw=adamw, muon=mmn.MuonConfig(), ns_mode=args.ns_mode,
+                         grad_dtype=spec["grad"], bf16_param_shadow=is_8b, loss_scaling=is_8b,
+                         rank=rank, world_size=world, use_graph=False)
+    stream = torch.cuda.current_stream(dev)
+    step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg, device=dev,
+                             stream=stream.cuda_stream)
+    step.enable_timing(True)
+    # seeded synthetic values, generated on the device
+    gen = torch.Generator(device=f"cuda:{dev}").manual_seed(0)
+    for k, (_, s, _) in enumerate(model):
+        step.param(k).normal_(0, 0.02, generator=gen)
+        gv = step.grad(k)
+        if gv.dtype == torch.bfloat16:
+            gv.copy_((torch.randn(s, device=f"cuda:{dev}", generator=gen) * (1e-3 * 65536.0)))
+        else:
+            gv.normal_(0, 1e-2 if args.workload in ("adamw_arena", "ns_batch") else 1e-3,
+                       generator=gen)
+    if is_8b:
+        for k in range(len(model)):
+            b = step.param_bf16(k)
+            b.copy_(step.param(k))
+    if args.workload == "adamw_arena":
+        step.set_state(0, "m", np.random.default_rng(0).normal(0, 1e-3, 1 << 28).astype(np.float32))
+        step.set_state(0, "v", np.abs(np.random.default_rng(1).normal(0, 1e-4, 1 << 28)).astype(np.float32))
+        step.adamw_step = 9  # the timed steps run at t = 10, 11, ...
+    divisor = 4.0 if args.workload == "adamw_arena" else 1.0
+    torch.cuda.synchronize()
+
+    gl = step.gather_layout()
+    gathers = []
+    if world > 1:
+        import torch.distributed as dist
+        from magicmindnet_b200.step import _view
+
+        use16 = is_8b
+        for key, region in (("adamw_param", "adamw_region"), ("muon_param", "muon_region")):
+            ptr = gl[key + ("_bf16" if use16 else "")]
+            if ptr and gl[region]:
+                full = _view(ptr, (gl[region] * world,), "bf16" if use16 else "f32", dev)
+                gathers.append((full, full[rank * gl[region]:(rank + 1) * gl[region]]))
+
+    def one_step():
+        step.step(divisor)
+        if gathers:
+            import torch.distributed as dist
+
+            for full, mine in gathers:
+                dist.all_gather_into_tensor(full, mine)
+
+    inj = []
+    for i in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev)).split(",")[0])
+                          if os.environ.get("CUDA_VISIBLE_DEVICES", "").isdigit() else dev)
+    clocks.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    phase = {"adamw": [], "muon_momentum": [], "newton_schulz": [], "muon_update": [], "step": []}
+    ev0.record(stream)
+    for i in range(args.steps):
+        if is_8b and i % 100 == 50:
+            inj.append(i)  # one injected inf grad per 100 steps
+            step.grad(0).view(-1)[0] = float("inf")
+        one_step()
+        t = step.last_timing() if args.steps <= 50 or i % 10 == 0 else None
+        if t:
+            for k2, v in t.items():
+                phase[k2].append(v)
+        if is_8b and i % 100 == 50:
+            step.grad(0).view(-1)[0] = 1e-3 * 65536.0
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+
+        tt = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = n_total / (ms / 1e3)
+
+    # --- e2e: host grads in, host params out through the public API
+    e2e = None
+    if args.e2e and world == 1:
+        pin_g = [torch.empty(s, dtype=step.grad(k).dtype, pin_memory=True)
+                 for k, (_, s, _) in enumerate(model)]
+        pin_p = [torch.empty(s, dtype=torch.float32, pin_memory=True) for _, s, _ in model]
+        for k in range(len(model)):
+            pin_g[k].copy_(step.grad(k))
+        views_g = [step.grad(k) for k in range(len(model))]
+        views_p = [step.param(k) for k in range(len(model))]
+        bi = sum(t.numel() * t.element_size() for t in pin_g)
+        bo = sum(t.numel() * 4 for t in pin_p)
+        e_steps = max(1, min(args.steps, 10))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e_steps):
+            for k in range(len(model)):
+                views_g[k].copy_(pin_g[k], non_blocking=True)
+            step.step(divisor)
+            for k in range(len(model)):
+                pin_p[k].copy_(views_p[k], non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e_ms = (time.perf_counter() - t0) * 1e3 / e_steps
+        e2e = {"value": n_total / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+
+    pk, pk_kind = peaks()
+    med = {k: (statistics.median(v) if v else 0.0) for k, v in phase.items()}
+    ns_flops = step.ns_flops()
+    total, n_adamw, n_muon = step.param_counts()
+    # AdamW algorithmic bytes: read p, g, m, v and write p, m, v (28 B/param at fp32);
+    # bf16 grads read 2 B instead of 4, and the bf16 copy adds 2 B written.
+    a_bytes_per = (28 if spec["grad"] == "f32" else 26) + (2 if is_8b else 0)
+    a_elems_rank = n_adamw / world
+    comp = {
+        "adamw": {"ms": med["adamw"], "bytes_per_param": a_bytes_per,
+                  "GB/s": (a_bytes_per * a_elems_rank / (med["adamw"] / 1e3) / 1e9)
+                  if med["adamw"] else None},
+        "newton_schulz": {"ms": med["newton_schulz"], "flops": ns_flops,
+                          "TFLOP/s": (ns_flops / (med["newton_schulz"] / 1e3) / 1e12)
+                          if med["newton_schulz"] else None},
+        "muon_momentum_ms": med["muon_momentum"], "muon_update_ms": med["muon_update"],
+    }
+    if n_muon and med["newton_schulz"] > 0:
+        ach = ns_flops / (med["newton_schulz"] / 1e3) / 1e12
+        peak = pk["bf16_tflops_sustained"] if args.workload.startswith("hybrid") else pk["bf16_tflops"]
+        roof = {"bound": "tensor", "kernel": "ns_gemm (tcgen05, Gram + Square + Poly per iteration)",
+                "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "peak_source": pk_kind, "traffic": None}
+    else:
+        ach = a_bytes_per * a_elems_rank / (med["adamw"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "adamw_kernel", "achieved": ach, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "peak_source": pk_kind,
+                "traffic": None}
+    launches_per_step = 5 + 15 * len({(min(s), max(s)) for _, s, r in model if r == "muon"})
+    line = {
+        "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (NS GEMMs bf16 x bf16 -> f32)" if not is_8b else "bf16 grads/params, f32 master",
+        "data": "synthetic (seeded normal params/grads)",
+        "config": {"workload": args.workload, "desc": spec["desc"], "params": n_total,
+                   "adamw_params": n_adamw, "muon_params": n_muon, "ns_mode": args.ns_mode,
+                   "parallelism": f"shard{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (no flush needed)"},
+        "roofline": roof, "components": comp, "clocks": clk, "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if is_8b:
+        line["loss_scale"] = dict(zip(("scale", "skipped_steps"), step.loss_scale()))
+        line["injected_inf_steps"] = inj
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, model)
+    step.close()
+    return line
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    spec = WORKLOADS[args.workload]
+    model = spec["model"]()
+    vals = []
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(args.workload, model, sample_s=2.0)
+        if i >= args.warmup:
+            vals.append(cb)
+    v = statistics.median(c["value"] for c in vals)
+    ms = statistics.median(c["step_s_extrapolated"] for c in vals) * 1e3
+    cb = dict(vals[-1])
+    cb["value"] = v
+    return {"metric": METRIC, "value": v, "unit": "params/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "data": "synthetic (seeded normal params/grads)",
+            "config": {"workload": args.workload, "desc": spec["desc"],
+                       "params": count_params(model)},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "params/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="hybrid_1b", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16"])
+    ap.add_argument("--no-e2e", dest="e2e", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    line = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,298 @@
+/*
+ * mmn_optim.h — C ABI of the B200-native MagicMindNet optimizer step.
+ *
+ * This is the boundary a rewritten `mmn-cuda` crate binds with `extern "C"`.
+ * Every entry point replaces one item of the reference's Rust API
+ * (crates/mmn-optim/src/lib.rs unless stated) and keeps its argument meaning:
+ * `param` is updated in place, `grad` is read, optimizer state lives with the
+ * handle (on the GPU) keyed by the caller's id exactly like the reference's
+ * HashMaps. The library owns device buffers; the caller owns host buffers.
+ *
+ * Conventions
+ *   - Return 0 (MMN_OK) on success, a negative MMN_E_* code on failure;
+ *     mmn_last_error() returns a message for the calling thread's last failure.
+ *     Where the reference panics (shape mismatch, lib.rs:148,161 unwrap) these
+ *     calls return MMN_E_SHAPE instead.
+ *   - `mem` says where pointers live: MMN_MEM_HOST (pageable or pinned host
+ *     memory; the call copies in, runs and copies out before returning) or
+ *     MMN_MEM_DEVICE (device memory of the handle's GPU; work is enqueued on
+ *     the handle's stream and the call returns without synchronising).
+ *   - One handle is used by one thread at a time (the reference's `&mut self`).
+ *   - No pointer argument carries a C++ or torch type; shapes are int64 arrays.
+ */
+#ifndef MMN_OPTIM_H
+#define MMN_OPTIM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MMN_OPTIM_ABI_VERSION 1
+
+/* status codes */
+#define MMN_OK 0
+#define MMN_E_INVALID (-1)   /* null pointer, bad enum, bad size */
+#define MMN_E_SHAPE (-2)     /* shape differs from the state registered for the id */
+#define MMN_E_CUDA (-3)      /* a CUDA runtime call failed */
+#define MMN_E_NO_DEVICE (-4) /* cuda requested without a usable GPU (MmnError::cuda_missing) */
+#define MMN_E_STATE (-5)     /* call out of order (e.g. step before finalize) */
+#define MMN_E_OOM (-6)       /* device allocation failed */
+#define MMN_E_TIMEOUT (-7)   /* a kernel gave up a bounded wait and reported it */
+#define MMN_E_UNSUPPORTED (-8)
+
+/* where a pointer lives */
+#define MMN_MEM_HOST 0
+#define MMN_MEM_DEVICE 1
+
+/* element types */
+#define MMN_DTYPE_F32 0
+#define MMN_DTYPE_BF16 1
+
+/* routing of one tensor (HybridOptimizer::classify_param, lib.rs:196-202) */
+#define MMN_ROUTE_AUTO 0  /* the reference rule: 2-D with both dims > 1 -> Muon */
+#define MMN_ROUTE_MUON 1
+#define MMN_ROUTE_ADAMW 2
+
+/* Newton-Schulz arithmetic */
+#define MMN_NS_REFERENCE 0 /* lib.rs:112-120 rounding points; B = b*A + c*A2 kept exact */
+#define MMN_NS_BF16 1      /* B rounded to bf16 before B*X (faster; looser tolerance) */
+
+/* AdamWConfig, lib.rs:6-11 (defaults lib.rs:13-21: 3e-4, (0.9, 0.95), 1e-8, 0.01) */
+typedef struct {
+    float lr;
+    float beta1;
+    float beta2;
+    float eps;
+    float weight_decay;
+} mmn_adamw_config;
+
+/* MuonConfig, lib.rs:63-69 (defaults lib.rs:71-80: 0.02, 0.95, true, 5) */
+typedef struct {
+    float lr;
+    float momentum;
+    int32_t nesterov;
+    int32_t ns_steps;
+} mmn_muon_config;
+
+typedef struct mmn_adamw mmn_adamw_t;
+typedef struct mmn_muon mmn_muon_t;
+typedef struct mmn_hybrid mmn_hybrid_t;
+typedef struct mmn_optim mmn_optim_t;
+
+/* ------------------------------------------------------------ environment */
+
+/* crates/mmn-cuda/src/lib.rs:5-12 is_available(): 1 when a CUDA device with
+ * compute capability 10.0 (B200) is usable, else 0. */
+int mmn_cuda_is_available(void);
+
+/* crates/mmn-core/src/device.rs:29-37 Device::require_cuda_available_checked:
+ * MMN_E_NO_DEVICE when cuda_requested and no usable device, else MMN_OK. */
+int mmn_require_cuda(int cuda_requested);
+
+/* Message for the calling thread's most recent failure ("" if none). */
+const char *mmn_last_error(void);
+
+/* MMN_OPTIM_ABI_VERSION of the loaded library. */
+int mmn_abi_version(void);
+
+/* AdamWConfig::default() / MuonConfig::default() (lib.rs:13-21, 71-80). */
+mmn_adamw_config mmn_adamw_config_default(void);
+mmn_muon_config mmn_muon_config_default(void);
+
+/* ------------------------------------------------------------------ AdamW */
+
+/* AdamW::new (lib.rs:32-39). `device` is the CUDA ordinal; `stream` a
+ * cudaStream_t (NULL = the library's own stream for this handle). */
+int mmn_adamw_create(const mmn_adamw_config *cfg, int device, void *stream, mmn_adamw_t **out);
+int mmn_adamw_destroy(mmn_adamw_t *h);
+
+/* AdamW::step_param (lib.rs:41-60): advances the per-instance step counter,
+ * creates zero m/v for a new id, updates param in place. `shape`/`ndim`
+ * describe param and grad (same shape). grad_divisor folds
+ * GradAccumulator::averaged_grad (lib.rs:254-257); pass 1 for none. */
+int mmn_adamw_step_param(mmn_adamw_t *h, uint64_t id, float *param, const float *grad,
+                         const int64_t *shape, int ndim, float grad_divisor, int mem);
+
+/* The instance step counter (lib.rs:26) — read or seed it. */
+int mmn_adamw_get_step(const mmn_adamw_t *h, uint64_t *step);
+int mmn_adamw_set_step(mmn_adamw_t *h, uint64_t step);
+
+/* Copy the m or v state of an id (which = 0: m, 1: v) to or from `buf`
+ * (numel floats, `mem` as above). Importing creates the id's state. */
+int mmn_adamw_export_state(mmn_adamw_t *h, uint64_t id, int which, float *buf, int64_t numel,
+                           int mem);
+int mmn_adamw_import_state(mmn_adamw_t *h, uint64_t id, int which, const float *buf,
+                           int64_t numel, int mem);
+
+/* ------------------------------------------------------------------- Muon */
+
+/* Muon::new (lib.rs:134-139) with the Newton-Schulz arithmetic mode. */
+int mmn_muon_create(const mmn_muon_config *cfg, int ns_mode, int device, void *stream,
+                    mmn_muon_t **out);
+int mmn_muon_destroy(mmn_muon_t *h);
+
+/* Muon::step_matrix (lib.rs:141-175) for a 2-D rows x cols param. */
+int mmn_muon_step_matrix(mmn_muon_t *h, uint64_t id, float *param, const float *grad,
+                         const int64_t *shape, int ndim, float grad_divisor, int mem);
+
+/* Create the zero velocity of an id without stepping it (lib.rs:150-153 does
+ * this lazily on the first step), so that state can be imported first. */
+int mmn_muon_register(mmn_muon_t *h, uint64_t id, const int64_t *shape, int ndim);
+
+/* Velocity state of an id (rows*cols floats). */
+int mmn_muon_export_velocity(mmn_muon_t *h, uint64_t id, float *buf, int64_t numel, int mem);
+int mmn_muon_import_velocity(mmn_muon_t *h, uint64_t id, const float *buf, int64_t numel,
+                             int mem);
+
+/* newton_schulz5 (lib.rs:83-126). A non-2-D input of len elements is
+ * zero-padded row-major to side x side, side = ceil(sqrt(len)) (lib.rs:89-99);
+ * `out` receives rows*cols (2-D) or side*side floats. `ns_mode` as above.
+ * Synchronous for MMN_MEM_HOST; enqueued on `stream` for MMN_MEM_DEVICE. */
+int mmn_newton_schulz5(const float *g, const int64_t *shape, int ndim, int steps, int ns_mode,
+                       float *out, int device, void *stream, int mem);
+
+/* One loop body of newton_schulz5 (lib.rs:113-119) on an n x m (n <= m)
+ * matrix x whose values are bf16-representable, divided by x_norm first
+ * (x_norm = the Frobenius norm for the first iteration, 1 afterwards). Writes
+ * A = bf16(x x^T), A2 = bf16(A A) (or, for MMN_NS_BF16, bf16(b*A + c*A2)),
+ * and the next x; any output pointer may be NULL. Host memory, synchronous.
+ * Exposes the three tensor-core products for per-iteration parity checks. */
+int mmn_newton_schulz_iteration(const float *x, int64_t n, int64_t m, float x_norm, int ns_mode,
+                                float *a_out, float *a2_out, float *x_next, int device);
+
+/* ---------------------------------------------------------------- Hybrid */
+
+/* HybridOptimizer::classify_param (lib.rs:196-202): MMN_ROUTE_MUON (Matrix)
+ * or MMN_ROUTE_ADAMW (Other). */
+int mmn_hybrid_classify_param(const int64_t *shape, int ndim);
+
+/* HybridOptimizer::new (lib.rs:189-194). */
+int mmn_hybrid_create(const mmn_muon_config *muon, const mmn_adamw_config *adamw, int ns_mode,
+                      int device, void *stream, mmn_hybrid_t **out);
+int mmn_hybrid_destroy(mmn_hybrid_t *h);
+
+/* HybridOptimizer::step (lib.rs:204-209). `route` MMN_ROUTE_AUTO applies the
+ * reference's shape rule; MMN_ROUTE_MUON / MMN_ROUTE_ADAMW override it (the
+ * tagged policy that sends embeddings and lm_head to AdamW). */
+int mmn_hybrid_step(mmn_hybrid_t *h, uint64_t id, float *param, const float *grad,
+                    const int64_t *shape, int ndim, int route, float grad_divisor, int mem);
+
+/* The AdamW and Muon members (HybridOptimizer.{adamw, muon}, lib.rs:183-186). */
+mmn_adamw_t *mmn_hybrid_adamw(mmn_hybrid_t *h);
+mmn_muon_t *mmn_hybrid_muon(mmn_hybrid_t *h);
+
+/* ------------------------------------------- batched device-resident step */
+/*
+ * The whole model's optimizer step as one device-resident operation. It
+ * replaces the per-tensor optim_step_weight calls of one training step
+ * (crates/mmn-models/src/chatbot.rs:208-227, call order :1104-1196 and
+ * :964-1075) and the optimizer construction in the trainer
+ * (crates/mmn-train/src/lib.rs:367-378). Parameters are registered once in
+ * the reference's call order; the AdamW step counter advances per AdamW
+ * tensor in that order, exactly as the reference's per-call counter does.
+ */
+typedef struct {
+    mmn_adamw_config adamw;
+    mmn_muon_config muon;
+    int32_t use_hybrid;       /* TrainConfig.optimizer == "hybrid" (crates/mmn-train/src/lib.rs:378);
+                                 0 routes every tensor to AdamW, as the reference does
+                                 for "adamw" and for the documented-but-unimplemented "muon" */
+    int32_t ns_mode;          /* MMN_NS_* */
+    int32_t fresh_state;      /* 1: m, v and velocity start at zero every step (the
+                                 trainer never reuses ids, crates/mmn-train/src/lib.rs:380) */
+    int32_t grad_dtype;       /* MMN_DTYPE_F32 or MMN_DTYPE_BF16 */
+    int32_t bf16_param_shadow;/* 1: keep a bf16 copy of every param, refreshed each step */
+    int32_t loss_scaling;     /* 1: grads are divided by a device loss scale, any
+                                 non-finite grad skips the step and halves the scale */
+    float loss_scale_init;    /* e.g. 65536 */
+    int32_t growth_interval;  /* clean steps before the scale doubles (e.g. 2000) */
+    int32_t rank;             /* shard of the step this process owns (0 .. world_size-1) */
+    int32_t world_size;       /* 1 = unsharded */
+    int32_t use_graph;        /* 1: capture the step in a CUDA graph at first use */
+} mmn_optim_config;
+
+/* Defaults: AdamW/Muon defaults, hybrid, reference NS, persistent state, f32
+ * grads, no shadow, no loss scaling, unsharded, graphs on. */
+mmn_optim_config mmn_optim_config_default(void);
+
+int mmn_optim_create(const mmn_optim_config *cfg, int device, void *stream, mmn_optim_t **out);
+int mmn_optim_destroy(mmn_optim_t *h);
+
+/* Register one parameter tensor (call order = optimizer call order). Returns
+ * its slot index in *slot. ids must be distinct. */
+int mmn_optim_add_param(mmn_optim_t *h, uint64_t id, const int64_t *shape, int ndim, int route,
+                        int *slot);
+
+/* Freeze the layout and allocate every device buffer. */
+int mmn_optim_finalize(mmn_optim_t *h);
+
+/* Device pointers of a slot's fp32 param, its grad (grad_dtype) and its bf16
+ * shadow (NULL without one). Valid until destroy. */
+int mmn_optim_slot_ptrs(mmn_optim_t *h, int slot, float **param, void **grad,
+                        void **param_bf16);
+
+/* Copy a slot's param in or out, or its grad in (`mem` as above; device
+ * copies are enqueued on the handle's stream). */
+int mmn_optim_set_param(mmn_optim_t *h, int slot, const float *src, int mem);
+int mmn_optim_get_param(mmn_optim_t *h, int slot, float *dst, int mem);
+int mmn_optim_set_grad(mmn_optim_t *h, int slot, const void *src, int mem);
+
+/* Optimizer state of a slot: which = 0 m, 1 v (AdamW slots), 2 velocity (Muon). */
+int mmn_optim_set_state(mmn_optim_t *h, int slot, int which, const float *src, int mem);
+int mmn_optim_get_state(mmn_optim_t *h, int slot, int which, float *dst, int mem);
+
+/* Seed / read the AdamW step counter (calls so far). */
+int mmn_optim_set_adamw_step(mmn_optim_t *h, uint64_t step);
+int mmn_optim_get_adamw_step(mmn_optim_t *h, uint64_t *step);
+
+/* Enqueue one optimizer step over every slot this rank owns. grad_divisor is
+ * GradAccumulator's micro-batch count (1 = none). Asynchronous. */
+int mmn_optim_step(mmn_optim_t *h, float grad_divisor);
+
+/* Wait for the handle's stream; reports MMN_E_TIMEOUT if a kernel gave up. */
+int mmn_optim_sync(mmn_optim_t *h);
+
+/* Loss-scaling state (after mmn_optim_sync): current scale, steps skipped. */
+int mmn_optim_loss_scale(mmn_optim_t *h, float *scale, int64_t *skipped_steps);
+
+/* Sharding plan (world_size > 1). A Muon matrix is stepped whole by one rank,
+ * chosen by longest-processing-time bin packing on its Newton-Schulz flops;
+ * the flat AdamW arena is cut into world_size equal element ranges.
+ * owner_rank is the Muon owner, or -1 for an AdamW slot (split by range). */
+int mmn_optim_slot_owner(mmn_optim_t *h, int slot, int *owner_rank);
+
+/* Where the params live for the post-step exchange. Each arena is
+ * world_size equal regions of `*_region` elements; rank r steps region r of
+ * both. An all-gather of region r from every rank into the same offsets
+ * completes the step everywhere. With bf16_param_shadow the bf16 arenas (same
+ * element layout) are the ones to gather. */
+typedef struct {
+    float *adamw_param;
+    void *adamw_param_bf16;
+    int64_t adamw_region;
+    float *muon_param;
+    void *muon_param_bf16;
+    int64_t muon_region;
+} mmn_optim_gather_layout;
+int mmn_optim_get_gather_layout(mmn_optim_t *h, mmn_optim_gather_layout *out);
+
+/* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
+int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
+
+/* Algorithmic Newton-Schulz flops of one step on this rank
+ * (ns_steps * (4 n^2 m + 2 n^3) per owned matrix, n <= m). */
+int mmn_optim_ns_flops(mmn_optim_t *h, double *flops);
+
+/* Per-step device-time breakdown of the last synchronised step, in ms:
+ * [0] AdamW kernel, [1] Muon momentum+norm, [2] Newton-Schulz GEMMs,
+ * [3] Muon update, [4] whole step. Needs timing enabled. */
+int mmn_optim_enable_timing(mmn_optim_t *h, int enable);
+int mmn_optim_last_timing(mmn_optim_t *h, float *ms5);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MMN_OPTIM_H */

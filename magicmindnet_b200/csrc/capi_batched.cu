@@ -1,0 +1,728 @@
+// Batched, device-resident optimizer step: every registered tensor is stepped
+// by one enqueue of a handful of kernels (optionally one CUDA graph launch).
+// This replaces the per-tensor optim_step_weight calls of one training step
+// (crates/mmn-models/src/chatbot.rs:208-227) with identical arithmetic:
+// tensors keep the reference's call order, which fixes each AdamW tensor's
+// step count t (crates/mmn-optim/src/lib.rs:41-43).
+#include <algorithm>
+#include <cstring>
+#include <unordered_set>
+
+#include "capi_internal.cuh"
+#include "elementwise.cuh"
+#include "ns_engine.cuh"
+
+using namespace mmn;
+
+namespace {
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DevGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+struct mmn_optim {
+  Ctx ctx;
+  mmn_optim_config cfg;
+  BiasTable bc;
+  bool finalized = false;
+
+  struct Slot {
+    uint64_t id = 0;
+    std::vector<int64_t> shape;
+    int64_t numel = 0;
+    int route = MMN_ROUTE_ADAMW;  // resolved: MMN_ROUTE_MUON or MMN_ROUTE_ADAMW
+    int64_t off = 0;              // element offset in its arena
+    int t_offset = 0;             // AdamW: 1-based call position in a step
+    int rows = 0, cols = 0;       // Muon
+    int owner = -1;               // Muon owner rank
+  };
+  std::vector<Slot> slots;
+  std::unordered_set<uint64_t> ids;
+
+  // AdamW arena (fp32 p/m/v, grads in grad_dtype, optional bf16 shadow)
+  int64_t a_used4 = 0, a_region4 = 0, a_total4 = 0;
+  float *ap = nullptr, *am = nullptr, *av = nullptr;
+  void* ag = nullptr;
+  __nv_bfloat16* ap16 = nullptr;
+  AdamwSeg* d_segs = nullptr;
+  int* d_chunk_seg = nullptr;
+  int n_adamw = 0;
+
+  // Muon arena
+  int64_t m_region = 0, m_total = 0;
+  float *mp = nullptr, *mvel = nullptr;
+  void* mg = nullptr;
+  __nv_bfloat16* mp16 = nullptr;
+  std::vector<NsClass> classes;
+  std::vector<MuonMat> mats;  // owned by this rank
+  MuonMat* d_mats = nullptr;
+  MuonClassPtr *d_cls_in = nullptr, *d_cls_out = nullptr;
+  float* d_partials = nullptr;
+  float* d_norms = nullptr;
+  int total_tiles = 0;
+  double ns_flops = 0.0;
+  int64_t n_params = 0, n_adamw_params = 0, n_muon_params = 0;
+
+  // device step state
+  long long* d_step = nullptr;
+  int* d_skip = nullptr;
+  float* d_scale = nullptr;
+  int* d_good = nullptr;
+  int* d_skipped = nullptr;
+
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  float graph_divisor = 0.0f;
+  bool timing = false;
+  cudaEvent_t ev[8] = {};
+  std::vector<void*> allocs;
+
+  int dalloc(void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    allocs.push_back(*p);
+    e = cudaMemset(*p, 0, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset");
+    return MMN_OK;
+  }
+};
+
+extern "C" mmn_optim_config mmn_optim_config_default(void) {
+  mmn_optim_config c;
+  memset(&c, 0, sizeof(c));
+  c.adamw = mmn_adamw_config_default();
+  c.muon = mmn_muon_config_default();
+  c.use_hybrid = 1;
+  c.ns_mode = MMN_NS_REFERENCE;
+  c.fresh_state = 0;
+  c.grad_dtype = MMN_DTYPE_F32;
+  c.bf16_param_shadow = 0;
+  c.loss_scaling = 0;
+  c.loss_scale_init = 65536.0f;
+  c.growth_interval = 2000;
+  c.rank = 0;
+  c.world_size = 1;
+  c.use_graph = 1;
+  return c;
+}
+
+extern "C" int mmn_optim_create(const mmn_optim_config* cfg, int device, void* stream,
+                                mmn_optim_t** out) {
+  if (!out) return fail(MMN_E_INVALID, "out is null");
+  *out = nullptr;
+  mmn_optim_config c = cfg ? *cfg : mmn_optim_config_default();
+  if (c.world_size < 1 || c.rank < 0 || c.rank >= c.world_size)
+    return fail(MMN_E_INVALID, "rank / world_size out of range");
+  if (c.ns_mode != MMN_NS_REFERENCE && c.ns_mode != MMN_NS_BF16)
+    return fail(MMN_E_INVALID, "unknown ns_mode");
+  if (c.grad_dtype != MMN_DTYPE_F32 && c.grad_dtype != MMN_DTYPE_BF16)
+    return fail(MMN_E_INVALID, "grad_dtype must be f32 or bf16");
+  if (c.muon.ns_steps < 0) return fail(MMN_E_INVALID, "ns_steps must be >= 0");
+  if (c.loss_scaling && !(c.loss_scale_init > 0.0f)) return fail(MMN_E_INVALID, "loss scale <= 0");
+  auto* h = new mmn_optim();
+  h->cfg = c;
+  int rc = h->ctx.init(device, stream);
+  if (rc == MMN_OK) {
+    DevGuard g(device);
+    rc = h->bc.build(c.adamw.beta1, c.adamw.beta2);
+  }
+  if (rc != MMN_OK) {
+    h->ctx.release();
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
+  if (!h) return MMN_OK;
+  DevGuard g(h->ctx.device);
+  cudaStreamSynchronize(h->ctx.stream);
+  if (h->graph) cudaGraphExecDestroy(h->graph);
+  for (auto& c : h->classes) ns_class_free(c);
+  for (void* p : h->allocs) cudaFree(p);
+  for (auto& e : h->ev)
+    if (e) cudaEventDestroy(e);
+  if (h->fork) cudaEventDestroy(h->fork);
+  if (h->join) cudaEventDestroy(h->join);
+  if (h->side) cudaStreamDestroy(h->side);
+  h->bc.release();
+  h->ctx.release();
+  delete h;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_add_param(mmn_optim_t* h, uint64_t id, const int64_t* shape, int ndim,
+                                   int route, int* slot) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (h->finalized) return fail(MMN_E_STATE, "add_param after finalize");
+  if (h->ids.count(id)) return fail(MMN_E_INVALID, "id registered twice");
+  int rc;
+  const int64_t numel = shape_numel(shape, ndim, &rc);
+  if (rc != MMN_OK) return rc;
+  if (route != MMN_ROUTE_AUTO && route != MMN_ROUTE_MUON && route != MMN_ROUTE_ADAMW)
+    return fail(MMN_E_INVALID, "unknown route");
+  mmn_optim::Slot s;
+  s.id = id;
+  s.shape.assign(shape, shape + ndim);
+  s.numel = numel;
+  if (!h->cfg.use_hybrid)
+    s.route = MMN_ROUTE_ADAMW;  // crates/mmn-train/src/lib.rs:378: only "hybrid" uses Muon
+  else if (route == MMN_ROUTE_AUTO)
+    s.route = mmn_hybrid_classify_param(shape, ndim);
+  else
+    s.route = route;
+  if (s.route == MMN_ROUTE_MUON) {
+    if (ndim != 2 || shape[0] < 1 || shape[1] < 1 || shape[0] > (1 << 30) || shape[1] > (1 << 30))
+      return fail(MMN_E_SHAPE, "Muon tensors must be 2-D");
+    s.rows = (int)shape[0];
+    s.cols = (int)shape[1];
+  }
+  h->ids.insert(id);
+  h->slots.push_back(s);
+  if (slot) *slot = (int)h->slots.size() - 1;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (h->finalized) return MMN_OK;
+  DevGuard g(h->ctx.device);
+  const int W = h->cfg.world_size, R = h->cfg.rank;
+  const int steps = h->cfg.muon.ns_steps;
+  int rc;
+
+  // ---- AdamW arena: registration order, each tensor padded to 4 elements.
+  std::vector<AdamwSeg> segs;
+  int64_t off4 = 0;
+  for (auto& s : h->slots) {
+    h->n_params += s.numel;
+    if (s.route != MMN_ROUTE_ADAMW) continue;
+    h->n_adamw_params += s.numel;
+    AdamwSeg sg{};
+    sg.start4 = off4;
+    sg.end4 = off4 + (s.numel + 3) / 4;
+    sg.t_offset = ++h->n_adamw;
+    s.off = off4 * 4;
+    s.t_offset = sg.t_offset;
+    off4 = sg.end4;
+    if (sg.end4 > sg.start4) segs.push_back(sg);
+  }
+  h->a_used4 = off4;
+  h->a_region4 = (off4 + W - 1) / W;
+  h->a_region4 = align_up(h->a_region4, 16);  // 256-byte aligned regions
+  h->a_total4 = h->a_region4 * W;
+  std::vector<int> chunk_seg((size_t)((h->a_used4 + kAdamwChunk4 - 1) / kAdamwChunk4) + 1, 0);
+  for (size_t k = 0, c = 0; c < chunk_seg.size(); ++c) {
+    const int64_t first = (int64_t)c * kAdamwChunk4;
+    while (k + 1 < segs.size() && segs[k].end4 <= first) ++k;
+    chunk_seg[c] = (int)k;
+  }
+
+  // ---- Muon: LPT assignment of whole matrices to ranks by Newton-Schulz flops.
+  std::vector<int> muon_idx;
+  for (int i = 0; i < (int)h->slots.size(); ++i)
+    if (h->slots[i].route == MMN_ROUTE_MUON) muon_idx.push_back(i);
+  auto cost = [&](const mmn_optim::Slot& s) {
+    const double n = std::min(s.rows, s.cols), m = std::max(s.rows, s.cols);
+    return (double)std::max(steps, 1) * (4.0 * n * n * m + 2.0 * n * n * n) + 64.0 * n * m;
+  };
+  std::vector<int> order = muon_idx;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    return cost(h->slots[a]) > cost(h->slots[b]);
+  });
+  std::vector<double> load(W, 0.0);
+  for (int i : order) {
+    int best = 0;
+    for (int r = 1; r < W; ++r)
+      if (load[r] < load[best]) best = r;
+    h->slots[i].owner = best;
+    load[best] += cost(h->slots[i]);
+  }
+  // Muon arena grouped by owner rank (registration order inside a rank).
+  std::vector<int64_t> region_used(W, 0);
+  for (int i : muon_idx) {
+    auto& s = h->slots[i];
+    h->n_muon_params += s.numel;
+    s.off = region_used[s.owner];
+    region_used[s.owner] = align_up(region_used[s.owner] + s.numel, 64);
+  }
+  h->m_region = 64;
+  for (int r = 0; r < W; ++r) h->m_region = std::max(h->m_region, region_used[r]);
+  for (int i : muon_idx) h->slots[i].off += (int64_t)h->slots[i].owner * h->m_region;
+  h->m_total = h->m_region * W;
+
+  // ---- Newton-Schulz shape classes over the matrices this rank owns.
+  std::vector<std::pair<int, int>> cls_shapes;
+  std::vector<int> cls_count;
+  int tiles = 0;
+  for (int i : muon_idx) {
+    auto& s = h->slots[i];
+    if (s.owner != R) continue;
+    const int n = std::min(s.rows, s.cols), m = std::max(s.rows, s.cols);
+    int ci = -1;
+    for (int k = 0; k < (int)cls_shapes.size(); ++k)
+      if (cls_shapes[k] == std::make_pair(n, m)) ci = k;
+    if (ci < 0) {
+      ci = (int)cls_shapes.size();
+      cls_shapes.emplace_back(n, m);
+      cls_count.push_back(0);
+    }
+    MuonMat mm{};
+    mm.off = s.off;
+    mm.rows = s.rows;
+    mm.cols = s.cols;
+    mm.transposed = s.rows > s.cols;
+    mm.xcls = ci;
+    mm.xbatch = cls_count[ci]++;
+    mm.tile0 = tiles;
+    tiles += ((s.rows + 63) / 64) * ((s.cols + 63) / 64);
+    mm.lr_scale = h->cfg.muon.lr * sqrtf((float)s.rows / (float)s.cols);  // lib.rs:169-173
+    h->mats.push_back(mm);
+    h->ns_flops += (double)steps * (4.0 * n * (double)n * m + 2.0 * (double)n * n * n);
+  }
+  h->total_tiles = tiles;
+  if (!h->mats.empty()) {
+    std::string e = ns_gemm_setup();
+    if (!e.empty()) return fail(MMN_E_CUDA, e);
+  }
+  h->classes.resize(cls_shapes.size());
+  int norm_base = 0;
+  std::vector<int> cls_norm0(cls_shapes.size());
+  for (size_t k = 0; k < cls_shapes.size(); ++k) {
+    std::string e = ns_class_init(h->classes[k], cls_shapes[k].first, cls_shapes[k].second,
+                                  cls_count[k], nullptr);
+    if (!e.empty()) return fail(MMN_E_OOM, e);
+    cls_norm0[k] = norm_base;
+    norm_base += cls_count[k];
+  }
+  for (auto& mm : h->mats) mm.norm_idx = cls_norm0[mm.xcls] + mm.xbatch;
+
+  // ---- device allocations
+  const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
+  const size_t a_el = (size_t)h->a_total4 * 4;
+  if ((rc = h->dalloc((void**)&h->ap, a_el * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->am, h->cfg.fresh_state ? 16 : a_el * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->av, h->cfg.fresh_state ? 16 : a_el * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc(&h->ag, a_el * gsz)) != MMN_OK) return rc;
+  if (h->cfg.bf16_param_shadow && (rc = h->dalloc((void**)&h->ap16, a_el * 2)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_segs, std::max<size_t>(segs.size(), 1) * sizeof(AdamwSeg))) != MMN_OK)
+    return rc;
+  if ((rc = h->dalloc((void**)&h->d_chunk_seg, chunk_seg.size() * sizeof(int))) != MMN_OK) return rc;
+  const size_t m_el = (size_t)h->m_total;
+  if ((rc = h->dalloc((void**)&h->mp, m_el * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->mvel, m_el * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc(&h->mg, m_el * gsz)) != MMN_OK) return rc;
+  if (h->cfg.bf16_param_shadow && (rc = h->dalloc((void**)&h->mp16, m_el * 2)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_mats, std::max<size_t>(h->mats.size(), 1) * sizeof(MuonMat))) != MMN_OK)
+    return rc;
+  const size_t ncls = std::max<size_t>(h->classes.size(), 1);
+  if ((rc = h->dalloc((void**)&h->d_cls_in, ncls * sizeof(MuonClassPtr))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_cls_out, ncls * sizeof(MuonClassPtr))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_partials, (size_t)std::max(tiles, 1) * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_norms, (size_t)std::max(norm_base, 1) * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_step, sizeof(long long))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_skip, sizeof(int))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_scale, sizeof(float))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_good, sizeof(int))) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_skipped, sizeof(int))) != MMN_OK) return rc;
+
+  MMN_CUDA_TRY(cudaMemcpy(h->d_segs, segs.data(), segs.size() * sizeof(AdamwSeg), cudaMemcpyHostToDevice));
+  MMN_CUDA_TRY(cudaMemcpy(h->d_chunk_seg, chunk_seg.data(), chunk_seg.size() * sizeof(int),
+                          cudaMemcpyHostToDevice));
+  MMN_CUDA_TRY(cudaMemcpy(h->d_mats, h->mats.data(), h->mats.size() * sizeof(MuonMat),
+                          cudaMemcpyHostToDevice));
+  std::vector<MuonClassPtr> cin(ncls), cout(ncls);
+  for (size_t k = 0; k < h->classes.size(); ++k) {
+    auto& c = h->classes[k];
+    c.norms = h->d_norms + cls_norm0[k];  // the class reads its norms from the shared array
+    cin[k].x = c.x[0];
+    cin[k].bstride = (long long)c.n * c.ld_x;
+    cin[k].ld = c.ld_x;
+    cout[k] = cin[k];
+    cout[k].x = c.x[steps % 2];
+  }
+  MMN_CUDA_TRY(cudaMemcpy(h->d_cls_in, cin.data(), ncls * sizeof(MuonClassPtr), cudaMemcpyHostToDevice));
+  MMN_CUDA_TRY(cudaMemcpy(h->d_cls_out, cout.data(), ncls * sizeof(MuonClassPtr), cudaMemcpyHostToDevice));
+  const float scale = h->cfg.loss_scale_init;
+  MMN_CUDA_TRY(cudaMemcpy(h->d_scale, &scale, sizeof(float), cudaMemcpyHostToDevice));
+
+  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming));
+  for (auto& e : h->ev) MMN_CUDA_TRY(cudaEventCreate(&e));
+  MMN_CUDA_TRY(cudaDeviceSynchronize());
+  h->finalized = true;
+  return MMN_OK;
+}
+
+static int check_slot(mmn_optim_t* h, int slot) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  if (slot < 0 || slot >= (int)h->slots.size()) return fail(MMN_E_INVALID, "slot out of range");
+  return MMN_OK;
+}
+
+static float* slot_param(mmn_optim_t* h, const mmn_optim::Slot& s) {
+  return (s.route == MMN_ROUTE_ADAMW ? h->ap : h->mp) + s.off;
+}
+
+extern "C" int mmn_optim_slot_ptrs(mmn_optim_t* h, int slot, float** param, void** grad,
+                                   void** param_bf16) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  const auto& s = h->slots[slot];
+  const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
+  const bool a = s.route == MMN_ROUTE_ADAMW;
+  if (param) *param = slot_param(h, s);
+  if (grad) *grad = static_cast<uint8_t*>(a ? h->ag : h->mg) + (size_t)s.off * gsz;
+  if (param_bf16) {
+    __nv_bfloat16* b = a ? h->ap16 : h->mp16;
+    *param_bf16 = b ? b + s.off : nullptr;
+  }
+  return MMN_OK;
+}
+
+static cudaMemcpyKind kind_in(int mem) {
+  return mem == MMN_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+}
+static cudaMemcpyKind kind_out(int mem) {
+  return mem == MMN_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+}
+
+extern "C" int mmn_optim_set_param(mmn_optim_t* h, int slot, const float* src, int mem) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  if (!src) return fail(MMN_E_INVALID, "null src");
+  DevGuard g(h->ctx.device);
+  const auto& s = h->slots[slot];
+  float* dst = slot_param(h, s);
+  MMN_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)s.numel * 4, kind_in(mem), h->ctx.stream));
+  if (h->cfg.bf16_param_shadow) {
+    // Keep the shadow equal to bf16(master) from the start.
+    __nv_bfloat16* b = (s.route == MMN_ROUTE_ADAMW ? h->ap16 : h->mp16) + s.off;
+    std::vector<__nv_bfloat16> tmp((size_t)s.numel);
+    std::vector<float> hostp((size_t)s.numel);
+    MMN_CUDA_TRY(cudaMemcpyAsync(hostp.data(), dst, (size_t)s.numel * 4, cudaMemcpyDeviceToHost,
+                                 h->ctx.stream));
+    MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+    for (size_t i = 0; i < hostp.size(); ++i) tmp[i] = __float2bfloat16_rn(hostp[i]);
+    MMN_CUDA_TRY(cudaMemcpyAsync(b, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice, h->ctx.stream));
+  }
+  if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_get_param(mmn_optim_t* h, int slot, float* dst, int mem) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  if (!dst) return fail(MMN_E_INVALID, "null dst");
+  DevGuard g(h->ctx.device);
+  const auto& s = h->slots[slot];
+  MMN_CUDA_TRY(cudaMemcpyAsync(dst, slot_param(h, s), (size_t)s.numel * 4, kind_out(mem),
+                               h->ctx.stream));
+  if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_set_grad(mmn_optim_t* h, int slot, const void* src, int mem) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  if (!src) return fail(MMN_E_INVALID, "null src");
+  DevGuard g(h->ctx.device);
+  void* dst = nullptr;
+  mmn_optim_slot_ptrs(h, slot, nullptr, &dst, nullptr);
+  const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
+  MMN_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)h->slots[slot].numel * gsz, kind_in(mem),
+                               h->ctx.stream));
+  if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+static int state_ptr(mmn_optim_t* h, int slot, int which, float** p) {
+  const auto& s = h->slots[slot];
+  if (which == 0 || which == 1) {
+    if (s.route != MMN_ROUTE_ADAMW) return fail(MMN_E_INVALID, "m/v exist only for AdamW slots");
+    if (h->cfg.fresh_state) return fail(MMN_E_STATE, "fresh_state handles keep no m/v");
+    *p = (which == 0 ? h->am : h->av) + s.off;
+    return MMN_OK;
+  }
+  if (which == 2) {
+    if (s.route != MMN_ROUTE_MUON) return fail(MMN_E_INVALID, "velocity exists only for Muon slots");
+    *p = h->mvel + s.off;
+    return MMN_OK;
+  }
+  return fail(MMN_E_INVALID, "which must be 0 (m), 1 (v) or 2 (velocity)");
+}
+
+extern "C" int mmn_optim_set_state(mmn_optim_t* h, int slot, int which, const float* src, int mem) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  float* p = nullptr;
+  if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaMemcpyAsync(p, src, (size_t)h->slots[slot].numel * 4, kind_in(mem), h->ctx.stream));
+  if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_get_state(mmn_optim_t* h, int slot, int which, float* dst, int mem) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  float* p = nullptr;
+  if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaMemcpyAsync(dst, p, (size_t)h->slots[slot].numel * 4, kind_out(mem), h->ctx.stream));
+  if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_set_adamw_step(mmn_optim_t* h, uint64_t step) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  DevGuard g(h->ctx.device);
+  const long long v = (long long)step;
+  MMN_CUDA_TRY(cudaMemcpyAsync(h->d_step, &v, sizeof(v), cudaMemcpyHostToDevice, h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
+  if (!h || !h->finalized || !step) return fail(MMN_E_STATE, "finalize first");
+  DevGuard g(h->ctx.device);
+  long long v = 0;
+  MMN_CUDA_TRY(cudaMemcpyAsync(&v, h->d_step, sizeof(v), cudaMemcpyDeviceToHost, h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  *step = (uint64_t)v;
+  return MMN_OK;
+}
+
+// Enqueues the whole step on the handle's stream (AdamW forked onto a side
+// stream so it overlaps the Newton-Schulz GEMMs).
+static int enqueue_step(mmn_optim_t* h, float divisor) {
+  cudaStream_t s = h->ctx.stream;
+  const bool tm = h->timing;
+  const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
+  const int R = h->cfg.rank;
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[0], s));
+  if (h->cfg.loss_scaling) {
+    // Every rank scans every grad (grads are replicated), so all ranks reach
+    // the same skip decision without a collective.
+    MMN_CUDA_TRY(cudaMemsetAsync(h->d_skip, 0, sizeof(int), s));
+    const int64_t a_n = h->a_used4 * 4;
+    if (bf) {
+      launch_nonfinite_scan(nullptr, 0, static_cast<const __nv_bfloat16*>(h->ag), a_n, h->d_skip,
+                            h->ctx.num_sms, s);
+      launch_nonfinite_scan(nullptr, 0, static_cast<const __nv_bfloat16*>(h->mg), h->m_total,
+                            h->d_skip, h->ctx.num_sms, s);
+    } else {
+      launch_nonfinite_scan(static_cast<const float*>(h->ag), a_n, nullptr, 0, h->d_skip,
+                            h->ctx.num_sms, s);
+      launch_nonfinite_scan(static_cast<const float*>(h->mg), h->m_total, nullptr, 0, h->d_skip,
+                            h->ctx.num_sms, s);
+    }
+  }
+  const int* skip = h->cfg.loss_scaling ? h->d_skip : nullptr;
+  const float* gscale = h->cfg.loss_scaling ? h->d_scale : nullptr;
+
+  // ---- AdamW on the side stream
+  MMN_CUDA_TRY(cudaEventRecord(h->fork, s));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->fork, 0));
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[1], h->side));
+  AdamwArgs a{};
+  a.p = h->ap;
+  a.g = bf ? nullptr : static_cast<const float*>(h->ag);
+  a.g_bf16 = bf ? static_cast<const __nv_bfloat16*>(h->ag) : nullptr;
+  a.m = h->am;
+  a.v = h->av;
+  a.p_bf16 = h->ap16;
+  a.segs = h->d_segs;
+  a.chunk_seg = h->d_chunk_seg;
+  a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
+  a.end4 = std::min<long long>(h->a_region4 * (R + 1), h->a_used4);
+  a.bc_table = h->bc.dev;
+  a.t_sat = h->bc.t_sat;
+  a.step_base = h->d_step;
+  a.skip = skip;
+  a.grad_scale = gscale;
+  a.lr = h->cfg.adamw.lr;
+  a.b1 = h->cfg.adamw.beta1;
+  a.b2 = h->cfg.adamw.beta2;
+  a.eps = h->cfg.adamw.eps;
+  a.wd = h->cfg.adamw.weight_decay;
+  a.grad_divisor = divisor;
+  a.fresh_state = h->cfg.fresh_state;
+  launch_adamw(a, h->ctx.num_sms, h->side);
+  MMN_CUDA_TRY(cudaGetLastError());
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
+  MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
+
+  // ---- Muon on the main stream
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[3], s));
+  if (!h->mats.empty()) {
+    MuonArgs m{};
+    m.p = h->mp;
+    m.g = bf ? nullptr : static_cast<const float*>(h->mg);
+    m.g_bf16 = bf ? static_cast<const __nv_bfloat16*>(h->mg) : nullptr;
+    m.vel = h->mvel;
+    m.p_bf16 = h->mp16;
+    m.mats = h->d_mats;
+    m.nmat = (int)h->mats.size();
+    m.total_tiles = h->total_tiles;
+    m.cls = h->d_cls_in;
+    m.partials = h->d_partials;
+    m.norms = h->d_norms;
+    m.skip = skip;
+    m.grad_scale = gscale;
+    m.momentum = h->cfg.muon.momentum;
+    m.nesterov = h->cfg.muon.nesterov;
+    m.grad_divisor = divisor;
+    m.fresh_state = h->cfg.fresh_state;
+    m.apply_divides_norm = h->cfg.muon.ns_steps == 0;
+    launch_muon_momentum(m, h->ctx.num_sms, s);
+    launch_muon_norms(m, s);
+    MMN_CUDA_TRY(cudaGetLastError());
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
+    for (auto& c : h->classes) {
+      std::string err;
+      if (ns_class_run(c, h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status, h->ctx.num_sms, s,
+                       &err) < 0)
+        return fail(MMN_E_CUDA, err);
+    }
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
+    m.cls = h->d_cls_out;
+    launch_muon_apply(m, h->ctx.num_sms, s);
+    MMN_CUDA_TRY(cudaGetLastError());
+  } else if (tm) {
+    MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
+    MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
+  }
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[6], s));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->join, 0));
+  StepTail t{};
+  t.step_counter = h->d_step;
+  t.adamw_calls = h->n_adamw;
+  t.skip = skip;
+  t.grad_scale = h->cfg.loss_scaling ? h->d_scale : nullptr;
+  t.good_steps = h->d_good;
+  t.growth_interval = h->cfg.growth_interval > 0 ? h->cfg.growth_interval : 2000;
+  t.skipped_total = h->d_skipped;
+  launch_step_tail(t, s);
+  MMN_CUDA_TRY(cudaGetLastError());
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[7], s));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
+  if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
+  DevGuard g(h->ctx.device);
+  if (!h->cfg.use_graph || h->timing) return enqueue_step(h, grad_divisor);
+  if (h->graph && h->graph_divisor != grad_divisor) {
+    cudaGraphExecDestroy(h->graph);
+    h->graph = nullptr;
+  }
+  if (!h->graph) {
+    cudaGraph_t graph = nullptr;
+    MMN_CUDA_TRY(cudaStreamBeginCapture(h->ctx.stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(h, grad_divisor);
+    cudaError_t e = cudaStreamEndCapture(h->ctx.stream, &graph);
+    if (rc != MMN_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&h->graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    h->graph_divisor = grad_divisor;
+  }
+  MMN_CUDA_TRY(cudaGraphLaunch(h->graph, h->ctx.stream));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_sync(mmn_optim_t* h) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  DevGuard g(h->ctx.device);
+  return h->ctx.check_status();
+}
+
+extern "C" int mmn_optim_loss_scale(mmn_optim_t* h, float* scale, int64_t* skipped_steps) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  float sc = 0.0f;
+  int sk = 0;
+  MMN_CUDA_TRY(cudaMemcpy(&sc, h->d_scale, sizeof(float), cudaMemcpyDeviceToHost));
+  MMN_CUDA_TRY(cudaMemcpy(&sk, h->d_skipped, sizeof(int), cudaMemcpyDeviceToHost));
+  if (scale) *scale = sc;
+  if (skipped_steps) *skipped_steps = sk;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_slot_owner(mmn_optim_t* h, int slot, int* owner_rank) {
+  int rc = check_slot(h, slot);
+  if (rc != MMN_OK) return rc;
+  if (owner_rank) *owner_rank = h->slots[slot].route == MMN_ROUTE_MUON ? h->slots[slot].owner : -1;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_get_gather_layout(mmn_optim_t* h, mmn_optim_gather_layout* out) {
+  if (!h || !out) return fail(MMN_E_INVALID, "null argument");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  out->adamw_param = h->ap;
+  out->adamw_param_bf16 = h->ap16;
+  out->adamw_region = h->a_region4 * 4;
+  out->muon_param = h->mp;
+  out->muon_param_bf16 = h->mp16;
+  out->muon_region = h->m_region;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_param_counts(mmn_optim_t* h, int64_t* total, int64_t* adamw,
+                                      int64_t* muon) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  if (total) *total = h->n_params;
+  if (adamw) *adamw = h->n_adamw_params;
+  if (muon) *muon = h->n_muon_params;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_ns_flops(mmn_optim_t* h, double* flops) {
+  if (!h || !h->finalized || !flops) return fail(MMN_E_STATE, "finalize first");
+  *flops = h->ns_flops;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_enable_timing(mmn_optim_t* h, int enable) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  h->timing = enable != 0;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_last_timing(mmn_optim_t* h, float* ms5) {
+  if (!h || !ms5) return fail(MMN_E_INVALID, "null argument");
+  if (!h->timing) return fail(MMN_E_STATE, "enable timing before the step");
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[0], h->ev[1], h->ev[2]));
+  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[1], h->ev[3], h->ev[4]));
+  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[2], h->ev[4], h->ev[5]));
+  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[3], h->ev[5], h->ev[6]));
+  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[4], h->ev[0], h->ev[7]));
+  return MMN_OK;
+}

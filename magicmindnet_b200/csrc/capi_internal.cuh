@@ -1,0 +1,60 @@
+// Internal helpers shared by the C ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/mmn_optim.h"
+
+namespace mmn {
+
+// Thread-local message for mmn_last_error().
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define MMN_CUDA_TRY(expr)                          \
+  do {                                              \
+    cudaError_t _e = (expr);                        \
+    if (_e != cudaSuccess) return cuda_fail(_e, #expr); \
+  } while (0)
+
+// Device, stream and SM count of a handle.
+struct Ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int* status = nullptr;  // device status word written by kernels on timeout
+
+  int init(int dev, void* user_stream);
+  void release();
+  // Reads the device status word (synchronises the stream).
+  int check_status();
+};
+
+// RAII-free device scratch that only grows.
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int ensure(size_t need);
+  void release();
+};
+
+// Host-side table of the AdamW bias-correction divisors (1 - b1^t, 1 - b2^t)
+// computed with the C library's powf exactly as the reference's f32::powf
+// (crates/mmn-optim/src/lib.rs:53-54), uploaded once; t_sat is the first step
+// from which both divisors are exactly 1.0f for every later t.
+struct BiasTable {
+  float2* dev = nullptr;
+  int t_sat = 0;
+  int build(float b1, float b2);
+  void release();
+};
+
+int64_t shape_numel(const int64_t* shape, int ndim, int* err);
+
+}  // namespace mmn

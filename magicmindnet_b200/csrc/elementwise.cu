@@ -1,0 +1,357 @@
+// Memory-bound kernels of the optimizer step. Every arithmetic step uses an
+// explicitly rounded intrinsic (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn) so
+// the compiler cannot contract a*b+c into an FMA: the reference (Rust, no FMA
+// contraction) rounds after every operation, and so do these kernels.
+#include "elementwise.cuh"
+#include "mmn_ptx.cuh"
+
+namespace mmn {
+
+namespace {
+
+__device__ __forceinline__ float load_grad(const float* g32, const __nv_bfloat16* g16,
+                                           long long i) {
+  return g16 ? __bfloat162float(g16[i]) : g32[i];
+}
+
+// AdamW::step_param arithmetic (crates/mmn-optim/src/lib.rs:47-59) for one element.
+struct AdamwConst {
+  float lr, b1, b2, one_m_b1, one_m_b2, eps, decay;
+};
+
+__device__ __forceinline__ void adamw_elem(float& p, float& m, float& v, float g, float bc1,
+                                           float bc2, const AdamwConst& c) {
+  m = __fadd_rn(__fmul_rn(c.b1, m), __fmul_rn(c.one_m_b1, g));
+  v = __fadd_rn(__fmul_rn(c.b2, v), __fmul_rn(__fmul_rn(c.one_m_b2, g), g));
+  const float mh = __fdiv_rn(m, bc1);
+  const float vh = __fdiv_rn(v, bc2);
+  const float upd = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), c.eps));
+  p = __fsub_rn(p, __fmul_rn(c.lr, upd));
+  p = __fmul_rn(p, c.decay);
+}
+
+template <bool BF16G, bool FRESH, bool SHADOW>
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamwArgs a) {
+  if (a.skip && *a.skip) return;
+  const long long base = a.step_base ? *a.step_base : a.step_base_value;
+  const float scale = a.grad_scale ? *a.grad_scale : 1.0f;
+  AdamwConst c;
+  c.lr = a.lr;
+  c.b1 = a.b1;
+  c.b2 = a.b2;
+  c.one_m_b1 = __fsub_rn(1.0f, a.b1);
+  c.one_m_b2 = __fsub_rn(1.0f, a.b2);
+  c.eps = a.eps;
+  c.decay = __fsub_rn(1.0f, __fmul_rn(a.lr, a.wd));
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = a.begin4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.end4;
+       i += stride) {
+    int t_off = a.seg0.t_offset;
+    if (a.segs) {
+      int s = __ldg(&a.chunk_seg[i / kAdamwChunk4]);
+      while (i >= a.segs[s].end4) ++s;
+      t_off = a.segs[s].t_offset;
+    }
+    long long t = base + t_off;
+    if (t > a.t_sat) t = a.t_sat;
+    const float2 bc = __ldg(&a.bc_table[t]);
+
+    float4 p4 = __ldcs(reinterpret_cast<const float4*>(a.p) + i);
+    float g[4];
+    if (BF16G) {
+      const uint2 raw = __ldcs(reinterpret_cast<const uint2*>(a.g_bf16) + i);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+      g[0] = f0.x;
+      g[1] = f0.y;
+      g[2] = f1.x;
+      g[3] = f1.y;
+    } else {
+      const float4 g4 = __ldcs(reinterpret_cast<const float4*>(a.g) + i);
+      g[0] = g4.x;
+      g[1] = g4.y;
+      g[2] = g4.z;
+      g[3] = g4.w;
+    }
+    float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!FRESH) {
+      m4 = __ldcs(reinterpret_cast<const float4*>(a.m) + i);
+      v4 = __ldcs(reinterpret_cast<const float4*>(a.v) + i);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (scale != 1.0f) g[e] = __fdiv_rn(g[e], scale);
+      if (a.grad_divisor != 1.0f) g[e] = __fdiv_rn(g[e], a.grad_divisor);
+    }
+    adamw_elem(p4.x, m4.x, v4.x, g[0], bc.x, bc.y, c);
+    adamw_elem(p4.y, m4.y, v4.y, g[1], bc.x, bc.y, c);
+    adamw_elem(p4.z, m4.z, v4.z, g[2], bc.x, bc.y, c);
+    adamw_elem(p4.w, m4.w, v4.w, g[3], bc.x, bc.y, c);
+    __stcs(reinterpret_cast<float4*>(a.p) + i, p4);
+    if (!FRESH) {
+      __stcs(reinterpret_cast<float4*>(a.m) + i, m4);
+      __stcs(reinterpret_cast<float4*>(a.v) + i, v4);
+    }
+    if (SHADOW) {
+      uint2 out;
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(p4.x, p4.y);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(p4.z, p4.w);
+      out.x = *reinterpret_cast<uint32_t*>(&h0);
+      out.y = *reinterpret_cast<uint32_t*>(&h1);
+      __stcs(reinterpret_cast<uint2*>(a.p_bf16) + i, out);
+    }
+  }
+}
+
+// Index of the matrix owning tile t: the last k with mats[k].tile0 <= t.
+__device__ __forceinline__ int find_mat(const MuonMat* mats, int nmat, int t) {
+  int lo = 0, hi = nmat - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (mats[mid].tile0 <= t)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+constexpr int kTile = 64;  // Muon elementwise kernels work on 64 x 64 tiles
+
+__device__ __forceinline__ float block_sum_256(float x, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = x;
+  __syncthreads();
+  float r = 0.0f;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r = __fadd_rn(r, red[i]);
+  }
+  __syncthreads();
+  return r;
+}
+
+// Muon momentum (lib.rs:154-165) + the bf16 cast and orientation of
+// newton_schulz5 (lib.rs:101-107) + per-tile sums of squares of the bf16
+// values (lib.rs:109), all in one pass over g and vel.
+template <bool BF16G, bool FRESH>
+__global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
+  __shared__ float tile[kTile][kTile + 1];
+  __shared__ float red[8];
+  if (a.skip && *a.skip) return;
+  const float scale = a.grad_scale ? *a.grad_scale : 1.0f;
+  const float mu = a.momentum;
+  const float one_m = __fsub_rn(1.0f, mu);
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  for (int t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
+    const int k = find_mat(a.mats, a.nmat, t);
+    const MuonMat mm = a.mats[k];
+    const int tiles_c = (mm.cols + kTile - 1) / kTile;
+    const int lt = t - mm.tile0;
+    const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
+    const MuonClassPtr cp = a.cls[mm.xcls];
+    __nv_bfloat16* X = cp.x + (long long)mm.xbatch * cp.bstride;
+    float ss = 0.0f;
+    for (int rr = ty; rr < kTile; rr += 4) {
+      const int r = r0 + rr, c = c0 + tx;
+      float y = 0.0f;
+      if (r < mm.rows && c < mm.cols) {
+        const long long idx = mm.off + (long long)r * mm.cols + c;
+        float g = load_grad(a.g, a.g_bf16, idx);
+        if (scale != 1.0f) g = __fdiv_rn(g, scale);
+        if (a.grad_divisor != 1.0f) g = __fdiv_rn(g, a.grad_divisor);
+        const float v0 = FRESH ? 0.0f : a.vel[idx];
+        const float v1 = __fadd_rn(__fmul_rn(mu, v0), __fmul_rn(one_m, g));
+        a.vel[idx] = v1;
+        const float u = a.nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
+        const __nv_bfloat16 h = __float2bfloat16_rn(u);
+        y = __bfloat162float(h);
+        if (!mm.transposed) X[(long long)r * cp.ld + c] = h;
+      }
+      if (mm.transposed) tile[rr][tx] = y;
+      ss = __fadd_rn(ss, __fmul_rn(y, y));
+    }
+    if (mm.transposed) {
+      __syncthreads();
+      // X[c][r] = tile[r - r0][c - c0]; consecutive threads write consecutive r.
+      for (int cc = ty; cc < kTile; cc += 4) {
+        const int c = c0 + cc, r = r0 + tx;
+        if (c < mm.cols && r < mm.rows)
+          X[(long long)c * cp.ld + r] = __float2bfloat16_rn(tile[tx][cc]);
+      }
+    }
+    const float tot = block_sum_256(ss, red);
+    if (threadIdx.x == 0) a.partials[t] = tot;
+  }
+}
+
+// Deterministic per-matrix total of the tile partials: norm = max(sqrt(sum), 1e-7).
+__global__ void __launch_bounds__(256) muon_norm_kernel(const MuonArgs a) {
+  __shared__ float red[8];
+  if (a.skip && *a.skip) return;
+  for (int k = blockIdx.x; k < a.nmat; k += gridDim.x) {
+    const MuonMat mm = a.mats[k];
+    const int ntiles = ((mm.rows + kTile - 1) / kTile) * ((mm.cols + kTile - 1) / kTile);
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < ntiles; i += 256) s = __fadd_rn(s, a.partials[mm.tile0 + i]);
+    const float tot = block_sum_256(s, red);
+    if (threadIdx.x == 0) a.norms[mm.norm_idx] = fmaxf(__fsqrt_rn(tot), 1e-7f);
+  }
+}
+
+// Muon::step_matrix tail (lib.rs:169-174): p -= (lr*scale) * O, O read back in
+// the parameter's orientation from the final Newton-Schulz X.
+template <bool SHADOW>
+__global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
+  __shared__ float tile[kTile][kTile + 1];
+  if (a.skip && *a.skip) return;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  for (int t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
+    const int k = find_mat(a.mats, a.nmat, t);
+    const MuonMat mm = a.mats[k];
+    const int tiles_c = (mm.cols + kTile - 1) / kTile;
+    const int lt = t - mm.tile0;
+    const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
+    const MuonClassPtr cp = a.cls[mm.xcls];
+    const __nv_bfloat16* X = cp.x + (long long)mm.xbatch * cp.bstride;
+    if (mm.transposed) {
+      __syncthreads();
+      for (int cc = ty; cc < kTile; cc += 4) {
+        const int c = c0 + cc, r = r0 + tx;
+        tile[cc][tx] = (c < mm.cols && r < mm.rows)
+                           ? __bfloat162float(X[(long long)c * cp.ld + r])
+                           : 0.0f;
+      }
+      __syncthreads();
+    }
+    for (int rr = ty; rr < kTile; rr += 4) {
+      const int r = r0 + rr, c = c0 + tx;
+      if (r < mm.rows && c < mm.cols) {
+        const long long idx = mm.off + (long long)r * mm.cols + c;
+        float o = mm.transposed ? tile[tx][rr] : __bfloat162float(X[(long long)r * cp.ld + c]);
+        if (a.apply_divides_norm) o = __fdiv_rn(o, a.norms[mm.norm_idx]);
+        const float pn = __fsub_rn(a.p[idx], __fmul_rn(mm.lr_scale, o));
+        a.p[idx] = pn;
+        if (SHADOW) a.p_bf16[idx] = __float2bfloat16_rn(pn);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool nonfinite_bits(uint32_t u) {
+  return (u & 0x7F800000u) == 0x7F800000u;
+}
+
+__global__ void __launch_bounds__(256) nonfinite_kernel(const float* g32, long long n32,
+                                                        const __nv_bfloat16* g16, long long n16,
+                                                        int* flag) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  bool bad = false;
+  if (g32) {
+    const long long n4 = n32 / 4;
+    const float4* p = reinterpret_cast<const float4*>(g32);
+    for (long long i = tid; i < n4; i += stride) {
+      const float4 x = __ldcs(p + i);
+      bad |= nonfinite_bits(__float_as_uint(x.x)) | nonfinite_bits(__float_as_uint(x.y)) |
+             nonfinite_bits(__float_as_uint(x.z)) | nonfinite_bits(__float_as_uint(x.w));
+    }
+    for (long long i = n4 * 4 + tid; i < n32; i += stride) bad |= nonfinite_bits(__float_as_uint(g32[i]));
+  }
+  if (g16) {
+    const long long n8 = n16 / 8;
+    const uint4* p = reinterpret_cast<const uint4*>(g16);
+    for (long long i = tid; i < n8; i += stride) {
+      const uint4 x = __ldcs(p + i);
+      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        bad |= ((w[e] & 0x7F80u) == 0x7F80u) | ((w[e] & 0x7F800000u) == 0x7F800000u);
+    }
+    for (long long i = n8 * 8 + tid; i < n16; i += stride) {
+      const uint32_t u = (uint32_t)__bfloat16_as_ushort(g16[i]) << 16;
+      bad |= nonfinite_bits(u);
+    }
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+
+__global__ void step_tail_kernel(const StepTail t) {
+  const bool skipped = t.skip && *t.skip;
+  if (!skipped) *t.step_counter += t.adamw_calls;
+  if (skipped && t.skipped_total) *t.skipped_total += 1;
+  if (t.grad_scale) {
+    if (skipped) {
+      *t.grad_scale = *t.grad_scale * 0.5f;
+      *t.good_steps = 0;
+    } else if (++*t.good_steps >= t.growth_interval) {
+      *t.grad_scale = *t.grad_scale * 2.0f;
+      *t.good_steps = 0;
+    }
+  }
+}
+
+int grid_for(long long work_items, int threads, int num_sms, int per_sm) {
+  long long blocks = (work_items + threads - 1) / threads;
+  const long long cap = (long long)num_sms * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+}  // namespace
+
+void launch_adamw(const AdamwArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.end4 <= a.begin4) return;
+  const int grid = grid_for(a.end4 - a.begin4, 256, num_sms, 8);
+  const bool bf = a.g_bf16 != nullptr, fresh = a.fresh_state != 0, sh = a.p_bf16 != nullptr;
+#define MMN_ADAMW(B, F, S) \
+  if (bf == B && fresh == F && sh == S) adamw_kernel<B, F, S><<<grid, 256, 0, stream>>>(a);
+  MMN_ADAMW(false, false, false)
+  MMN_ADAMW(false, false, true)
+  MMN_ADAMW(false, true, false)
+  MMN_ADAMW(false, true, true)
+  MMN_ADAMW(true, false, false)
+  MMN_ADAMW(true, false, true)
+  MMN_ADAMW(true, true, false)
+  MMN_ADAMW(true, true, true)
+#undef MMN_ADAMW
+}
+
+void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.total_tiles <= 0) return;
+  const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
+  const bool bf = a.g_bf16 != nullptr, fresh = a.fresh_state != 0;
+  if (bf && fresh) muon_momentum_kernel<true, true><<<grid, 256, 0, stream>>>(a);
+  if (bf && !fresh) muon_momentum_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+  if (!bf && fresh) muon_momentum_kernel<false, true><<<grid, 256, 0, stream>>>(a);
+  if (!bf && !fresh) muon_momentum_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+}
+
+void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
+  if (a.nmat <= 0) return;
+  muon_norm_kernel<<<a.nmat < 1024 ? a.nmat : 1024, 256, 0, stream>>>(a);
+}
+
+void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.total_tiles <= 0) return;
+  const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
+  if (a.p_bf16)
+    muon_apply_kernel<true><<<grid, 256, 0, stream>>>(a);
+  else
+    muon_apply_kernel<false><<<grid, 256, 0, stream>>>(a);
+}
+
+void launch_nonfinite_scan(const float* g32, long long n32, const __nv_bfloat16* g16,
+                           long long n16, int* flag, int num_sms, cudaStream_t stream) {
+  const long long work = (n32 / 4 > n16 / 8 ? n32 / 4 : n16 / 8) + 1;
+  nonfinite_kernel<<<grid_for(work, 256, num_sms, 8), 256, 0, stream>>>(g32, n32, g16, n16, flag);
+}
+
+void launch_step_tail(const StepTail& t, cudaStream_t stream) {
+  step_tail_kernel<<<1, 1, 0, stream>>>(t);
+}
+
+}  // namespace mmn

@@ -1,0 +1,54 @@
+// Host side of the batched Newton-Schulz iteration: one NsClass per matrix
+// shape (n x m after orientation, n <= m), holding the bf16 working buffers of
+// every matrix of that shape and the TMA descriptors over them.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+namespace mmn {
+
+enum NsMode : int {
+  kNsReference = 0,  // reference recipe: fp32 B kept exact via two accumulators
+  kNsBf16 = 1,       // B rounded to bf16, one accumulator (faster, looser)
+};
+
+struct NsClass {
+  int n = 0, m = 0;   // oriented shape, n <= m
+  int batch = 0;      // matrices of this shape
+  int ld_x = 0;       // row stride of X (elements, multiple of 8)
+  int ld_a = 0;       // row stride of A / A2 (elements, multiple of 8)
+  __nv_bfloat16* x[2] = {nullptr, nullptr};  // ping-pong X (batch x n x ld_x)
+  __nv_bfloat16* a = nullptr;                // bf16(X X^T)          (batch x n x ld_a)
+  __nv_bfloat16* a2 = nullptr;               // bf16(A A) or bf16(B) (batch x n x ld_a)
+  float* norms = nullptr;                    // device, batch entries
+  int2* sym_tiles = nullptr;                 // device (tm, tn) list for n x n outputs
+  int n_sym_tiles = 0;
+  CUtensorMap tm_x_a[2], tm_x_b[2], tm_x_mn[2];
+  CUtensorMap tm_a_a, tm_a_b, tm_a2_a;
+  bool owns_memory = false;
+
+  size_t x_elems() const { return (size_t)batch * n * ld_x; }
+  size_t a_elems() const { return (size_t)batch * n * ld_a; }
+};
+
+// Sizes the class, allocates its buffers (or uses the caller's when base is not
+// null; base must then hold ns_class_bytes() bytes) and encodes the tensor maps.
+// Returns an empty string on success, else a message.
+std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base);
+size_t ns_class_bytes(int n, int m, int batch);
+void ns_class_free(NsClass& c);
+
+// Runs `steps` iterations on every matrix of the class; X starts in x[0] with
+// c.norms holding the first-iteration divisors. Returns the index of the X
+// buffer that holds the result, or -1 on a launch error (message in err).
+int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
+                 cudaStream_t stream, std::string* err);
+
+// Opt-in shared memory for every GEMM instantiation (once per device).
+std::string ns_gemm_setup();
+
+}  // namespace mmn

@@ -1,0 +1,259 @@
+"""The batched, device-resident optimizer step (mmn_optim_* in include/mmn_optim.h)
+and the trainer-facing configuration (crates/mmn-train/src/lib.rs:22-41,
+crates/mmn-py/src/train_config.rs:4-56).
+
+One ``OptimizerStep`` owns every parameter, grad and optimizer-state buffer of
+a model on one GPU and steps them all with one call, replacing the per-tensor
+``optim_step_weight`` calls of crates/mmn-models/src/chatbot.rs:208-227.
+Parameters must be registered in the reference's call order
+(``chatbot_param_order`` gives it for the Chatbot model).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native as N
+from .optim import AdamWConfig, MuonConfig, NS_MODES, _stream_of
+
+
+@dataclass
+class TrainConfig:
+    """TrainConfig (crates/mmn-train/src/lib.rs:22-41); Python defaults of
+    crates/mmn-py/src/train_config.rs:21."""
+
+    epochs: int = 1
+    batch_size: int = 8
+    cuda: bool = False
+    optimizer: str = "hybrid"
+    learning_rate: float = 3e-4
+
+    def __repr__(self) -> str:  # crates/mmn-py/src/train_config.rs:37-44
+        return (f"TrainConfig(epochs={self.epochs}, batch_size={self.batch_size}, "
+                f"cuda={'true' if self.cuda else 'false'}, optimizer={self.optimizer!r}, "
+                f"learning_rate={self.learning_rate})").replace("'", '"')
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ wrapper so torch can view library memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
+def _view(ptr: int, shape, dtype: str, device: int):
+    import torch
+
+    t = torch.as_tensor(_CudaArray(ptr, shape, {"f32": "<f4", "bf16": "<i2"}[dtype]),
+                        device=f"cuda:{device}")
+    return t.view(torch.bfloat16) if dtype == "bf16" else t
+
+
+ROUTES = {"auto": N.ROUTE_AUTO, "muon": N.ROUTE_MUON, "adamw": N.ROUTE_ADAMW}
+
+
+@dataclass
+class StepConfig:
+    adamw: AdamWConfig = None
+    muon: MuonConfig = None
+    use_hybrid: bool = True
+    ns_mode: str = "reference"
+    fresh_state: bool = False
+    grad_dtype: str = "f32"
+    bf16_param_shadow: bool = False
+    loss_scaling: bool = False
+    loss_scale_init: float = 65536.0
+    growth_interval: int = 2000
+    rank: int = 0
+    world_size: int = 1
+    use_graph: bool = True
+
+    def c(self) -> N.OptimConfigC:
+        c = N.lib().mmn_optim_config_default()
+        c.adamw = (self.adamw or AdamWConfig()).c()
+        c.muon = (self.muon or MuonConfig()).c()
+        c.use_hybrid = int(self.use_hybrid)
+        c.ns_mode = NS_MODES[self.ns_mode]
+        c.fresh_state = int(self.fresh_state)
+        c.grad_dtype = {"f32": N.DTYPE_F32, "bf16": N.DTYPE_BF16}[self.grad_dtype]
+        c.bf16_param_shadow = int(self.bf16_param_shadow)
+        c.loss_scaling = int(self.loss_scaling)
+        c.loss_scale_init = self.loss_scale_init
+        c.growth_interval = self.growth_interval
+        c.rank = self.rank
+        c.world_size = self.world_size
+        c.use_graph = int(self.use_graph)
+        return c
+
+
+def step_config_for(train: TrainConfig, **overrides) -> StepConfig:
+    """The optimizer the trainer builds (crates/mmn-train/src/lib.rs:367-380):
+    Muon with MuonConfig::default() (TrainConfig.learning_rate never reaches
+    Muon), AdamW with lr = learning_rate and default betas/eps/decay, hybrid
+    routing only for optimizer == "hybrid", and fresh state every step because
+    the trainer's param ids are never reused."""
+    if train.cuda:
+        from .optim import require_cuda
+
+        require_cuda(True)
+    cfg = StepConfig(adamw=AdamWConfig(lr=train.learning_rate), muon=MuonConfig(),
+                     use_hybrid=train.optimizer == "hybrid", fresh_state=True)
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+class OptimizerStep:
+    """Whole-model optimizer step on one GPU (or one rank's shard of it)."""
+
+    def __init__(self, params, config: StepConfig | None = None, device: int = 0, stream=None):
+        """params: iterable of (id, shape) or (id, shape, route) in call order;
+        route is "auto" (reference shape rule), "muon" or "adamw"."""
+        self.config = config or StepConfig()
+        self.device = device
+        h = ctypes.c_void_p()
+        cfg = self.config.c()
+        N.check(N.lib().mmn_optim_create(ctypes.byref(cfg), device, _stream_of(device, stream),
+                                         ctypes.byref(h)))
+        self._h = h
+        self.shapes = []
+        self.routes = []
+        for p in params:
+            pid, shape = p[0], tuple(int(s) for s in p[1])
+            route = p[2] if len(p) > 2 else "auto"
+            slot = ctypes.c_int()
+            N.check(N.lib().mmn_optim_add_param(h, pid, N.shape_array(shape), len(shape),
+                                                ROUTES[route], ctypes.byref(slot)))
+            self.shapes.append(shape)
+        N.check(N.lib().mmn_optim_finalize(h))
+        for i in range(len(self.shapes)):
+            owner = ctypes.c_int()
+            N.check(N.lib().mmn_optim_slot_owner(h, i, ctypes.byref(owner)))
+            self.routes.append("muon" if owner.value >= 0 else "adamw")
+        self._views = {}
+
+    # -- buffers -----------------------------------------------------------------
+    def _ptrs(self, slot: int):
+        p, g, b = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        N.check(N.lib().mmn_optim_slot_ptrs(self._h, slot, ctypes.byref(p), ctypes.byref(g),
+                                            ctypes.byref(b)))
+        return p.value, g.value, b.value
+
+    def param(self, slot: int):
+        """torch view (fp32, device) of a slot's parameter inside the library arena."""
+        return _view(self._ptrs(slot)[0], self.shapes[slot], "f32", self.device)
+
+    def grad(self, slot: int):
+        """torch view of a slot's grad buffer (fp32 or bf16 per grad_dtype)."""
+        return _view(self._ptrs(slot)[1], self.shapes[slot],
+                     "bf16" if self.config.grad_dtype == "bf16" else "f32", self.device)
+
+    def param_bf16(self, slot: int):
+        ptr = self._ptrs(slot)[2]
+        return None if not ptr else _view(ptr, self.shapes[slot], "bf16", self.device)
+
+    def set_param(self, slot: int, values: np.ndarray) -> None:
+        v = np.ascontiguousarray(values, np.float32)
+        N.check(N.lib().mmn_optim_set_param(self._h, slot, v.ctypes.data, N.MEM_HOST))
+
+    def get_param(self, slot: int) -> np.ndarray:
+        out = np.empty(self.shapes[slot], np.float32)
+        N.check(N.lib().mmn_optim_get_param(self._h, slot, out.ctypes.data, N.MEM_HOST))
+        return out
+
+    def set_grad(self, slot: int, values: np.ndarray) -> None:
+        v = np.ascontiguousarray(values)
+        N.check(N.lib().mmn_optim_set_grad(self._h, slot, v.ctypes.data, N.MEM_HOST))
+
+    def set_state(self, slot: int, which: str, values: np.ndarray) -> None:
+        v = np.ascontiguousarray(values, np.float32)
+        N.check(N.lib().mmn_optim_set_state(self._h, slot, {"m": 0, "v": 1, "velocity": 2}[which],
+                                            v.ctypes.data, N.MEM_HOST))
+
+    def get_state(self, slot: int, which: str) -> np.ndarray:
+        out = np.empty(self.shapes[slot], np.float32)
+        N.check(N.lib().mmn_optim_get_state(self._h, slot, {"m": 0, "v": 1, "velocity": 2}[which],
+                                            out.ctypes.data, N.MEM_HOST))
+        return out
+
+    @property
+    def adamw_step(self) -> int:
+        v = ctypes.c_uint64()
+        N.check(N.lib().mmn_optim_get_adamw_step(self._h, ctypes.byref(v)))
+        return v.value
+
+    @adamw_step.setter
+    def adamw_step(self, value: int) -> None:
+        N.check(N.lib().mmn_optim_set_adamw_step(self._h, int(value)))
+
+    # -- stepping ------------------------------------------------------------------
+    def step(self, grad_divisor: float = 1.0) -> None:
+        N.check(N.lib().mmn_optim_step(self._h, grad_divisor))
+
+    def sync(self) -> None:
+        N.check(N.lib().mmn_optim_sync(self._h))
+
+    def loss_scale(self):
+        s, k = ctypes.c_float(), ctypes.c_int64()
+        N.check(N.lib().mmn_optim_loss_scale(self._h, ctypes.byref(s), ctypes.byref(k)))
+        return s.value, k.value
+
+    def enable_timing(self, on: bool = True) -> None:
+        N.check(N.lib().mmn_optim_enable_timing(self._h, int(on)))
+
+    def last_timing(self) -> dict:
+        ms = (ctypes.c_float * 5)()
+        N.check(N.lib().mmn_optim_last_timing(self._h, ms))
+        return dict(zip(("adamw", "muon_momentum", "newton_schulz", "muon_update", "step"),
+                        list(ms)))
+
+    def gather_layout(self) -> dict:
+        g = N.GatherLayoutC()
+        N.check(N.lib().mmn_optim_get_gather_layout(self._h, ctypes.byref(g)))
+        return {k: getattr(g, k) for k, _ in N.GatherLayoutC._fields_}
+
+    def param_counts(self):
+        t, a, m = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        N.check(N.lib().mmn_optim_param_counts(self._h, ctypes.byref(t), ctypes.byref(a),
+                                               ctypes.byref(m)))
+        return t.value, a.value, m.value
+
+    def ns_flops(self) -> float:
+        f = ctypes.c_double()
+        N.check(N.lib().mmn_optim_ns_flops(self._h, ctypes.byref(f)))
+        return f.value
+
+    def close(self) -> None:
+        if self._h:
+            N.lib().mmn_optim_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def chatbot_param_order(vocab_size: int, n_layer: int, d_model: int, ffn_mult: int = 4,
+                        pos_embed_len: int | None = None):
+    """(name, shape) of every trained tensor of the reference Chatbot in the order
+    its LM step calls the optimizer (crates/mmn-models/src/chatbot.rs:1104-1196,
+    block order :118-206): lm_head; blocks L-1..0 as ffn2, ffn, out, q, k, v,
+    ln2.gamma, ln2.beta, ln1.gamma, ln1.beta; embed; [pos_embed]. Linear weights
+    are [out, in] (crates/mmn-nn/src/lib.rs:305-307)."""
+    d, f = d_model, ffn_mult * d_model
+    out = [("lm_head", (vocab_size, d))]
+    for layer in reversed(range(n_layer)):
+        b = f"blocks.{layer}."
+        out += [(b + "ffn2", (d, f)), (b + "ffn", (f, d)), (b + "out", (d, d)), (b + "q", (d, d)),
+                (b + "k", (d, d)), (b + "v", (d, d)), (b + "ln2.gamma", (d,)),
+                (b + "ln2.beta", (d,)), (b + "ln1.gamma", (d,)), (b + "ln1.beta", (d,))]
+    out.append(("embed", (vocab_size, d)))
+    if pos_embed_len:
+        out.append(("pos_embed", (pos_embed_len, d)))
+    return out

@@ -1,0 +1,270 @@
+"""CPU oracle for the MagicMindNet optimizer step — TEST INFRASTRUCTURE ONLY.
+
+Python mirror of the Rust optimizer structs in crates/mmn-optim/src/lib.rs on top
+of the C restatement in mmn_optim_ref.c. Only tests/, the smoke check and the
+CPU-baseline leg of bench.py import this module; the product path never does.
+
+State handling follows the reference exactly:
+  * AdamW keeps ONE step counter per instance, advanced on every step_param
+    call (lib.rs:41-43), so every tensor stepped in one model step sees a
+    different bias-correction t.
+  * m, v and Muon velocity are created lazily as zeros per caller id
+    (lib.rs:45-46, 150-153) and never freed.
+  * Routing is by shape only (lib.rs:196-202).
+
+Parity status: partially pinned (see mmn_optim_ref.h). The reference cannot be
+run here (Rust, no toolchain); its own tests pin only the accumulator average and
+the routing table.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libmmn_optim_ref.so")
+
+GEMM_F32_SEQ, GEMM_F32_FMA, GEMM_F64 = 0, 1, 2
+NS_REFERENCE, NS_BF16 = 0, 1
+
+_f = ctypes.c_float
+_i64 = ctypes.c_int64
+_fp = ctypes.POINTER(ctypes.c_float)
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc) and return the .so path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.ref_bf16_round.restype = _f
+        L.ref_bf16_round.argtypes = [_f]
+        L.ref_adamw_step.argtypes = [_fp, _fp, _fp, _fp, _i64, _f, _f, _f, _f, _f, _i64, _f]
+        L.ref_adamw_step_timed.restype = ctypes.c_double
+        L.ref_adamw_step_timed.argtypes = [_fp, _fp, _fp, _fp, _i64, _f, _f, _f, _f, _f,
+                                           _i64, _f, ctypes.c_int]
+        L.ref_muon_momentum.argtypes = [_fp, _fp, _fp, _i64, _f, ctypes.c_int, _f]
+        L.ref_newton_schulz5.argtypes = [_fp, _i64, _i64, ctypes.c_int, _fp, ctypes.c_int,
+                                         ctypes.c_int, _fp, ctypes.c_int]
+        L.ref_ns_iteration.argtypes = [_fp, _i64, _i64, _fp, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int]
+        L.ref_gemm.argtypes = [_fp, _fp, _fp, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int]
+        L.ref_muon_apply.argtypes = [_fp, _fp, _i64, _i64, _f]
+        L.ref_muon_scale.restype = _f
+        L.ref_muon_scale.argtypes = [_i64, _i64]
+        L.ref_bias_correction.restype = _f
+        L.ref_bias_correction.argtypes = [_f, _i64]
+        L.ref_grad_average.argtypes = [_fp, _fp, _i64, _i64]
+        L.ref_max_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Vectorised bf16 round-to-nearest-even (same rule as ref_bf16_round)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    lo = u & 0xFFFF
+    hi = u >> 16
+    up = (lo > 0x8000) | ((lo == 0x8000) & ((hi & 1) == 1))
+    r = ((hi + up.astype(np.uint64)) << 16)
+    r = np.where(nan, (u | 0x00400000) & 0xFFFF0000, r)
+    return r.astype(np.uint32).view(np.float32).reshape(x.shape)
+
+
+def bias_correction(beta: float, t: int) -> float:
+    return float(lib().ref_bias_correction(beta, t))
+
+
+def muon_scale(rows: int, cols: int) -> float:
+    return float(lib().ref_muon_scale(rows, cols))
+
+
+def adamw_update(p, m, v, g, *, lr, betas, eps, weight_decay, t, grad_divisor=1.0):
+    """In-place AdamW update of one tensor at step count t (lib.rs:41-60)."""
+    lib().ref_adamw_step(_ptr(p), _ptr(m), _ptr(v), _ptr(np.ascontiguousarray(g, np.float32)),
+                         p.size, lr, betas[0], betas[1], eps, weight_decay, t, grad_divisor)
+
+
+def muon_momentum(vel, g, *, momentum, nesterov, grad_divisor=1.0):
+    u = np.empty_like(vel)
+    lib().ref_muon_momentum(_ptr(vel), _ptr(np.ascontiguousarray(g, np.float32)), _ptr(u),
+                            vel.size, momentum, int(nesterov), grad_divisor)
+    return u
+
+
+def gemm(a, b, order=GEMM_F64, threads=0):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    c = np.empty((a.shape[0], b.shape[1]), np.float32)
+    lib().ref_gemm(_ptr(a), _ptr(b), _ptr(c), a.shape[0], b.shape[1], a.shape[1], order, threads)
+    return c
+
+
+def pad_to_square(g: np.ndarray) -> np.ndarray:
+    """lib.rs:89-99: a non-2-D input is zero-padded row-major into side x side,
+    side = ceil(sqrt(len)) computed in f32."""
+    if g.ndim == 2:
+        return np.ascontiguousarray(g, np.float32)
+    n = g.size
+    side = int(np.ceil(np.sqrt(np.float32(n), dtype=np.float32)))
+    out = np.zeros(side * side, np.float32)
+    out[:n] = g.reshape(-1)
+    return out.reshape(side, side)
+
+
+def newton_schulz5(g, steps=5, order=GEMM_F32_FMA, variant=NS_REFERENCE, threads=0,
+                   return_norm=False):
+    """newton_schulz5 (lib.rs:83-126). Output has the (padded) 2-D input shape."""
+    g2 = pad_to_square(np.asarray(g, np.float32))
+    rows, cols = g2.shape
+    out = np.empty((rows, cols), np.float32)
+    norm = _f(0.0)
+    lib().ref_newton_schulz5(_ptr(g2), rows, cols, steps, _ptr(out), order, variant,
+                             ctypes.byref(norm), threads)
+    return (out, float(norm.value)) if return_norm else out
+
+
+def ns_iteration(x, order=GEMM_F64, variant=NS_REFERENCE, threads=0):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().ref_ns_iteration(_ptr(x), x.shape[0], x.shape[1], _ptr(y), order, variant, threads)
+    return y
+
+
+def muon_apply(p, o, lr):
+    lib().ref_muon_apply(_ptr(p), _ptr(np.ascontiguousarray(o, np.float32)), p.shape[0],
+                         p.shape[1] if p.ndim > 1 else 1, lr)
+
+
+class AdamWConfig:
+    """lib.rs:6-22; defaults lr 3e-4, betas (0.9, 0.95), eps 1e-8, wd 0.01."""
+
+    def __init__(self, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01):
+        self.lr, self.betas, self.eps, self.weight_decay = lr, tuple(betas), eps, weight_decay
+
+
+class MuonConfig:
+    """lib.rs:63-80; defaults lr 0.02, momentum 0.95, nesterov, 5 steps."""
+
+    def __init__(self, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5):
+        self.lr, self.momentum, self.nesterov, self.ns_steps = lr, momentum, nesterov, ns_steps
+
+
+class AdamW:
+    """lib.rs:24-61."""
+
+    def __init__(self, config: AdamWConfig):
+        self.config = config
+        self.step = 0
+        self.m: dict[int, np.ndarray] = {}
+        self.v: dict[int, np.ndarray] = {}
+
+    def step_param(self, pid: int, param: np.ndarray, grad: np.ndarray, grad_divisor=1.0):
+        self.step += 1
+        m = self.m.setdefault(pid, np.zeros(param.shape, np.float32))
+        v = self.v.setdefault(pid, np.zeros(param.shape, np.float32))
+        c = self.config
+        adamw_update(param, m, v, grad, lr=c.lr, betas=c.betas, eps=c.eps,
+                     weight_decay=c.weight_decay, t=self.step, grad_divisor=grad_divisor)
+
+
+class Muon:
+    """lib.rs:128-176."""
+
+    def __init__(self, config: MuonConfig, order=GEMM_F32_FMA, variant=NS_REFERENCE):
+        self.config = config
+        self.velocity: dict[int, np.ndarray] = {}
+        self.order, self.variant = order, variant
+
+    def step_matrix(self, pid: int, param: np.ndarray, grad: np.ndarray, grad_divisor=1.0):
+        g2 = np.ascontiguousarray(grad, np.float32)
+        if g2.ndim != 2:
+            side = int(np.ceil(np.sqrt(np.float32(g2.size), dtype=np.float32)))
+            g2 = g2.reshape(side, side)  # lib.rs:146-149 (panics unless len == side^2)
+        vel = self.velocity.setdefault(pid, np.zeros(g2.shape, np.float32))
+        c = self.config
+        u = muon_momentum(vel, g2, momentum=c.momentum, nesterov=c.nesterov,
+                          grad_divisor=grad_divisor)
+        o = newton_schulz5(u, c.ns_steps, order=self.order, variant=self.variant)
+        muon_apply(param, o, c.lr)
+
+
+MATRIX, OTHER = "Matrix", "Other"
+
+
+def classify_param(shape) -> str:
+    """lib.rs:196-202."""
+    return MATRIX if len(shape) == 2 and shape[0] > 1 and shape[1] > 1 else OTHER
+
+
+class HybridOptimizer:
+    """lib.rs:183-210."""
+
+    def __init__(self, muon: MuonConfig, adamw: AdamWConfig, order=GEMM_F32_FMA,
+                 variant=NS_REFERENCE):
+        self.muon = Muon(muon, order, variant)
+        self.adamw = AdamW(adamw)
+
+    def step(self, pid, param, grad, route=None, grad_divisor=1.0):
+        kind = route or classify_param(param.shape)
+        if kind == MATRIX:
+            self.muon.step_matrix(pid, param, grad, grad_divisor)
+        else:
+            self.adamw.step_param(pid, param, grad, grad_divisor)
+
+
+class GradAccumulator:
+    """lib.rs:212-262."""
+
+    def __init__(self):
+        self.grads: list[np.ndarray] = []
+        self.micro_batches = 0
+        self.param_index = 0
+
+    def clear(self):
+        self.grads.clear()
+        self.micro_batches = 0
+        self.param_index = 0
+
+    def begin_micro_batch(self):
+        self.param_index = 0
+
+    def finish_micro_batch(self):
+        self.micro_batches += 1
+        self.param_index = 0
+
+    def add_param_grad(self, grad):
+        if self.param_index < len(self.grads):
+            self.grads[self.param_index] += np.asarray(grad, np.float32)
+        else:
+            self.grads.append(np.array(grad, np.float32, copy=True))
+        self.param_index += 1
+
+    def averaged_grad(self, index):
+        s = self.grads[index]
+        out = np.empty_like(s)
+        lib().ref_grad_average(_ptr(s), _ptr(out), s.size, self.micro_batches)
+        return out
+
+    def __len__(self):
+        return len(self.grads)

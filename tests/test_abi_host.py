@@ -1,0 +1,142 @@
+"""CPU-only checks of the boundary and the host logic: the C-ABI library loads
+and exports every function include/mmn_optim.h declares; configuration, call
+order and CUDA gating behave like the reference's."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    text = open(os.path.join(ROOT, "include", "mmn_optim.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mmn_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+    names = declared_functions()
+    assert len(names) >= 45
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    # the ctypes table covers exactly the declared functions
+    assert sorted(N.SIGNATURES) == names
+
+
+def test_abi_version_and_defaults():
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+    assert L.mmn_abi_version() == 1
+    a = L.mmn_adamw_config_default()
+    assert (round(a.lr, 7), round(a.beta1, 6), round(a.beta2, 6), a.eps, round(a.weight_decay, 6)) \
+        == (3e-4, 0.9, 0.95, np.float32(1e-8), 0.01)
+    m = L.mmn_muon_config_default()
+    assert (round(m.lr, 6), round(m.momentum, 6), m.nesterov, m.ns_steps) == (0.02, 0.95, 1, 5)
+
+
+def test_classify_param_matches_reference_table():
+    import magicmindnet_b200 as mmn
+
+    H = mmn.HybridOptimizer.classify_param
+    assert H((64, 32)) == "Matrix"
+    assert H((16,)) == "Other"
+    assert H((16, 1)) == "Other"
+    assert H((1, 3, 3, 3)) == "Other"
+    assert H((2, 2)) == "Matrix"
+
+
+def test_cuda_gate_without_gpu():
+    """crates/mmn-core/src/device.rs:29-37 + tests/test_cuda_parity.py of the
+    reference: cuda=True without a usable device raises CUDAError; cuda=False
+    never does."""
+    import magicmindnet_b200 as mmn
+
+    mmn.require_cuda(False)
+    if mmn.is_available():
+        mmn.require_cuda(True)
+        return
+    with pytest.raises(mmn.CUDAError):
+        mmn.require_cuda(True)
+    with pytest.raises(mmn.CUDAError):
+        mmn.step_config_for(mmn.TrainConfig(cuda=True))
+    with pytest.raises(mmn.CUDAError):
+        mmn.AdamW()
+
+
+def test_train_config_defaults_and_repr():
+    """crates/mmn-py/src/train_config.rs:21,37-44."""
+    import magicmindnet_b200 as mmn
+
+    c = mmn.TrainConfig()
+    assert (c.epochs, c.batch_size, c.cuda, c.optimizer, c.learning_rate) == (1, 8, False, "hybrid",
+                                                                            3e-4)
+    assert repr(c) == ('TrainConfig(epochs=1, batch_size=8, cuda=false, optimizer="hybrid", '
+                       'learning_rate=0.0003)')
+
+
+def test_step_config_follows_trainer_construction():
+    """crates/mmn-train/src/lib.rs:367-380: AdamW gets learning_rate, Muon keeps
+    its defaults, only "hybrid" routes to Muon, ids never repeat."""
+    import magicmindnet_b200 as mmn
+
+    s = mmn.step_config_for(mmn.TrainConfig(learning_rate=1e-3, optimizer="hybrid"))
+    assert s.use_hybrid and s.fresh_state and s.adamw.lr == 1e-3 and s.muon.lr == 0.02
+    for opt in ("adamw", "muon"):
+        assert not mmn.step_config_for(mmn.TrainConfig(optimizer=opt)).use_hybrid
+
+
+def test_chatbot_param_order_config1():
+    """22 tensors / 164,352 params; 14 Muon matrices (163,840) under the
+    reference rule, in the call order of crates/mmn-models/src/chatbot.rs."""
+    import magicmindnet_b200 as mmn
+
+    order = mmn.chatbot_param_order(512, 2, 64)
+    assert len(order) == 22
+    assert sum(int(np.prod(s)) for _, s in order) == 164352
+    muon = [s for _, s in order if mmn.HybridOptimizer.classify_param(s) == "Matrix"]
+    assert len(muon) == 14 and sum(int(np.prod(s)) for s in muon) == 163840
+    names = [n for n, _ in order]
+    assert names[0] == "lm_head" and names[-1] == "embed"
+    assert names[1:11] == ["blocks.1." + x for x in ("ffn2", "ffn", "out", "q", "k", "v",
+                                                      "ln2.gamma", "ln2.beta", "ln1.gamma",
+                                                      "ln1.beta")]
+
+
+def test_grad_accumulator_mirror():
+    import magicmindnet_b200 as mmn
+
+    acc = mmn.GradAccumulator()
+    for val in (1.0, 3.0):
+        acc.begin_micro_batch()
+        acc.add_param_grad(np.array([[val]], np.float32))
+        acc.finish_micro_batch()
+    assert acc.divisor == 2.0
+    assert abs(acc.averaged_grad(0)[0, 0] - 2.0) < 1e-6
+    acc.clear()
+    assert len(acc) == 0 and acc.divisor == 1.0
+
+
+def test_bench_workload_sizes():
+    import bench
+
+    n1b = bench.count_params(bench.WORKLOADS["hybrid_1b"]["model"]())
+    n8b = bench.count_params(bench.WORKLOADS["hybrid_8b"]["model"]())
+    assert n1b == 1339228160 and n8b == 5362941952
+    muon_1b = sum(s[0] * s[1] for _, s, r in bench.WORKLOADS["hybrid_1b"]["model"]() if r == "muon")
+    assert muon_1b == 1207959552
+
+
+def test_errors_report_through_last_error():
+    from magicmindnet_b200 import _native as N
+
+    h = ctypes.c_void_p()
+    rc = N.lib().mmn_optim_create(None, -5, None, ctypes.byref(h))
+    assert rc in (N.MMN_E_INVALID, N.MMN_E_NO_DEVICE)
+    assert N.lib().mmn_last_error()
