@@ -75,6 +75,9 @@ WORKLOADS = {
     "ns_batch": dict(model=lambda: [(f"sq{i}", (4096, 4096), "muon") for i in range(64)] +
                      [(f"ffn{i}", (4096, 14336), "muon") for i in range(32)], grad="f32",
                      desc="Newton-Schulz on 64 x [4096,4096] + 32 x [4096,14336]"),
+    "ns_probe": dict(model=lambda: [(f"ffn{i}", (2048, 8192), "muon") for i in range(8)],
+                     grad="f32", desc="Newton-Schulz on 8 x [2048,8192] (profiling case: "
+                                      "X is 268 MB, larger than L2; about 1.5 GB on the device)"),
 }
 
 
