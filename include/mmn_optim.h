@@ -154,6 +154,23 @@ int mmn_muon_import_velocity(mmn_muon_t *h, uint64_t id, const float *buf, int64
 int mmn_newton_schulz5(const float *g, const int64_t *shape, int ndim, int steps, int ns_mode,
                        float *out, int device, void *stream, int mem);
 
+/* newton_schulz5 that allocates no device memory. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc (device memory
+ * wholly owned by another framework's allocator or a fixed arena, hosts that
+ * forbid allocation after start-up, or paths where cudaMalloc's implicit
+ * device synchronisation is not acceptable). Same kernels and result as
+ * mmn_newton_schulz5 on a rows x cols matrix; g and out are device pointers
+ * (rows*cols floats) on `device`. Its scratch is one fixed 8.25 MiB array in
+ * the library, held by every GPU that loads the library until exit, so the
+ * size is limited to min(rows, cols) <= 1024 and rows*cols <= 1048576; larger
+ * inputs return MMN_E_UNSUPPORTED. The first call on a device resolves that
+ * array's device address and should come before any stream capture. All calls
+ * on a device share the array, so calls that overlap on the GPU race. Work is
+ * enqueued on `stream` (NULL = legacy default stream) and the call returns
+ * after it has finished. */
+int mmn_newton_schulz5_noalloc(const float *g, int64_t rows, int64_t cols, int steps,
+                               int ns_mode, float *out, int device, void *stream);
+
 /* One loop body of newton_schulz5 (lib.rs:113-119) on an n x m (n <= m)
  * matrix x whose values are bf16-representable, divided by x_norm first
  * (x_norm = the Frobenius norm for the first iteration, 1 afterwards). Writes

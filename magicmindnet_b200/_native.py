@@ -98,6 +98,7 @@ SIGNATURES = {
     "mmn_muon_export_velocity": (_i, [_vp, _u64, _vp, _i64, _i]),
     "mmn_muon_import_velocity": (_i, [_vp, _u64, _vp, _i64, _i]),
     "mmn_newton_schulz5": (_i, [_vp, _i64p, _i, _i, _i, _vp, _i, _vp, _i]),
+    "mmn_newton_schulz5_noalloc": (_i, [_vp, _i64, _i64, _i, _i, _vp, _i, _vp]),
     "mmn_newton_schulz_iteration": (_i, [_vp, _i64, _i64, _f, _i, _vp, _vp, _vp, _i]),
     "mmn_hybrid_classify_param": (_i, [_i64p, _i]),
     "mmn_hybrid_create": (_i, [ctypes.POINTER(MuonConfigC), ctypes.POINTER(AdamWConfigC), _i, _i,

@@ -21,7 +21,7 @@ LIB_NAME = "libmmn_optim_cuda.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
 SOURCES = ["elementwise.cu", "ns_engine.cu", "capi_common.cu", "capi_percall.cu",
-           "capi_batched.cu"]
+           "capi_batched.cu", "ns_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
               "-Wall", "-I", os.path.join(ROOT, "include")]

@@ -135,6 +135,49 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
   return "";
 }
 
+std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
+                          std::vector<int2>* tiles_out) {
+  if (n <= 0 || m <= 0 || n > m || batch <= 0 || !base || !tiles_out)
+    return "invalid Newton-Schulz class shape or base";
+  std::string err = get_encode();
+  if (!err.empty()) return err;
+  c = NsClass();
+  c.n = n;
+  c.m = m;
+  c.batch = batch;
+  c.ld_x = round_up(m, 8);
+  c.ld_a = round_up(n, 8);
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  c.x[0] = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += al(c.x_elems() * 2);
+  c.x[1] = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += al(c.x_elems() * 2);
+  c.a = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += al(c.a_elems() * 2);
+  c.a2 = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += al(c.a_elems() * 2);
+  c.norms = reinterpret_cast<float*>(p + off);
+  off += al((size_t)batch * 4);
+  c.sym_tiles = reinterpret_cast<int2*>(p + off);
+  tiles_out->clear();
+  const int tm_n = (n + kBM - 1) / kBM, tn_n = (n + 255) / 256;
+  for (int tm = 0; tm < tm_n; ++tm)
+    for (int tn = 0; tn < tn_n; ++tn)
+      if (tn * 256 + 255 >= tm * kBM) tiles_out->push_back(make_int2(tm, tn));
+  c.n_sym_tiles = (int)tiles_out->size();
+  for (int i = 0; i < 2; ++i) {
+    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM)).empty()) return err;
+    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256)).empty()) return err;
+    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, batch, c.ld_x, 64)).empty()) return err;
+  }
+  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
+  return "";
+}
+
 void ns_class_free(NsClass& c) {
   if (c.owns_memory && c.x[0]) cudaFree(c.x[0]);
   c = NsClass();

@@ -42,6 +42,12 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base);
 size_t ns_class_bytes(int n, int m, int batch);
 void ns_class_free(NsClass& c);
 
+// Lays the class out over caller memory at `base` (ns_class_bytes() bytes) and
+// encodes its tensor maps, touching no device memory: the caller clears the
+// region and uploads `tiles_out` to c.sym_tiles on its own stream.
+std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
+                          std::vector<int2>* tiles_out);
+
 // Runs `steps` iterations on every matrix of the class; X starts in x[0] with
 // c.norms holding the first-iteration divisors. Returns the index of the X
 // buffer that holds the result, or -1 on a launch error (message in err).
