@@ -11,6 +11,7 @@
 #include "capi_internal.cuh"
 #include "elementwise.cuh"
 #include "ns_engine.cuh"
+#include "ns_gemm.cuh"
 
 using namespace mmn;
 
@@ -70,6 +71,8 @@ struct mmn_optim {
   MuonClassPtr *d_cls_in = nullptr, *d_cls_out = nullptr;
   float* d_partials = nullptr;
   float* d_norms = nullptr;
+  NsApply* d_apply = nullptr;   // per owned matrix, indexed like the norms
+  std::vector<int> cls_base;    // first norm / apply slot of every class
   int total_tiles = 0;
   double ns_flops = 0.0;
   int64_t n_params = 0, n_adamw_params = 0, n_muon_params = 0;
@@ -311,6 +314,13 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
     norm_base += cls_count[k];
   }
   for (auto& mm : h->mats) mm.norm_idx = cls_norm0[mm.xcls] + mm.xbatch;
+  h->cls_base = cls_norm0;
+  std::vector<NsApply> applies((size_t)std::max(norm_base, 1));
+  for (auto& mm : h->mats) {
+    applies[mm.norm_idx].off = mm.off;
+    applies[mm.norm_idx].lr_scale = mm.lr_scale;
+    applies[mm.norm_idx].transposed = mm.transposed;
+  }
 
   // ---- device allocations
   const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
@@ -335,6 +345,7 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   if ((rc = h->dalloc((void**)&h->d_cls_out, ncls * sizeof(MuonClassPtr))) != MMN_OK) return rc;
   if ((rc = h->dalloc((void**)&h->d_partials, (size_t)std::max(tiles, 1) * 4)) != MMN_OK) return rc;
   if ((rc = h->dalloc((void**)&h->d_norms, (size_t)std::max(norm_base, 1) * 4)) != MMN_OK) return rc;
+  if ((rc = h->dalloc((void**)&h->d_apply, applies.size() * sizeof(NsApply))) != MMN_OK) return rc;
   if ((rc = h->dalloc((void**)&h->d_step, sizeof(long long))) != MMN_OK) return rc;
   if ((rc = h->dalloc((void**)&h->d_skip, sizeof(int))) != MMN_OK) return rc;
   if ((rc = h->dalloc((void**)&h->d_scale, sizeof(float))) != MMN_OK) return rc;
@@ -345,6 +356,8 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaMemcpy(h->d_chunk_seg, chunk_seg.data(), chunk_seg.size() * sizeof(int),
                           cudaMemcpyHostToDevice));
   MMN_CUDA_TRY(cudaMemcpy(h->d_mats, h->mats.data(), h->mats.size() * sizeof(MuonMat),
+                          cudaMemcpyHostToDevice));
+  MMN_CUDA_TRY(cudaMemcpy(h->d_apply, applies.data(), applies.size() * sizeof(NsApply),
                           cudaMemcpyHostToDevice));
   std::vector<MuonClassPtr> cin(ncls), cout(ncls);
   for (size_t k = 0; k < h->classes.size(); ++k) {
@@ -596,16 +609,25 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
     launch_muon_norms(m, s);
     MMN_CUDA_TRY(cudaGetLastError());
     if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
-    for (auto& c : h->classes) {
+    // The last Newton-Schulz iteration applies p -= lr*scale*O itself
+    // (lib.rs:169-174); with zero iterations the update kernel does it.
+    const bool fuse = h->cfg.muon.ns_steps >= 1;
+    for (size_t k = 0; k < h->classes.size(); ++k) {
+      NsFused f;
+      f.p = h->mp;
+      f.p_bf16 = h->mp16;
+      f.apply = h->d_apply + h->cls_base[k];
       std::string err;
-      if (ns_class_run(c, h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status, h->ctx.num_sms, s,
-                       &err) < 0)
+      if (ns_class_run(h->classes[k], h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status,
+                       h->ctx.num_sms, s, &err, fuse ? &f : nullptr) < 0)
         return fail(MMN_E_CUDA, err);
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
-    m.cls = h->d_cls_out;
-    launch_muon_apply(m, h->ctx.num_sms, s);
-    MMN_CUDA_TRY(cudaGetLastError());
+    if (!fuse) {
+      m.cls = h->d_cls_out;
+      launch_muon_apply(m, h->ctx.num_sms, s);
+      MMN_CUDA_TRY(cudaGetLastError());
+    }
   } else if (tm) {
     MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
     MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));

@@ -43,59 +43,29 @@ std::string encode_3d(CUtensorMap* map, const void* base, int inner, int rows, i
 
 int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int BN, bool DUAL, bool B_MN, int EPI>
-cudaError_t set_smem() {
-  using S = NsGemmShape<BN, DUAL, B_MN>;
-  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+// Tiles of an n x n symmetric output that touch the upper triangle, for
+// tile_m-row by 256-column tiles.
+void sym_tile_list(int n, int tile_m, std::vector<int2>* out) {
+  const int tm_n = (n + tile_m - 1) / tile_m, tn_n = (n + 255) / 256;
+  for (int tm = 0; tm < tm_n; ++tm)
+    for (int tn = 0; tn < tn_n; ++tn)
+      if (tn * 256 + 255 >= tm * tile_m) out->push_back(make_int2(tm, tn));
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI>
-cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
-                   const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
-  using S = NsGemmShape<BN, DUAL, B_MN>;
-  if (args.num_tiles <= 0) return cudaSuccess;
-  const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
-  ns_gemm_kernel<BN, DUAL, B_MN, EPI><<<grid, 192, S::kSmemBytes, stream>>>(a1, a2, b, args);
-  return cudaGetLastError();
+size_t sym_tiles_total(int n) {
+  const size_t a = (size_t)((n + 127) / 128) * ((n + 255) / 256);
+  const size_t b = (size_t)((n + 255) / 256) * ((n + 255) / 256);
+  return a + b;
 }
 
-}  // namespace
-
-std::string ns_gemm_setup() {
-  cudaError_t e = cudaSuccess;
-  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiGram>();
-  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare>();
-  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquareBf16>();
-  if (e == cudaSuccess) e = set_smem<128, true, true, kEpiPolyDual>();
-  if (e == cudaSuccess) e = set_smem<256, false, true, kEpiPolySingle>();
-  if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-  return get_encode();
-}
-
-size_t ns_class_bytes(int n, int m, int batch) {
-  const size_t ld_x = (size_t)round_up(m, 8), ld_a = (size_t)round_up(n, 8);
-  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-  const int tm = (n + kBM - 1) / kBM, tn = (n + 255) / 256;
-  return 2 * al((size_t)batch * n * ld_x * 2) + 2 * al((size_t)batch * n * ld_a * 2) +
-         al((size_t)batch * 4) + al((size_t)tm * tn * sizeof(int2));
-}
-
-std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
-  if (n <= 0 || m <= 0 || n > m || batch <= 0) return "invalid Newton-Schulz class shape";
-  std::string err = get_encode();
-  if (!err.empty()) return err;
+// Lays out the buffers of a class over `p` and encodes its tensor maps.
+std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
+                   std::vector<int2>* tiles) {
   c.n = n;
   c.m = m;
   c.batch = batch;
   c.ld_x = round_up(m, 8);
   c.ld_a = round_up(n, 8);
-  const size_t bytes = ns_class_bytes(n, m, batch);
-  uint8_t* p = static_cast<uint8_t*>(base);
-  if (!p) {
-    if (cudaMalloc(&p, bytes) != cudaSuccess) return "cudaMalloc failed for Newton-Schulz buffers";
-    c.owns_memory = true;
-  }
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
   size_t off = 0;
   c.x[0] = reinterpret_cast<__nv_bfloat16*>(p + off);
@@ -108,22 +78,14 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
   off += al(c.a_elems() * 2);
   c.norms = reinterpret_cast<float*>(p + off);
   off += al((size_t)batch * 4);
+  tiles->clear();
+  sym_tile_list(n, kBM, tiles);
+  c.n_sym_tiles = (int)tiles->size();
+  sym_tile_list(n, 2 * kBM, tiles);
+  c.n_sym_tiles2 = (int)tiles->size() - c.n_sym_tiles;
   c.sym_tiles = reinterpret_cast<int2*>(p + off);
-  // Padding columns of X and A are never written by the kernels but are read
-  // by nothing either (the tensor maps stop at n / m); zero them once anyway.
-  if (cudaMemset(p, 0, bytes) != cudaSuccess) return "cudaMemset failed";
-
-  // Tiles of an n x n symmetric output that touch the upper triangle.
-  std::vector<int2> tiles;
-  const int tm_n = (n + kBM - 1) / kBM, tn_n = (n + 255) / 256;
-  for (int tm = 0; tm < tm_n; ++tm)
-    for (int tn = 0; tn < tn_n; ++tn)
-      if (tn * 256 + 255 >= tm * kBM) tiles.push_back(make_int2(tm, tn));
-  c.n_sym_tiles = (int)tiles.size();
-  if (cudaMemcpy(c.sym_tiles, tiles.data(), tiles.size() * sizeof(int2), cudaMemcpyHostToDevice) !=
-      cudaSuccess)
-    return "cudaMemcpy of the tile list failed";
-
+  c.sym_tiles2 = c.sym_tiles + c.n_sym_tiles;
+  std::string err;
   for (int i = 0; i < 2; ++i) {
     if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM)).empty()) return err;
     if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256)).empty()) return err;
@@ -132,6 +94,101 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
   if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
+  return "";
+}
+
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
+cudaError_t set_smem() {
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
+  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+}
+
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
+cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
+                   const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
+  if (args.num_tiles <= 0) return cudaSuccess;
+  if (!PAIR) {
+    const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
+    ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR><<<grid, 192, S::kSmemBytes, stream>>>(a1, a2, b, args);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = S::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // A persistent grid must not exceed the clusters that fit at once: a
+  // cluster scheduled late would run its whole tile list after the others.
+  static int max_pairs = 0;
+  if (max_pairs == 0) {
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
+                                                   &cfg);
+    if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
+    max_pairs = n < num_sms / 2 ? n : num_sms / 2;
+  }
+  const int pairs = args.num_tiles < max_pairs ? args.num_tiles : max_pairs;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>, a1, a2, b, args);
+}
+
+// CTA pairs pay off once a matrix fills 256-row tiles.
+bool use_pairs(const NsClass& c) { return c.n >= 256; }
+
+}  // namespace
+
+std::string ns_gemm_setup() {
+  cudaError_t e = cudaSuccess;
+#define MMN_SET(BN, D, MN, E)                                  \
+  if (e == cudaSuccess) e = set_smem<BN, D, MN, E, false>();   \
+  if (e == cudaSuccess) e = set_smem<BN, D, MN, E, true>();
+  MMN_SET(256, false, false, kEpiGram)
+  MMN_SET(256, false, false, kEpiSquare)
+  MMN_SET(256, false, false, kEpiSquareBf16)
+  MMN_SET(128, true, true, kEpiPolyDual)
+  MMN_SET(256, false, true, kEpiPolySingle)
+#undef MMN_SET
+  if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+  return get_encode();
+}
+
+size_t ns_class_bytes(int n, int m, int batch) {
+  const size_t ld_x = (size_t)round_up(m, 8), ld_a = (size_t)round_up(n, 8);
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  return 2 * al((size_t)batch * n * ld_x * 2) + 2 * al((size_t)batch * n * ld_a * 2) +
+         al((size_t)batch * 4) + al(sym_tiles_total(n) * sizeof(int2));
+}
+
+std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
+  if (n <= 0 || m <= 0 || n > m || batch <= 0) return "invalid Newton-Schulz class shape";
+  std::string err = get_encode();
+  if (!err.empty()) return err;
+  const size_t bytes = ns_class_bytes(n, m, batch);
+  uint8_t* p = static_cast<uint8_t*>(base);
+  bool own = false;
+  if (!p) {
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return "cudaMalloc failed for Newton-Schulz buffers";
+    own = true;
+  }
+  std::vector<int2> tiles;
+  err = layout(c, n, m, batch, p, &tiles);
+  c.owns_memory = own;
+  if (!err.empty()) return err;
+  // Padding columns of X and A are never read (the tensor maps stop at n / m);
+  // zero them once anyway.
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) return "cudaMemset failed";
+  if (cudaMemcpy(c.sym_tiles, tiles.data(), tiles.size() * sizeof(int2), cudaMemcpyHostToDevice) !=
+      cudaSuccess)
+    return "cudaMemcpy of the tile list failed";
   return "";
 }
 
@@ -142,40 +199,7 @@ std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
   std::string err = get_encode();
   if (!err.empty()) return err;
   c = NsClass();
-  c.n = n;
-  c.m = m;
-  c.batch = batch;
-  c.ld_x = round_up(m, 8);
-  c.ld_a = round_up(n, 8);
-  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-  uint8_t* p = static_cast<uint8_t*>(base);
-  size_t off = 0;
-  c.x[0] = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.x_elems() * 2);
-  c.x[1] = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.x_elems() * 2);
-  c.a = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.a_elems() * 2);
-  c.a2 = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.a_elems() * 2);
-  c.norms = reinterpret_cast<float*>(p + off);
-  off += al((size_t)batch * 4);
-  c.sym_tiles = reinterpret_cast<int2*>(p + off);
-  tiles_out->clear();
-  const int tm_n = (n + kBM - 1) / kBM, tn_n = (n + 255) / 256;
-  for (int tm = 0; tm < tm_n; ++tm)
-    for (int tn = 0; tn < tn_n; ++tn)
-      if (tn * 256 + 255 >= tm * kBM) tiles_out->push_back(make_int2(tm, tn));
-  c.n_sym_tiles = (int)tiles_out->size();
-  for (int i = 0; i < 2; ++i) {
-    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM)).empty()) return err;
-    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256)).empty()) return err;
-    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, batch, c.ld_x, 64)).empty()) return err;
-  }
-  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
-  return "";
+  return layout(c, n, m, batch, static_cast<uint8_t*>(base), tiles_out);
 }
 
 void ns_class_free(NsClass& c) {
@@ -186,78 +210,97 @@ void ns_class_free(NsClass& c) {
 // Coefficients of the quintic iteration (crates/mmn-optim/src/lib.rs:84-86).
 static constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;
 
+namespace {
+
+template <bool PAIR>
+cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int mode,
+                          const NsGemmArgs& base, const NsFused* fused, int num_sms,
+                          cudaStream_t stream) {
+  const int tile_m = PAIR ? 2 * kBM : kBM;
+  NsGemmArgs g = base;
+
+  // A = bf16((X X^T) / s / s)
+  g.out = c.a;
+  g.out_bstride = (long long)c.n * c.ld_a;
+  g.out_ld = c.ld_a;
+  g.aux = nullptr;
+  g.norms = norms;
+  g.M = c.n;
+  g.N = c.n;
+  g.K = c.m;
+  g.tile_list = PAIR ? c.sym_tiles2 : c.sym_tiles;
+  g.tiles_per_matrix = PAIR ? c.n_sym_tiles2 : c.n_sym_tiles;
+  g.tiles_n = 0;
+  g.num_tiles = g.tiles_per_matrix * c.batch;
+  // B is the same X rows: 128 rows per CTA of a pair, 256 for a single CTA.
+  const CUtensorMap& xb = PAIR ? c.tm_x_a[cur] : c.tm_x_b[cur];
+  cudaError_t e =
+      launch<256, false, false, kEpiGram, PAIR>(c.tm_x_a[cur], c.tm_x_a[cur], xb, g, num_sms, stream);
+  if (e != cudaSuccess) return e;
+
+  // A2 = bf16(A A)   or   Bm = bf16(b*A + c*bf16(A A))
+  g.out = c.a2;
+  g.norms = nullptr;
+  g.K = c.n;
+  const CUtensorMap& ab = PAIR ? c.tm_a_a : c.tm_a_b;
+  if (mode == kNsBf16) {
+    g.aux = c.a;
+    g.aux_bstride = (long long)c.n * c.ld_a;
+    g.aux_ld = c.ld_a;
+    e = launch<256, false, false, kEpiSquareBf16, PAIR>(c.tm_a_a, c.tm_a_a, ab, g, num_sms, stream);
+  } else {
+    e = launch<256, false, false, kEpiSquare, PAIR>(c.tm_a_a, c.tm_a_a, ab, g, num_sms, stream);
+  }
+  if (e != cudaSuccess) return e;
+
+  // X' = bf16((X/s)*a + (b*(A X) + c*(A2 X))/s)   or   bf16((X/s)*a + (Bm X)/s)
+  g.out = c.x[nxt];
+  g.out_bstride = (long long)c.n * c.ld_x;
+  g.out_ld = c.ld_x;
+  g.aux = c.x[cur];
+  g.aux_bstride = (long long)c.n * c.ld_x;
+  g.aux_ld = c.ld_x;
+  g.norms = norms;
+  g.M = c.n;
+  g.N = c.m;
+  g.K = c.n;
+  g.tile_list = nullptr;
+  if (fused) {
+    g.p = fused->p;
+    g.p_bf16 = fused->p_bf16;
+    g.apply = fused->apply;
+  }
+  if (mode == kNsBf16) {
+    g.tiles_n = (c.m + 255) / 256;
+    g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
+    g.num_tiles = g.tiles_per_matrix * c.batch;
+    return launch<256, false, true, kEpiPolySingle, PAIR>(c.tm_a2_a, c.tm_a2_a, c.tm_x_mn[cur], g,
+                                                          num_sms, stream);
+  }
+  g.tiles_n = (c.m + 127) / 128;
+  g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
+  g.num_tiles = g.tiles_per_matrix * c.batch;
+  return launch<128, true, true, kEpiPolyDual, PAIR>(c.tm_a_a, c.tm_a2_a, c.tm_x_mn[cur], g,
+                                                     num_sms, stream);
+}
+
+}  // namespace
+
 int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
-                 cudaStream_t stream, std::string* err) {
+                 cudaStream_t stream, std::string* err, const NsFused* fused) {
   int cur = 0;
+  NsGemmArgs base{};
+  base.status = status;
+  base.coef_a = kNsA;
+  base.coef_b = kNsB;
+  base.coef_c = kNsC;
+  const bool pair = use_pairs(c);
   for (int it = 0; it < steps; ++it) {
     const int nxt = cur ^ 1;
     const float* norms = it == 0 ? c.norms : nullptr;
-    NsGemmArgs g{};
-    g.status = status;
-    g.coef_a = kNsA;
-    g.coef_b = kNsB;
-    g.coef_c = kNsC;
-
-    // A = bf16((X X^T) / s / s)
-    g.out = c.a;
-    g.out_bstride = (long long)c.n * c.ld_a;
-    g.out_ld = c.ld_a;
-    g.aux = nullptr;
-    g.norms = norms;
-    g.M = c.n;
-    g.N = c.n;
-    g.K = c.m;
-    g.tile_list = c.sym_tiles;
-    g.tiles_per_matrix = c.n_sym_tiles;
-    g.tiles_n = 0;
-    g.num_tiles = c.n_sym_tiles * c.batch;
-    cudaError_t e = launch<256, false, false, kEpiGram>(c.tm_x_a[cur], c.tm_x_a[cur],
-                                                        c.tm_x_b[cur], g, num_sms, stream);
-
-    // A2 = bf16(A A)   or   Bm = bf16(b*A + c*bf16(A A))
-    g.out = c.a2;
-    g.norms = nullptr;
-    g.K = c.n;
-    if (e == cudaSuccess) {
-      if (mode == kNsBf16) {
-        g.aux = c.a;
-        g.aux_bstride = (long long)c.n * c.ld_a;
-        g.aux_ld = c.ld_a;
-        e = launch<256, false, false, kEpiSquareBf16>(c.tm_a_a, c.tm_a_a, c.tm_a_b, g, num_sms,
-                                                      stream);
-      } else {
-        e = launch<256, false, false, kEpiSquare>(c.tm_a_a, c.tm_a_a, c.tm_a_b, g, num_sms,
-                                                  stream);
-      }
-    }
-
-    // X' = bf16((X/s)*a + (b*(A X) + c*(A2 X))/s)   or   bf16((X/s)*a + (Bm X)/s)
-    g.out = c.x[nxt];
-    g.out_bstride = (long long)c.n * c.ld_x;
-    g.out_ld = c.ld_x;
-    g.aux = c.x[cur];
-    g.aux_bstride = (long long)c.n * c.ld_x;
-    g.aux_ld = c.ld_x;
-    g.norms = norms;
-    g.M = c.n;
-    g.N = c.m;
-    g.K = c.n;
-    g.tile_list = nullptr;
-    if (e == cudaSuccess) {
-      if (mode == kNsBf16) {
-        g.tiles_n = (c.m + 255) / 256;
-        g.tiles_per_matrix = ((c.n + kBM - 1) / kBM) * g.tiles_n;
-        g.num_tiles = g.tiles_per_matrix * c.batch;
-        e = launch<256, false, true, kEpiPolySingle>(c.tm_a2_a, c.tm_a2_a, c.tm_x_mn[cur], g,
-                                                     num_sms, stream);
-      } else {
-        g.tiles_n = (c.m + 127) / 128;
-        g.tiles_per_matrix = ((c.n + kBM - 1) / kBM) * g.tiles_n;
-        g.num_tiles = g.tiles_per_matrix * c.batch;
-        e = launch<128, true, true, kEpiPolyDual>(c.tm_a_a, c.tm_a2_a, c.tm_x_mn[cur], g,
-                                                  num_sms, stream);
-      }
-    }
+    const NsFused* f = (fused && it == steps - 1) ? fused : nullptr;
+    cudaError_t e = pair ? run_iteration<true>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
+                         : run_iteration<false>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
     if (e != cudaSuccess) {
       if (err) *err = std::string("Newton-Schulz GEMM launch: ") + cudaGetErrorString(e);
       return -1;

@@ -25,8 +25,10 @@ struct NsClass {
   __nv_bfloat16* a = nullptr;                // bf16(X X^T)          (batch x n x ld_a)
   __nv_bfloat16* a2 = nullptr;               // bf16(A A) or bf16(B) (batch x n x ld_a)
   float* norms = nullptr;                    // device, batch entries
-  int2* sym_tiles = nullptr;                 // device (tm, tn) list for n x n outputs
+  int2* sym_tiles = nullptr;                 // device (tm, tn) list, 128-row tiles
   int n_sym_tiles = 0;
+  int2* sym_tiles2 = nullptr;                // device (tm, tn) list, 256-row tiles (CTA pairs)
+  int n_sym_tiles2 = 0;
   CUtensorMap tm_x_a[2], tm_x_b[2], tm_x_mn[2];
   CUtensorMap tm_a_a, tm_a_b, tm_a2_a;
   bool owns_memory = false;
@@ -48,11 +50,22 @@ void ns_class_free(NsClass& c);
 std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
                           std::vector<int2>* tiles_out);
 
+// The Muon update fused into the last iteration: p -= lr*scale * O for every
+// matrix of the class (apply[b] gives batch item b's parameter).
+struct NsApply;
+struct NsFused {
+  float* p = nullptr;
+  __nv_bfloat16* p_bf16 = nullptr;
+  const NsApply* apply = nullptr;
+};
+
 // Runs `steps` iterations on every matrix of the class; X starts in x[0] with
 // c.norms holding the first-iteration divisors. Returns the index of the X
-// buffer that holds the result, or -1 on a launch error (message in err).
+// buffer that holds the result, or -1 on a launch error (message in err). With
+// `fused` (and steps >= 1) the last iteration updates the parameters instead
+// of storing X.
 int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
-                 cudaStream_t stream, std::string* err);
+                 cudaStream_t stream, std::string* err, const NsFused* fused = nullptr);
 
 // Opt-in shared memory for every GEMM instantiation (once per device).
 std::string ns_gemm_setup();

@@ -15,11 +15,16 @@
 // s is the per-matrix Frobenius norm in the first iteration (lib.rs:109-110)
 // and 1 afterwards. All operand values are exactly bf16, so the tensor-core
 // products are exact and only the fp32 summation order differs from the CPU.
+// In the last iteration the Poly epilogue can apply the Muon update
+// p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
-// Roles (192 threads): warp 0 issues TMA loads, warp 1 owns TMEM and one lane
-// issues tcgen05.mma, warps 2-5 drain TMEM and run the fused epilogue. Every
-// mbarrier wait is time-bounded; on timeout the kernel records a status,
-// drains what it issued, frees TMEM and returns.
+// Roles (192 threads per CTA): warp 0 issues TMA loads, warp 1 owns TMEM and
+// one lane issues tcgen05.mma, warps 2-5 drain TMEM and run the epilogue.
+// PAIR=true runs one 256-row tile on a CTA pair (cluster of 2, cta_group::2):
+// each CTA loads its 128 rows of A and half of B's columns, the leader CTA
+// issues the MMAs for both and commits to both CTAs' barriers. No TMA load
+// uses cluster multicast. Every mbarrier wait is time-bounded; on timeout the
+// kernel records a status, drains what it issued, frees TMEM and returns.
 #pragma once
 #include <cuda.h>
 
@@ -35,8 +40,15 @@ enum NsEpilogue : int {
   kEpiPolySingle = 4,
 };
 
-constexpr int kBM = 128;  // tile rows (TMEM lanes)
+constexpr int kBM = 128;  // rows per CTA (TMEM lanes)
 constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of bf16
+
+// Where the last iteration writes when it is fused with the Muon update.
+struct NsApply {
+  long long off;   // element offset of the parameter in the fp32 arena
+  float lr_scale;  // lr * sqrt(rows / cols), f32 as the reference computes it
+  int transposed;  // parameter is m x n and X holds its transpose
+};
 
 struct NsGemmArgs {
   __nv_bfloat16* out;        // output matrices (bf16)
@@ -53,20 +65,30 @@ struct NsGemmArgs {
   const int2* tile_list;     // symmetric schedule: (tm, tn) per tile, or nullptr
   int* status;               // device status word (0 = ok)
   float coef_a, coef_b, coef_c;
+  float* p;                  // Poly, last iteration: fp32 params to update (or nullptr)
+  __nv_bfloat16* p_bf16;     // optional bf16 copy of the updated params
+  const NsApply* apply;      // per batch item, used when p is set
 };
 
-template <int BN, bool DUAL, bool B_MN>
+template <int BN, bool DUAL, bool B_MN, bool PAIR>
 struct NsGemmShape {
-  static constexpr int kABytes = kBM * kBK * 2;             // 16 KB
-  static constexpr int kBBytes = BN * kBK * 2;              // BN*128 B
+  static constexpr int kCtas = PAIR ? 2 : 1;
+  static constexpr int kTileM = kBM * kCtas;        // output rows per tile
+  static constexpr int kBNc = BN / kCtas;           // B columns loaded by one CTA
+  static constexpr int kABytes = kBM * kBK * 2;     // 16 KB per A operand
+  static constexpr int kBBytes = kBNc * kBK * 2;
   static constexpr int kStageBytes = kABytes * (DUAL ? 2 : 1) + kBBytes;
-  static constexpr int kStages = (196608 / kStageBytes) < 8 ? (196608 / kStageBytes) : 8;
-  static constexpr int kAccCols = BN * (DUAL ? 2 : 1);      // per accumulator buffer
-  static constexpr int kTmemCols = 2 * kAccCols;            // double-buffered
+  static constexpr int kStages = (204800 / kStageBytes) < 8 ? (204800 / kStageBytes) : 8;
+  static constexpr int kAccCols = BN * (DUAL ? 2 : 1);  // per accumulator buffer
+  static constexpr int kTmemCols = 2 * kAccCols;        // double-buffered
   static constexpr int kBarBytes = 1024;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // +align slack
+  static constexpr int kEpiStride = 40;  // bf16 per staging row: 80 B keeps v4 reads conflict-free
+  static constexpr int kEpiBytes = 4 * 32 * kEpiStride * 2;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiBytes + 1024;
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(!B_MN || kBNc % 64 == 0, "MN-major B is loaded in 64-column boxes");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -74,28 +96,67 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI>
+__device__ __forceinline__ float bf16r(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// 32 consecutive bf16 -> float (16-byte aligned source).
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + q * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      v[q * 8 + e * 2] = f.x;
+      v[q * 8 + e * 2 + 1] = f.y;
+    }
+  }
+}
+
+// 32 floats -> 32 consecutive bf16 (16-byte aligned destination).
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(dst + q * 8) = u;
+  }
+}
+
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
-  using S = NsGemmShape<BN, DUAL, B_MN>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
   constexpr int STAGES = S::kStages;
+  constexpr bool kSym = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
-  uint64_t* full = bars;                  // [STAGES] TMA -> MMA
-  uint64_t* empty = bars + STAGES;        // [STAGES] MMA -> TMA
-  uint64_t* tfull = bars + 2 * STAGES;    // [2] MMA -> epilogue
+  uint64_t* full = bars;                     // [STAGES] TMA -> MMA
+  uint64_t* empty = bars + STAGES;           // [STAGES] MMA -> TMA
+  uint64_t* tfull = bars + 2 * STAGES;       // [2] MMA -> epilogue
   uint64_t* tempty = bars + 2 * STAGES + 2;  // [2] epilogue -> MMA
   uint64_t* drain = bars + 2 * STAGES + 4;   // abort path: MMA completion
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 6);
+  __nv_bfloat16* epi_stage =
+      reinterpret_cast<__nv_bfloat16*>(smem + STAGES * S::kStageBytes + S::kBarBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int group = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int groups = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -104,7 +165,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 128 * S::kCtas);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -116,11 +177,17 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tm_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, S::kTmemCols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, S::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, S::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // peer barriers initialised, both TMEM allocations done
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (args.K + kBK - 1) / kBK;
@@ -145,26 +212,41 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, last_parity = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      for (int tile = group; ok && tile < args.num_tiles; tile += groups) {
         int b, tm, tn;
         decode(tile, b, tm, tn);
+        const int row0 = tm * S::kTileM + (int)rank * kBM;
+        const int col0 = tn * BN + (int)rank * S::kBNc;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
           uint8_t* st = tiles + stage * S::kStageBytes;
-          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          if (leader) mbar_arrive_expect_tx(&full[stage], S::kStageBytes * S::kCtas);
           const int k0 = kb * kBK;
-          tma_load_3d(st, &tm_a1, &full[stage], k0, tm * kBM, b);
-          if (DUAL) tma_load_3d(st + S::kABytes, &tm_a2, &full[stage], k0, tm * kBM, b);
           uint8_t* sb = st + S::kABytes * (DUAL ? 2 : 1);
-          if (B_MN) {
+          if (PAIR) {
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_3d_pair(st, &tm_a1, fb, k0, row0, b);
+            if (DUAL) tma_load_3d_pair(st + S::kABytes, &tm_a2, fb, k0, row0, b);
+            if (B_MN) {
 #pragma unroll
-            for (int g = 0; g < BN / 64; ++g)
-              tma_load_3d(sb + g * (kBK * 128), &tm_b, &full[stage], tn * BN + g * 64, k0, b);
+              for (int g = 0; g < S::kBNc / 64; ++g)
+                tma_load_3d_pair(sb + g * (kBK * 128), &tm_b, fb, col0 + g * 64, k0, b);
+            } else {
+              tma_load_3d_pair(sb, &tm_b, fb, k0, col0, b);
+            }
           } else {
-            tma_load_3d(sb, &tm_b, &full[stage], k0, tn * BN, b);
+            tma_load_3d(st, &tm_a1, &full[stage], k0, row0, b);
+            if (DUAL) tma_load_3d(st + S::kABytes, &tm_a2, &full[stage], k0, row0, b);
+            if (B_MN) {
+#pragma unroll
+              for (int g = 0; g < S::kBNc / 64; ++g)
+                tma_load_3d(sb + g * (kBK * 128), &tm_b, &full[stage], col0 + g * 64, k0, b);
+            } else {
+              tma_load_3d(sb, &tm_b, &full[stage], k0, col0, b);
+            }
           }
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -174,29 +256,33 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      // Every load this thread issued must land before the CTA may exit.
-      for (int s = 0; s < STAGES; ++s)
-        if (issued_mask & (1u << s)) {
-          const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&full[s], (last_parity >> s) & 1u)) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-              *abort_flag = 1;
-              break;
+      // Every load must land before the CTA may exit. The leader's full
+      // barriers count both CTAs' bytes; the peer is held by the final
+      // cluster barrier until the leader has seen them complete.
+      if (leader) {
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s)) {
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(&full[s], (last_parity >> s) & 1u)) {
+              if (global_timer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                break;
+              }
             }
           }
-        }
+      }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, false, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_bf16(S::kTileM, BN, false, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      for (int tile = group; ok && tile < args.num_tiles; tile += groups) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d1 = tmem_base + acc * S::kAccCols;
@@ -216,21 +302,33 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t db = B_MN ? umma_desc_sw128(bb + kk * 2048, kBK * 128, 1024)
                                      : umma_desc_sw128(bb + kk * 32, 16, 1024);
             const uint32_t accum = (kb | kk) != 0;
-            tc_mma_bf16(d1, da1, db, idesc, accum);
+            if (PAIR)
+              tc_mma_bf16_pair(d1, da1, db, idesc, accum);
+            else
+              tc_mma_bf16(d1, da1, db, idesc, accum);
             if (DUAL) {
               const uint64_t da2 = umma_desc_sw128(a2 + kk * 32, 16, 1024);
-              tc_mma_bf16(d2, da2, db, idesc, accum);
+              if (PAIR)
+                tc_mma_bf16_pair(d2, da2, db, idesc, accum);
+              else
+                tc_mma_bf16(d2, da2, db, idesc, accum);
             }
           }
           issued_any = true;
-          tc_commit(&empty[stage]);
+          if (PAIR)
+            tc_commit_pair_mc(&empty[stage], 0x3);
+          else
+            tc_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if (PAIR)
+          tc_commit_pair_mc(&tfull[acc], 0x3);
+        else
+          tc_commit(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -238,8 +336,11 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (*abort_flag && issued_any) {
         // Let every MMA this thread issued finish before TMEM is freed.
-        tc_commit(drain);
-        uint64_t t0 = global_timer_ns();
+        if (PAIR)
+          tc_commit_pair_mc(drain, 0x1);
+        else
+          tc_commit(drain);
+        const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(drain, 0)) {
           if (global_timer_ns() - t0 > kWaitLimitNs) break;
         }
@@ -248,9 +349,11 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
+    __nv_bfloat16* stg = epi_stage + (warp - 2) * 32 * S::kEpiStride;
+    const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+    for (int tile = group; tile < args.num_tiles; tile += groups) {
       int b, tm, tn;
       decode(tile, b, tm, tn);
       // tcgen05.ld is warp-collective: the warp proceeds only if every lane saw
@@ -258,70 +361,81 @@ __global__ void __launch_bounds__(192, 1)
       const bool ready = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int r = tm * kBM + sub * 32 + lane;
+      const int rw = tm * S::kTileM + (int)rank * kBM + sub * 32;  // first row of this warp
+      const int r = rw + lane;
       const uint32_t tbase = tmem_base + acc * S::kAccCols + ((uint32_t)(sub * 32) << 16);
       const float s = args.norms ? args.norms[b] : 1.0f;
       __nv_bfloat16* out = args.out + (long long)b * args.out_bstride;
       const __nv_bfloat16* aux = args.aux ? args.aux + (long long)b * args.aux_bstride : nullptr;
       const bool row_ok = r < args.M;
+      const bool rows_full = rw + 32 <= args.M;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int c0 = tn * BN + ch * 32;
+        if (c0 >= args.N) break;  // whole chunk beyond the matrix (uniform over the warp)
+        const bool cols_full = c0 + 32 <= args.N;
         float v[32];
         tmem_ld_32x32b_x32(tbase + ch * 32, v);
         float w[32];
         if (DUAL) tmem_ld_32x32b_x32(tbase + BN + ch * 32, w);
         tmem_ld_wait();
-        if (EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16) {
-          // Symmetric output: this tile owns the elements with col >= row and
-          // writes each one twice, at (r, c) and at (c, r).
-          float a_in[32];
+        if (kSym) {
+          // This tile owns the symmetric entries with col >= row and writes each
+          // at (r, c) and, through a transposing smem stage, at (c, r).
+          if (c0 + 31 < rw) continue;  // block entirely below the diagonal
           if (EPI == kEpiSquareBf16) {
+            float a_in[32];
+            const __nv_bfloat16* arow = aux + (long long)r * args.aux_ld + c0;
+            if (row_ok && cols_full) {
+              load_bf16x32(arow, a_in);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int c = c0 + j;
-              a_in[j] = (row_ok && c < args.N)
-                            ? __bfloat162float(aux[(long long)r * args.aux_ld + c])
-                            : 0.0f;
+              for (int j = 0; j < 32; ++j)
+                a_in[j] = (row_ok && c0 + j < args.N) ? __bfloat162float(arow[j]) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = __fadd_rn(__fmul_rn(a_in[j], args.coef_b), __fmul_rn(bf16r(v[j]), args.coef_c));
+          } else if (EPI == kEpiGram) {
+            if (s != 1.0f) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fdiv_rn(__fdiv_rn(v[j], s), s);
             }
           }
+          // direct write (r, c), c >= r
+          __nv_bfloat16* orow = out + (long long)r * args.out_ld + c0;
+          if (rows_full && cols_full && c0 >= rw + 31) {
+            store_bf16x32(orow, v);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = v[j];
-            if (EPI == kEpiGram) x = __fdiv_rn(__fdiv_rn(x, s), s);
-            if (EPI == kEpiSquareBf16) {
-              const float sq = __bfloat162float(__float2bfloat16_rn(x));
-              x = __fadd_rn(__fmul_rn(a_in[j], args.coef_b), __fmul_rn(sq, args.coef_c));
-            }
-            v[j] = x;
+            for (int j = 0; j < 32; ++j)
+              if (row_ok && c0 + j < args.N && c0 + j >= r) orow[j] = __float2bfloat16_rn(v[j]);
           }
+          // mirror write (c, r), c > r: stage transposed, then lane L writes row c0 + L
+          if (c0 + 31 > rw) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int c = c0 + j;
-            if (row_ok && c < args.N && c >= r) {
-              const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
-              out[(long long)r * args.out_ld + c] = h;
-              out[(long long)c * args.out_ld + r] = h;
+            for (int j = 0; j < 32; ++j) stg[j * S::kEpiStride + lane] = __float2bfloat16_rn(v[j]);
+            __syncwarp();
+            const int c = c0 + lane;
+            const __nv_bfloat16* srow = stg + lane * S::kEpiStride;
+            __nv_bfloat16* mrow = out + (long long)c * args.out_ld + rw;
+            if (rows_full && cols_full && c0 >= rw + 32) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(mrow + q * 8) =
+                    *reinterpret_cast<const uint4*>(srow + q * 8);
+            } else if (c < args.N) {
+              for (int i = 0; i < 32; ++i)
+                if (c > rw + i && rw + i < args.M) mrow[i] = srow[i];
             }
+            __syncwarp();
           }
         } else {
-          // Poly: X' = bf16((X/s)*a + (b*D1 + c*D2)/s)  or  bf16((X/s)*a + D/s).
+          // Poly: o = bf16((X/s)*a + (b*D1 + c*D2)/s)  or  bf16((X/s)*a + D/s)
           const __nv_bfloat16* xrow = aux + (long long)r * args.aux_ld + c0;
-          __nv_bfloat16* orow = out + (long long)r * args.out_ld + c0;
-          const bool full_chunk = row_ok && (c0 + 32 <= args.N);
           float xv[32];
-          if (full_chunk) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 u = *reinterpret_cast<const uint4*>(xrow + q * 8);
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
-                xv[q * 8 + e * 2] = f.x;
-                xv[q * 8 + e * 2 + 1] = f.y;
-              }
-            }
+          if (row_ok && cols_full) {
+            load_bf16x32(xrow, xv);
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -329,30 +443,72 @@ __global__ void __launch_bounds__(192, 1)
           }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float bx = DUAL ? __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j]))
-                            : v[j];
-            const float x0 = __fdiv_rn(xv[j], s);
-            v[j] = __fadd_rn(__fmul_rn(x0, args.coef_a), __fdiv_rn(bx, s));
+            const float bx =
+                DUAL ? __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j])) : v[j];
+            const float x0 = s != 1.0f ? __fdiv_rn(xv[j], s) : xv[j];
+            const float bs = s != 1.0f ? __fdiv_rn(bx, s) : bx;
+            v[j] = bf16r(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
           }
-          if (full_chunk) {
+          if (!args.p) {
+            __nv_bfloat16* orow = out + (long long)r * args.out_ld + c0;
+            if (row_ok && cols_full) {
+              store_bf16x32(orow, v);
+            } else if (row_ok) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 u;
-              u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-              u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-              u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-              u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-              *reinterpret_cast<uint4*>(orow + q * 8) = u;
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
             }
-          } else if (row_ok) {
+          } else {
+            // Fused Muon update: p -= (lr*scale) * O, O in the parameter's orientation.
+            const NsApply ap = args.apply[b];
+            const float ls = ap.lr_scale;
+            if (!ap.transposed) {
+              const long long base = ap.off + (long long)r * args.N + c0;
+              float* prow = args.p + base;
+              if (row_ok && cols_full && (base & 3) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
+                for (int q = 0; q < 8; ++q) {
+                  float4 pv = *reinterpret_cast<float4*>(prow + q * 4);
+                  pv.x = __fsub_rn(pv.x, __fmul_rn(ls, v[q * 4 + 0]));
+                  pv.y = __fsub_rn(pv.y, __fmul_rn(ls, v[q * 4 + 1]));
+                  pv.z = __fsub_rn(pv.z, __fmul_rn(ls, v[q * 4 + 2]));
+                  pv.w = __fsub_rn(pv.w, __fmul_rn(ls, v[q * 4 + 3]));
+                  *reinterpret_cast<float4*>(prow + q * 4) = pv;
+                  if (args.p_bf16) {
+                    uint2 u;
+                    u.x = pack_bf16x2(pv.x, pv.y);
+                    u.y = pack_bf16x2(pv.z, pv.w);
+                    *reinterpret_cast<uint2*>(args.p_bf16 + base + q * 4) = u;
+                  }
+                }
+              } else if (row_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (c0 + j < args.N) {
+                    const float pn = __fsub_rn(prow[j], __fmul_rn(ls, v[j]));
+                    prow[j] = pn;
+                    if (args.p_bf16) args.p_bf16[base + j] = __float2bfloat16_rn(pn);
+                  }
+              }
+            } else if (row_ok) {
+              // Parameter element (c, r): consecutive lanes touch consecutive r.
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (c0 + j < args.N) {
+                  const long long idx = ap.off + (long long)(c0 + j) * args.M + r;
+                  const float pn = __fsub_rn(args.p[idx], __fmul_rn(ls, v[j]));
+                  args.p[idx] = pn;
+                  if (args.p_bf16) args.p_bf16[idx] = __float2bfloat16_rn(pn);
+                }
+            }
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (PAIR && !leader)
+        mbar_arrive_cluster(tempty_leader0 + acc * 8);
+      else
+        mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -362,10 +518,14 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // peer loads landed, remote arrivals done, MMAs retired
   if (*abort_flag && threadIdx.x == 0) atomicExch(args.status, kDevWaitTimeout);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::kTmemCols);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, S::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, S::kTmemCols);
   }
 }
 
