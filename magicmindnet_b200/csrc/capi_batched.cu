@@ -605,6 +605,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
     m.grad_divisor = divisor;
     m.fresh_state = h->cfg.fresh_state;
     m.apply_divides_norm = h->cfg.muon.ns_steps == 0;
+    m.vec_ok = 1;  // arena bases come from cudaMalloc; offsets are 64-element aligned
     launch_muon_momentum(m, h->ctx.num_sms, s);
     launch_muon_norms(m, s);
     MMN_CUDA_TRY(cudaGetLastError());

@@ -30,6 +30,105 @@ __device__ __forceinline__ void adamw_elem(float& p, float& m, float& v, float g
   p = __fmul_rn(p, c.decay);
 }
 
+// Division of a grad by the loss scale or the accumulation divisor. A power
+// of two divides exactly as a multiplication by its reciprocal (both round
+// the same real value), which saves the division sequence.
+struct GradScaler {
+  float d;
+  float inv;
+  int mode;  // 0: identity, 1: multiply by inv, 2: IEEE division by d
+};
+
+__device__ __forceinline__ GradScaler make_scaler(float d) {
+  GradScaler s;
+  s.d = d;
+  s.inv = 1.0f;
+  const uint32_t u = __float_as_uint(d);
+  const uint32_t ex = (u >> 23) & 0xFFu;
+  if (d == 1.0f) {
+    s.mode = 0;
+  } else if ((u & 0x007FFFFFu) == 0 && ex > 1 && ex < 253) {
+    s.mode = 1;
+    s.inv = __uint_as_float((254u - ex) << 23 | (u & 0x80000000u));  // exactly 1/d
+  } else {
+    s.mode = 2;
+  }
+  return s;
+}
+
+__device__ __forceinline__ float apply_scaler(float g, const GradScaler& s) {
+  return s.mode == 0 ? g : (s.mode == 1 ? __fmul_rn(g, s.inv) : __fdiv_rn(g, s.d));
+}
+
+struct AdamwVec {
+  float4 p, m, v;
+  float g[4];
+};
+
+template <bool BF16G, bool FRESH>
+__device__ __forceinline__ void adamw_load(const AdamwArgs& a, long long i, AdamwVec& q) {
+  q.p = __ldcs(reinterpret_cast<const float4*>(a.p) + i);
+  if (BF16G) {
+    const uint2 raw = __ldcs(reinterpret_cast<const uint2*>(a.g_bf16) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+    q.g[0] = f0.x;
+    q.g[1] = f0.y;
+    q.g[2] = f1.x;
+    q.g[3] = f1.y;
+  } else {
+    const float4 g4 = __ldcs(reinterpret_cast<const float4*>(a.g) + i);
+    q.g[0] = g4.x;
+    q.g[1] = g4.y;
+    q.g[2] = g4.z;
+    q.g[3] = g4.w;
+  }
+  if (FRESH) {
+    q.m = make_float4(0.f, 0.f, 0.f, 0.f);
+    q.v = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    q.m = __ldcs(reinterpret_cast<const float4*>(a.m) + i);
+    q.v = __ldcs(reinterpret_cast<const float4*>(a.v) + i);
+  }
+}
+
+template <bool FRESH, bool SHADOW>
+__device__ __forceinline__ void adamw_store(const AdamwArgs& a, long long i, const AdamwVec& q) {
+  __stcs(reinterpret_cast<float4*>(a.p) + i, q.p);
+  if (!FRESH) {
+    __stcs(reinterpret_cast<float4*>(a.m) + i, q.m);
+    __stcs(reinterpret_cast<float4*>(a.v) + i, q.v);
+  }
+  if (SHADOW) {
+    uint2 out;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(q.p.x, q.p.y);
+    __nv_bfloat162 h1 = __floats2bfloat162_rn(q.p.z, q.p.w);
+    out.x = *reinterpret_cast<uint32_t*>(&h0);
+    out.y = *reinterpret_cast<uint32_t*>(&h1);
+    __stcs(reinterpret_cast<uint2*>(a.p_bf16) + i, out);
+  }
+}
+
+__device__ __forceinline__ void adamw_math(const AdamwArgs& a, long long i, long long base,
+                                           const GradScaler& sc_scale, const GradScaler& sc_div,
+                                           const AdamwConst& c, AdamwVec& q) {
+  int t_off = a.seg0.t_offset;
+  if (a.segs) {
+    int s = __ldg(&a.chunk_seg[i / kAdamwChunk4]);
+    while (i >= a.segs[s].end4) ++s;
+    t_off = a.segs[s].t_offset;
+  }
+  long long t = base + t_off;
+  if (t > a.t_sat) t = a.t_sat;
+  const float2 bc = __ldg(&a.bc_table[t]);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) q.g[e] = apply_scaler(apply_scaler(q.g[e], sc_scale), sc_div);
+  adamw_elem(q.p.x, q.m.x, q.v.x, q.g[0], bc.x, bc.y, c);
+  adamw_elem(q.p.y, q.m.y, q.v.y, q.g[1], bc.x, bc.y, c);
+  adamw_elem(q.p.z, q.m.z, q.v.z, q.g[2], bc.x, bc.y, c);
+  adamw_elem(q.p.w, q.m.w, q.v.w, q.g[3], bc.x, bc.y, c);
+}
+
 template <bool BF16G, bool FRESH, bool SHADOW>
 __global__ void __launch_bounds__(256) adamw_kernel(const AdamwArgs a) {
   if (a.skip && *a.skip) return;
@@ -43,62 +142,23 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamwArgs a) {
   c.one_m_b2 = __fsub_rn(1.0f, a.b2);
   c.eps = a.eps;
   c.decay = __fsub_rn(1.0f, __fmul_rn(a.lr, a.wd));
+  const GradScaler sc_scale = make_scaler(scale);
+  const GradScaler sc_div = make_scaler(a.grad_divisor);
+  // Two float4 groups per thread and iteration: all eight loads are issued
+  // before any arithmetic, doubling the bytes each thread keeps in flight.
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = a.begin4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.end4;
-       i += stride) {
-    int t_off = a.seg0.t_offset;
-    if (a.segs) {
-      int s = __ldg(&a.chunk_seg[i / kAdamwChunk4]);
-      while (i >= a.segs[s].end4) ++s;
-      t_off = a.segs[s].t_offset;
-    }
-    long long t = base + t_off;
-    if (t > a.t_sat) t = a.t_sat;
-    const float2 bc = __ldg(&a.bc_table[t]);
-
-    float4 p4 = __ldcs(reinterpret_cast<const float4*>(a.p) + i);
-    float g[4];
-    if (BF16G) {
-      const uint2 raw = __ldcs(reinterpret_cast<const uint2*>(a.g_bf16) + i);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-      g[0] = f0.x;
-      g[1] = f0.y;
-      g[2] = f1.x;
-      g[3] = f1.y;
-    } else {
-      const float4 g4 = __ldcs(reinterpret_cast<const float4*>(a.g) + i);
-      g[0] = g4.x;
-      g[1] = g4.y;
-      g[2] = g4.z;
-      g[3] = g4.w;
-    }
-    float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (!FRESH) {
-      m4 = __ldcs(reinterpret_cast<const float4*>(a.m) + i);
-      v4 = __ldcs(reinterpret_cast<const float4*>(a.v) + i);
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (scale != 1.0f) g[e] = __fdiv_rn(g[e], scale);
-      if (a.grad_divisor != 1.0f) g[e] = __fdiv_rn(g[e], a.grad_divisor);
-    }
-    adamw_elem(p4.x, m4.x, v4.x, g[0], bc.x, bc.y, c);
-    adamw_elem(p4.y, m4.y, v4.y, g[1], bc.x, bc.y, c);
-    adamw_elem(p4.z, m4.z, v4.z, g[2], bc.x, bc.y, c);
-    adamw_elem(p4.w, m4.w, v4.w, g[3], bc.x, bc.y, c);
-    __stcs(reinterpret_cast<float4*>(a.p) + i, p4);
-    if (!FRESH) {
-      __stcs(reinterpret_cast<float4*>(a.m) + i, m4);
-      __stcs(reinterpret_cast<float4*>(a.v) + i, v4);
-    }
-    if (SHADOW) {
-      uint2 out;
-      __nv_bfloat162 h0 = __floats2bfloat162_rn(p4.x, p4.y);
-      __nv_bfloat162 h1 = __floats2bfloat162_rn(p4.z, p4.w);
-      out.x = *reinterpret_cast<uint32_t*>(&h0);
-      out.y = *reinterpret_cast<uint32_t*>(&h1);
-      __stcs(reinterpret_cast<uint2*>(a.p_bf16) + i, out);
+  for (long long i0 = a.begin4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < a.end4;
+       i0 += 2 * stride) {
+    const long long i1 = i0 + stride;
+    const bool has1 = i1 < a.end4;
+    AdamwVec q0, q1;
+    adamw_load<BF16G, FRESH>(a, i0, q0);
+    if (has1) adamw_load<BF16G, FRESH>(a, i1, q1);
+    adamw_math(a, i0, base, sc_scale, sc_div, c, q0);
+    adamw_store<FRESH, SHADOW>(a, i0, q0);
+    if (has1) {
+      adamw_math(a, i1, base, sc_scale, sc_div, c, q1);
+      adamw_store<FRESH, SHADOW>(a, i1, q1);
     }
   }
 }
@@ -133,6 +193,96 @@ __device__ __forceinline__ float block_sum_256(float x, float* red) {
   return r;
 }
 
+// Momentum arithmetic of lib.rs:154-165 for one element; returns bf16(u).
+__device__ __forceinline__ float momentum_elem(float g, float& vel, float mu, float one_m,
+                                               int nesterov) {
+  const float v1 = __fadd_rn(__fmul_rn(mu, vel), __fmul_rn(one_m, g));
+  vel = v1;
+  const float u = nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
+  return __bfloat162float(__float2bfloat16_rn(u));
+}
+
+// 128-bit variant of one 64 x 64 momentum tile: thread t covers 4 consecutive
+// columns; a transposed X is written through `tile` in groups of 4 rows.
+template <bool BF16G, bool FRESH>
+__device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const MuonMat& mm, int r0,
+                                                   int c0, __nv_bfloat16* X, int ld,
+                                                   float (*tile)[kTile + 1], float scale,
+                                                   float mu, float one_m) {
+  const int cq = (threadIdx.x & 15) * 4;
+  const int rs = threadIdx.x >> 4;
+  float ss = 0.0f;
+  for (int rr = rs; rr < kTile; rr += 16) {
+    const int r = r0 + rr, c = c0 + cq;
+    float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (r < mm.rows && c < mm.cols) {
+      const long long idx = mm.off + (long long)r * mm.cols + c;
+      float g[4];
+      if (BF16G) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(a.g_bf16 + idx);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+        g[0] = f0.x;
+        g[1] = f0.y;
+        g[2] = f1.x;
+        g[3] = f1.y;
+      } else {
+        const float4 g4 = __ldcs(reinterpret_cast<const float4*>(a.g + idx));
+        g[0] = g4.x;
+        g[1] = g4.y;
+        g[2] = g4.z;
+        g[3] = g4.w;
+      }
+      float4 v4 = FRESH ? make_float4(0.f, 0.f, 0.f, 0.f)
+                        : __ldcs(reinterpret_cast<const float4*>(a.vel + idx));
+      float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (scale != 1.0f) g[e] = __fdiv_rn(g[e], scale);
+        if (a.grad_divisor != 1.0f) g[e] = __fdiv_rn(g[e], a.grad_divisor);
+        y[e] = momentum_elem(g[e], vv[e], mu, one_m, a.nesterov);
+      }
+      __stcs(reinterpret_cast<float4*>(a.vel + idx), make_float4(vv[0], vv[1], vv[2], vv[3]));
+      if (!mm.transposed) {
+        uint2 o;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(y[2], y[3]);
+        o.x = *reinterpret_cast<uint32_t*>(&h0);
+        o.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(X + (long long)r * ld + c) = o;
+      }
+    }
+    if (mm.transposed) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[rr][cq + e] = y[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(y[e], y[e]));
+  }
+  if (mm.transposed) {
+    __syncthreads();
+    // X row c = c0 + cl holds u[r0 .. r0+63][c]; thread writes 4 consecutive r.
+    const int rq = (threadIdx.x & 15) * 4;
+    for (int cl = rs; cl < kTile; cl += 16) {
+      const int c = c0 + cl, r = r0 + rq;
+      if (c < mm.cols && r < mm.rows) {
+        __nv_bfloat16* dst = X + (long long)c * ld + r;
+        if (r + 3 < mm.rows) {
+          uint2 o;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(tile[rq][cl], tile[rq + 1][cl]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(tile[rq + 2][cl], tile[rq + 3][cl]);
+          o.x = *reinterpret_cast<uint32_t*>(&h0);
+          o.y = *reinterpret_cast<uint32_t*>(&h1);
+          *reinterpret_cast<uint2*>(dst) = o;
+        } else {
+          for (int e = 0; e < 4 && r + e < mm.rows; ++e) dst[e] = __float2bfloat16_rn(tile[rq + e][cl]);
+        }
+      }
+    }
+  }
+  return ss;
+}
+
 // Muon momentum (lib.rs:154-165) + the bf16 cast and orientation of
 // newton_schulz5 (lib.rs:101-107) + per-tile sums of squares of the bf16
 // values (lib.rs:109), all in one pass over g and vel.
@@ -153,6 +303,13 @@ __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
     const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
     const MuonClassPtr cp = a.cls[mm.xcls];
     __nv_bfloat16* X = cp.x + (long long)mm.xbatch * cp.bstride;
+    if (a.vec_ok && (mm.cols & 3) == 0 && (mm.off & 3) == 0) {
+      const float ssv =
+          momentum_tile_vec<BF16G, FRESH>(a, mm, r0, c0, X, cp.ld, tile, scale, mu, one_m);
+      const float totv = block_sum_256(ssv, red);
+      if (threadIdx.x == 0) a.partials[t] = totv;
+      continue;
+    }
     float ss = 0.0f;
     for (int rr = ty; rr < kTile; rr += 4) {
       const int r = r0 + rr, c = c0 + tx;

@@ -80,6 +80,8 @@ struct MuonArgs {
   float grad_divisor;
   int fresh_state;      // velocity read as zero
   int apply_divides_norm;  // zero Newton-Schulz steps: O = bf16(u) / norm (lib.rs:110)
+  int vec_ok;              // p / g / vel bases are 16-byte aligned: matrices with
+                           // cols % 4 == 0 and off % 4 == 0 take the 128-bit path
 };
 
 void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream);

@@ -80,7 +80,10 @@ struct NsGemmShape {
   static constexpr int kStageBytes = kABytes * (DUAL ? 2 : 1) + kBBytes;
   static constexpr int kStages = (204800 / kStageBytes) < 8 ? (204800 / kStageBytes) : 8;
   static constexpr int kAccCols = BN * (DUAL ? 2 : 1);  // per accumulator buffer
-  static constexpr int kTmemCols = 2 * kAccCols;        // double-buffered
+  // two accumulator buffers when they fit in TMEM's 512 columns, else one
+  // (the MMA of the next tile then waits for the epilogue)
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccBufs * kAccCols;
   static constexpr int kBarBytes = 1024;
   static constexpr int kEpiStride = 40;  // bf16 per staging row: 80 B keeps v4 reads conflict-free
   static constexpr int kEpiBytes = 4 * 32 * kEpiStride * 2;
@@ -125,6 +128,84 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
     u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
     u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
     *reinterpret_cast<uint4*>(dst + q * 8) = u;
+  }
+}
+
+// Last step of every Poly epilogue for one row r and 32 columns c0..c0+31,
+// given bx = (b*A X + c*A2 X) or Bm X: o = bf16((X/s)*a + bx/s), stored as X'
+// or, in the last iteration, applied as p -= lr*scale*o in the parameter's
+// orientation (lib.rs:169-174). bx is overwritten with o.
+__device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r, int c0,
+                                            bool row_ok, bool cols_full, float s,
+                                            float (&v)[32]) {
+  const __nv_bfloat16* xrow = args.aux + (long long)b * args.aux_bstride +
+                              (long long)r * args.aux_ld + c0;
+  float xv[32];
+  if (row_ok && cols_full) {
+    load_bf16x32(xrow, xv);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      xv[j] = (row_ok && c0 + j < args.N) ? __bfloat162float(xrow[j]) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float x0 = s != 1.0f ? __fdiv_rn(xv[j], s) : xv[j];
+    const float bs = s != 1.0f ? __fdiv_rn(v[j], s) : v[j];
+    v[j] = bf16r(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
+  }
+  if (!args.p) {
+    __nv_bfloat16* orow =
+        args.out + (long long)b * args.out_bstride + (long long)r * args.out_ld + c0;
+    if (row_ok && cols_full) {
+      store_bf16x32(orow, v);
+    } else if (row_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
+    }
+    return;
+  }
+  const NsApply ap = args.apply[b];
+  const float ls = ap.lr_scale;
+  if (!ap.transposed) {
+    const long long base = ap.off + (long long)r * args.N + c0;
+    float* prow = args.p + base;
+    if (row_ok && cols_full && (base & 3) == 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 pv = *reinterpret_cast<float4*>(prow + q * 4);
+        pv.x = __fsub_rn(pv.x, __fmul_rn(ls, v[q * 4 + 0]));
+        pv.y = __fsub_rn(pv.y, __fmul_rn(ls, v[q * 4 + 1]));
+        pv.z = __fsub_rn(pv.z, __fmul_rn(ls, v[q * 4 + 2]));
+        pv.w = __fsub_rn(pv.w, __fmul_rn(ls, v[q * 4 + 3]));
+        *reinterpret_cast<float4*>(prow + q * 4) = pv;
+        if (args.p_bf16) {
+          uint2 u;
+          u.x = pack_bf16x2(pv.x, pv.y);
+          u.y = pack_bf16x2(pv.z, pv.w);
+          *reinterpret_cast<uint2*>(args.p_bf16 + base + q * 4) = u;
+        }
+      }
+    } else if (row_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < args.N) {
+          const float pn = __fsub_rn(prow[j], __fmul_rn(ls, v[j]));
+          prow[j] = pn;
+          if (args.p_bf16) args.p_bf16[base + j] = __float2bfloat16_rn(pn);
+        }
+    }
+  } else if (row_ok) {
+    // Parameter element (c, r): consecutive lanes touch consecutive r.
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j < args.N) {
+        const long long idx = ap.off + (long long)(c0 + j) * args.M + r;
+        const float pn = __fsub_rn(args.p[idx], __fmul_rn(ls, v[j]));
+        args.p[idx] = pn;
+        if (args.p_bf16) args.p_bf16[idx] = __float2bfloat16_rn(pn);
+      }
   }
 }
 
@@ -329,7 +410,7 @@ __global__ void __launch_bounds__(192, 1)
           tc_commit_pair_mc(&tfull[acc], 0x3);
         else
           tc_commit(&tfull[acc]);
-        if (++acc == 2) {
+        if (++acc == S::kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -431,77 +512,11 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
           }
         } else {
-          // Poly: o = bf16((X/s)*a + (b*D1 + c*D2)/s)  or  bf16((X/s)*a + D/s)
-          const __nv_bfloat16* xrow = aux + (long long)r * args.aux_ld + c0;
-          float xv[32];
-          if (row_ok && cols_full) {
-            load_bf16x32(xrow, xv);
-          } else {
+          // Poly: bx = b*D1 + c*D2 (reference mode) or D (bf16 mode)
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              xv[j] = (row_ok && c0 + j < args.N) ? __bfloat162float(xrow[j]) : 0.0f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float bx =
-                DUAL ? __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j])) : v[j];
-            const float x0 = s != 1.0f ? __fdiv_rn(xv[j], s) : xv[j];
-            const float bs = s != 1.0f ? __fdiv_rn(bx, s) : bx;
-            v[j] = bf16r(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
-          }
-          if (!args.p) {
-            __nv_bfloat16* orow = out + (long long)r * args.out_ld + c0;
-            if (row_ok && cols_full) {
-              store_bf16x32(orow, v);
-            } else if (row_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
-            }
-          } else {
-            // Fused Muon update: p -= (lr*scale) * O, O in the parameter's orientation.
-            const NsApply ap = args.apply[b];
-            const float ls = ap.lr_scale;
-            if (!ap.transposed) {
-              const long long base = ap.off + (long long)r * args.N + c0;
-              float* prow = args.p + base;
-              if (row_ok && cols_full && (base & 3) == 0) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  float4 pv = *reinterpret_cast<float4*>(prow + q * 4);
-                  pv.x = __fsub_rn(pv.x, __fmul_rn(ls, v[q * 4 + 0]));
-                  pv.y = __fsub_rn(pv.y, __fmul_rn(ls, v[q * 4 + 1]));
-                  pv.z = __fsub_rn(pv.z, __fmul_rn(ls, v[q * 4 + 2]));
-                  pv.w = __fsub_rn(pv.w, __fmul_rn(ls, v[q * 4 + 3]));
-                  *reinterpret_cast<float4*>(prow + q * 4) = pv;
-                  if (args.p_bf16) {
-                    uint2 u;
-                    u.x = pack_bf16x2(pv.x, pv.y);
-                    u.y = pack_bf16x2(pv.z, pv.w);
-                    *reinterpret_cast<uint2*>(args.p_bf16 + base + q * 4) = u;
-                  }
-                }
-              } else if (row_ok) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (c0 + j < args.N) {
-                    const float pn = __fsub_rn(prow[j], __fmul_rn(ls, v[j]));
-                    prow[j] = pn;
-                    if (args.p_bf16) args.p_bf16[base + j] = __float2bfloat16_rn(pn);
-                  }
-              }
-            } else if (row_ok) {
-              // Parameter element (c, r): consecutive lanes touch consecutive r.
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (c0 + j < args.N) {
-                  const long long idx = ap.off + (long long)(c0 + j) * args.M + r;
-                  const float pn = __fsub_rn(args.p[idx], __fmul_rn(ls, v[j]));
-                  args.p[idx] = pn;
-                  if (args.p_bf16) args.p_bf16[idx] = __float2bfloat16_rn(pn);
-                }
-            }
-          }
+          for (int j = 0; j < 32; ++j)
+            if (DUAL) v[j] = __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j]));
+          poly_finish(args, b, r, c0, row_ok, cols_full, s, v);
         }
       }
       tc_fence_before();
@@ -509,7 +524,7 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive_cluster(tempty_leader0 + acc * 8);
       else
         mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
+      if (++acc == S::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
       }
