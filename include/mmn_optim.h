@@ -296,6 +296,16 @@ typedef struct {
 } mmn_optim_gather_layout;
 int mmn_optim_get_gather_layout(mmn_optim_t *h, mmn_optim_gather_layout *out);
 
+/* The layout and sharding plan mmn_optim_finalize uses, computed on the host
+ * alone (no device): n tensors, `shapes` holds their dims back to back
+ * (ndims[i] each), `routes` as for mmn_optim_add_param. Fills, per tensor, the
+ * Muon owner rank (-1 for AdamW tensors, which are split by arena range) and
+ * the element offset in its arena, plus both arenas' per-rank region sizes.
+ * Every rank computes the same plan from the same inputs. */
+int mmn_optim_plan(const int64_t *shapes, const int *ndims, const int *routes, int n,
+                   int use_hybrid, int ns_steps, int world_size, int *owner, int64_t *offset,
+                   int64_t *adamw_region, int64_t *muon_region);
+
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
 

@@ -30,7 +30,110 @@ struct DevGuard {
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
+struct ShardTensor {
+  int64_t numel = 0;
+  int route = MMN_ROUTE_ADAMW;  // resolved route
+  int rows = 0, cols = 0;       // Muon matrices
+};
+
+struct ShardPlan {
+  std::vector<int64_t> off;  // element offset in the tensor's arena
+  std::vector<int> t_offset; // AdamW: 1-based position among the step's AdamW calls
+  std::vector<int> owner;    // Muon: owner rank; AdamW: -1
+  int n_adamw = 0;
+  int64_t a_used4 = 0, a_region4 = 0;  // AdamW arena: used float4s, float4s per rank
+  int64_t m_region = 0;                // Muon arena: elements per rank region
+};
+
+// Layout of both arenas and the ownership of every tensor.
+//  - AdamW tensors keep the registration (= reference call) order, each padded
+//    to 4 elements; the arena is cut into world_size equal 256-byte-aligned
+//    ranges, rank r stepping range r.
+//  - Muon matrices go whole to a rank by longest-processing-time bin packing
+//    on their Newton-Schulz flops (ties to the lower rank), and are stored
+//    grouped by owner so each rank's matrices form one equal-size region.
+// The plan depends only on the shapes, routes, world size and step count, so
+// every rank computes the same plan without communicating.
+void make_shard_plan(const std::vector<ShardTensor>& ts, int world, int ns_steps, ShardPlan* p) {
+  const size_t n = ts.size();
+  p->off.assign(n, 0);
+  p->t_offset.assign(n, 0);
+  p->owner.assign(n, -1);
+  int64_t off4 = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (ts[i].route != MMN_ROUTE_ADAMW) continue;
+    p->off[i] = off4 * 4;
+    p->t_offset[i] = ++p->n_adamw;
+    off4 += (ts[i].numel + 3) / 4;
+  }
+  p->a_used4 = off4;
+  p->a_region4 = align_up((off4 + world - 1) / world, 16);
+  std::vector<size_t> muon;
+  for (size_t i = 0; i < n; ++i)
+    if (ts[i].route == MMN_ROUTE_MUON) muon.push_back(i);
+  auto cost = [&](size_t i) {
+    const double a = std::min(ts[i].rows, ts[i].cols), b = std::max(ts[i].rows, ts[i].cols);
+    return (double)std::max(ns_steps, 1) * (4.0 * a * a * b + 2.0 * a * a * a) + 64.0 * a * b;
+  };
+  std::vector<size_t> order = muon;
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return cost(a) > cost(b); });
+  std::vector<double> load((size_t)world, 0.0);
+  for (size_t i : order) {
+    int best = 0;
+    for (int r = 1; r < world; ++r)
+      if (load[r] < load[best]) best = r;
+    p->owner[i] = best;
+    load[best] += cost(i);
+  }
+  std::vector<int64_t> used((size_t)world, 0);
+  for (size_t i : muon) {
+    p->off[i] = used[p->owner[i]];
+    used[p->owner[i]] = align_up(used[p->owner[i]] + ts[i].numel, 64);
+  }
+  p->m_region = 64;
+  for (int r = 0; r < world; ++r) p->m_region = std::max(p->m_region, used[r]);
+  for (size_t i : muon) p->off[i] += (int64_t)p->owner[i] * p->m_region;
+}
+
 }  // namespace
+
+extern "C" int mmn_optim_plan(const int64_t* shapes, const int* ndims, const int* routes, int n,
+                              int use_hybrid, int ns_steps, int world_size, int* owner,
+                              int64_t* offset, int64_t* adamw_region, int64_t* muon_region) {
+  if (n < 0 || (n > 0 && (!shapes || !ndims || !routes)) || world_size < 1 || ns_steps < 0)
+    return fail(MMN_E_INVALID, "bad plan arguments");
+  std::vector<ShardTensor> ts((size_t)n);
+  const int64_t* sp = shapes;
+  for (int i = 0; i < n; ++i) {
+    int rc;
+    const int64_t numel = shape_numel(sp, ndims[i], &rc);
+    if (rc != MMN_OK) return rc;
+    int route = routes[i];
+    if (route != MMN_ROUTE_AUTO && route != MMN_ROUTE_MUON && route != MMN_ROUTE_ADAMW)
+      return fail(MMN_E_INVALID, "unknown route");
+    if (!use_hybrid)
+      route = MMN_ROUTE_ADAMW;
+    else if (route == MMN_ROUTE_AUTO)
+      route = mmn_hybrid_classify_param(sp, ndims[i]);
+    ts[i].numel = numel;
+    ts[i].route = route;
+    if (route == MMN_ROUTE_MUON) {
+      if (ndims[i] != 2 || sp[0] < 1 || sp[1] < 1) return fail(MMN_E_SHAPE, "Muon tensors must be 2-D");
+      ts[i].rows = (int)sp[0];
+      ts[i].cols = (int)sp[1];
+    }
+    sp += ndims[i];
+  }
+  ShardPlan p;
+  make_shard_plan(ts, world_size, ns_steps, &p);
+  for (int i = 0; i < n; ++i) {
+    if (owner) owner[i] = p.owner[i];
+    if (offset) offset[i] = p.off[i];
+  }
+  if (adamw_region) *adamw_region = p.a_region4 * 4;
+  if (muon_region) *muon_region = p.m_region;
+  return MMN_OK;
+}
 
 struct mmn_optim {
   Ctx ctx;
@@ -209,65 +312,51 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   const int steps = h->cfg.muon.ns_steps;
   int rc;
 
-  // ---- AdamW arena: registration order, each tensor padded to 4 elements.
-  std::vector<AdamwSeg> segs;
-  int64_t off4 = 0;
-  for (auto& s : h->slots) {
-    h->n_params += s.numel;
-    if (s.route != MMN_ROUTE_ADAMW) continue;
-    h->n_adamw_params += s.numel;
-    AdamwSeg sg{};
-    sg.start4 = off4;
-    sg.end4 = off4 + (s.numel + 3) / 4;
-    sg.t_offset = ++h->n_adamw;
-    s.off = off4 * 4;
-    s.t_offset = sg.t_offset;
-    off4 = sg.end4;
-    if (sg.end4 > sg.start4) segs.push_back(sg);
+  // ---- Layout and sharding plan (host only; shared with mmn_optim_plan).
+  std::vector<ShardTensor> pts(h->slots.size());
+  for (size_t i = 0; i < h->slots.size(); ++i) {
+    pts[i].numel = h->slots[i].numel;
+    pts[i].route = h->slots[i].route;
+    pts[i].rows = h->slots[i].rows;
+    pts[i].cols = h->slots[i].cols;
   }
-  h->a_used4 = off4;
-  h->a_region4 = (off4 + W - 1) / W;
-  h->a_region4 = align_up(h->a_region4, 16);  // 256-byte aligned regions
+  ShardPlan plan;
+  make_shard_plan(pts, W, steps, &plan);
+  std::vector<int> muon_idx;
+  for (size_t i = 0; i < h->slots.size(); ++i) {
+    auto& s = h->slots[i];
+    s.off = plan.off[i];
+    s.t_offset = plan.t_offset[i];
+    s.owner = plan.owner[i];
+    h->n_params += s.numel;
+    if (s.route == MMN_ROUTE_MUON) {
+      h->n_muon_params += s.numel;
+      muon_idx.push_back((int)i);
+    } else {
+      h->n_adamw_params += s.numel;
+    }
+  }
+  h->n_adamw = plan.n_adamw;
+  h->a_used4 = plan.a_used4;
+  h->a_region4 = plan.a_region4;
   h->a_total4 = h->a_region4 * W;
+  h->m_region = plan.m_region;
+  h->m_total = h->m_region * W;
+  std::vector<AdamwSeg> segs;
+  for (auto& s : h->slots) {
+    if (s.route != MMN_ROUTE_ADAMW || s.numel == 0) continue;
+    AdamwSeg sg{};
+    sg.start4 = s.off / 4;
+    sg.end4 = sg.start4 + (s.numel + 3) / 4;
+    sg.t_offset = s.t_offset;
+    segs.push_back(sg);
+  }
   std::vector<int> chunk_seg((size_t)((h->a_used4 + kAdamwChunk4 - 1) / kAdamwChunk4) + 1, 0);
   for (size_t k = 0, c = 0; c < chunk_seg.size(); ++c) {
     const int64_t first = (int64_t)c * kAdamwChunk4;
     while (k + 1 < segs.size() && segs[k].end4 <= first) ++k;
     chunk_seg[c] = (int)k;
   }
-
-  // ---- Muon: LPT assignment of whole matrices to ranks by Newton-Schulz flops.
-  std::vector<int> muon_idx;
-  for (int i = 0; i < (int)h->slots.size(); ++i)
-    if (h->slots[i].route == MMN_ROUTE_MUON) muon_idx.push_back(i);
-  auto cost = [&](const mmn_optim::Slot& s) {
-    const double n = std::min(s.rows, s.cols), m = std::max(s.rows, s.cols);
-    return (double)std::max(steps, 1) * (4.0 * n * n * m + 2.0 * n * n * n) + 64.0 * n * m;
-  };
-  std::vector<int> order = muon_idx;
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
-    return cost(h->slots[a]) > cost(h->slots[b]);
-  });
-  std::vector<double> load(W, 0.0);
-  for (int i : order) {
-    int best = 0;
-    for (int r = 1; r < W; ++r)
-      if (load[r] < load[best]) best = r;
-    h->slots[i].owner = best;
-    load[best] += cost(h->slots[i]);
-  }
-  // Muon arena grouped by owner rank (registration order inside a rank).
-  std::vector<int64_t> region_used(W, 0);
-  for (int i : muon_idx) {
-    auto& s = h->slots[i];
-    h->n_muon_params += s.numel;
-    s.off = region_used[s.owner];
-    region_used[s.owner] = align_up(region_used[s.owner] + s.numel, 64);
-  }
-  h->m_region = 64;
-  for (int r = 0; r < W; ++r) h->m_region = std::max(h->m_region, region_used[r]);
-  for (int i : muon_idx) h->slots[i].off += (int64_t)h->slots[i].owner * h->m_region;
-  h->m_total = h->m_region * W;
 
   // ---- Newton-Schulz shape classes over the matrices this rank owns.
   std::vector<std::pair<int, int>> cls_shapes;
@@ -620,7 +709,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
       f.apply = h->d_apply + h->cls_base[k];
       std::string err;
       if (ns_class_run(h->classes[k], h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status,
-                       h->ctx.num_sms, s, &err, fuse ? &f : nullptr) < 0)
+                       h->ctx.num_sms, s, &err, fuse ? &f : nullptr, skip) < 0)
         return fail(MMN_E_CUDA, err);
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));

@@ -290,10 +290,11 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
 }  // namespace
 
 int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
-                 cudaStream_t stream, std::string* err, const NsFused* fused) {
+                 cudaStream_t stream, std::string* err, const NsFused* fused, const int* skip) {
   int cur = 0;
   NsGemmArgs base{};
   base.status = status;
+  base.skip = skip;
   base.coef_a = kNsA;
   base.coef_b = kNsB;
   base.coef_c = kNsC;

@@ -65,7 +65,8 @@ struct NsFused {
 // `fused` (and steps >= 1) the last iteration updates the parameters instead
 // of storing X.
 int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
-                 cudaStream_t stream, std::string* err, const NsFused* fused = nullptr);
+                 cudaStream_t stream, std::string* err, const NsFused* fused = nullptr,
+                 const int* skip = nullptr);
 
 // Opt-in shared memory for every GEMM instantiation (once per device).
 std::string ns_gemm_setup();

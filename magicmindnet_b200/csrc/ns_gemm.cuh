@@ -68,6 +68,7 @@ struct NsGemmArgs {
   float* p;                  // Poly, last iteration: fp32 params to update (or nullptr)
   __nv_bfloat16* p_bf16;     // optional bf16 copy of the updated params
   const NsApply* apply;      // per batch item, used when p is set
+  const int* skip;           // device non-finite flag: when set the launch does nothing
 };
 
 template <int BN, bool DUAL, bool B_MN, bool PAIR>
@@ -232,6 +233,9 @@ __global__ void __launch_bounds__(192, 1)
   __nv_bfloat16* epi_stage =
       reinterpret_cast<__nv_bfloat16*>(smem + STAGES * S::kStageBytes + S::kBarBytes);
 
+  // A skipped step (non-finite grads) leaves every buffer untouched. Both CTAs
+  // of a pair read the same flag, so both leave before any cluster barrier.
+  if (args.skip && *args.skip) return;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;

@@ -239,6 +239,30 @@ class OptimizerStep:
             pass
 
 
+def shard_plan(params, world_size: int, use_hybrid: bool = True, ns_steps: int = 5) -> dict:
+    """The arena layout and rank ownership OptimizerStep uses (host only, no GPU).
+    params: (id, shape[, route]) as for OptimizerStep. Returns per-tensor
+    `owner` (Muon owner rank, -1 for AdamW) and `offset` (element offset in its
+    arena), and the per-rank region sizes of the AdamW and Muon arenas."""
+    shapes, ndims, routes = [], [], []
+    for p in params:
+        s = tuple(int(d) for d in p[1])
+        shapes.extend(s)
+        ndims.append(len(s))
+        routes.append(ROUTES[p[2] if len(p) > 2 else "auto"])
+    n = len(ndims)
+    sh = (ctypes.c_int64 * max(len(shapes), 1))(*shapes)
+    nd = (ctypes.c_int * max(n, 1))(*ndims)
+    rt = (ctypes.c_int * max(n, 1))(*routes)
+    owner = (ctypes.c_int * max(n, 1))()
+    off = (ctypes.c_int64 * max(n, 1))()
+    ar, mr = ctypes.c_int64(), ctypes.c_int64()
+    N.check(N.lib().mmn_optim_plan(sh, nd, rt, n, int(use_hybrid), ns_steps, world_size, owner, off,
+                                   ctypes.byref(ar), ctypes.byref(mr)))
+    return {"owner": list(owner)[:n], "offset": list(off)[:n], "adamw_region": ar.value,
+            "muon_region": mr.value}
+
+
 def chatbot_param_order(vocab_size: int, n_layer: int, d_model: int, ffn_mult: int = 4,
                         pos_embed_len: int | None = None):
     """(name, shape) of every trained tensor of the reference Chatbot in the order

@@ -268,3 +268,44 @@ class GradAccumulator:
 
     def __len__(self):
         return len(self.grads)
+
+
+class LossScaleState:
+    """Dynamic loss scaling for bf16 grads. NEW BEHAVIOUR with no reference
+    counterpart (the reference trains in fp32 without loss scaling), defined
+    here so the GPU path has something to be checked against:
+      * grads arrive multiplied by `scale` and rounded to bf16; the step uses
+        g = float(g_bf16) / scale (exact for a power-of-two scale);
+      * if any grad of any tensor is non-finite the whole step is skipped:
+        params, m, v, velocity and the AdamW call counter stay as they are,
+        the scale halves and the clean-step count resets;
+      * after `growth_interval` consecutive clean steps the scale doubles."""
+
+    def __init__(self, scale=65536.0, growth_interval=2000):
+        self.scale = np.float32(scale)
+        self.growth_interval = growth_interval
+        self.good = 0
+        self.skipped = 0
+
+    def unscale(self, g_bf16_values):
+        return (np.asarray(g_bf16_values, np.float32) / self.scale).astype(np.float32)
+
+    def check(self, grads) -> bool:
+        """True when the step may run (all grads finite)."""
+        return all(np.isfinite(g).all() for g in grads)
+
+    def update(self, stepped: bool) -> None:
+        if not stepped:
+            self.scale = np.float32(self.scale * np.float32(0.5))
+            self.good = 0
+            self.skipped += 1
+            return
+        self.good += 1
+        if self.good >= self.growth_interval:
+            self.scale = np.float32(self.scale * np.float32(2.0))
+            self.good = 0
+
+
+def bf16_bits(x) -> np.ndarray:
+    """uint16 bit patterns of bf16(x) (round to nearest even)."""
+    return (bf16_round(x).view(np.uint32) >> 16).astype(np.uint16)
