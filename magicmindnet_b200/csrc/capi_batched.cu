@@ -187,7 +187,9 @@ struct mmn_optim {
   int* d_good = nullptr;
   int* d_skipped = nullptr;
 
-  cudaStream_t side = nullptr;
+  cudaStream_t work = nullptr;  // the step's own stream, event-joined to ctx.stream
+  cudaStream_t side = nullptr;  // AdamW runs here, overlapping the Newton-Schulz GEMMs
+  cudaEvent_t in_ev = nullptr, out_ev = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
   cudaGraphExec_t graph = nullptr;
   float graph_divisor = 0.0f;
@@ -266,6 +268,9 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   if (h->fork) cudaEventDestroy(h->fork);
   if (h->join) cudaEventDestroy(h->join);
   if (h->side) cudaStreamDestroy(h->side);
+  if (h->work) cudaStreamDestroy(h->work);
+  if (h->in_ev) cudaEventDestroy(h->in_ev);
+  if (h->out_ev) cudaEventDestroy(h->out_ev);
   h->bc.release();
   h->ctx.release();
   delete h;
@@ -464,6 +469,9 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaMemcpy(h->d_scale, &scale, sizeof(float), cudaMemcpyHostToDevice));
 
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->work, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->in_ev, cudaEventDisableTiming));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->out_ev, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming));
   for (auto& e : h->ev) MMN_CUDA_TRY(cudaEventCreate(&e));
@@ -615,7 +623,7 @@ extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
 // Enqueues the whole step on the handle's stream (AdamW forked onto a side
 // stream so it overlaps the Newton-Schulz GEMMs).
 static int enqueue_step(mmn_optim_t* h, float divisor) {
-  cudaStream_t s = h->ctx.stream;
+  cudaStream_t s = h->work;
   const bool tm = h->timing;
   const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
   const int R = h->cfg.rank;
@@ -743,28 +751,40 @@ extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
   if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
   if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
   DevGuard g(h->ctx.device);
-  if (!h->cfg.use_graph || h->timing) return enqueue_step(h, grad_divisor);
-  if (h->graph && h->graph_divisor != grad_divisor) {
-    cudaGraphExecDestroy(h->graph);
-    h->graph = nullptr;
-  }
-  if (!h->graph) {
-    cudaGraph_t graph = nullptr;
-    MMN_CUDA_TRY(cudaStreamBeginCapture(h->ctx.stream, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(h, grad_divisor);
-    cudaError_t e = cudaStreamEndCapture(h->ctx.stream, &graph);
-    if (rc != MMN_OK) {
-      if (graph) cudaGraphDestroy(graph);
-      return rc;
+  // The step runs on the handle's own work stream, ordered after everything
+  // already queued on the caller's stream and before anything queued there
+  // later. Capture therefore never touches the caller's stream (which may be
+  // the legacy default stream, where capture is not allowed).
+  MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
+  int rc = MMN_OK;
+  if (!h->cfg.use_graph || h->timing) {
+    rc = enqueue_step(h, grad_divisor);
+  } else {
+    if (h->graph && h->graph_divisor != grad_divisor) {
+      cudaGraphExecDestroy(h->graph);
+      h->graph = nullptr;
     }
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
-    e = cudaGraphInstantiate(&h->graph, graph, 0);
-    cudaGraphDestroy(graph);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-    h->graph_divisor = grad_divisor;
+    if (!h->graph) {
+      cudaGraph_t graph = nullptr;
+      MMN_CUDA_TRY(cudaStreamBeginCapture(h->work, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_step(h, grad_divisor);
+      cudaError_t e = cudaStreamEndCapture(h->work, &graph);
+      if (rc != MMN_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+      }
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+      e = cudaGraphInstantiate(&h->graph, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+      h->graph_divisor = grad_divisor;
+    }
+    MMN_CUDA_TRY(cudaGraphLaunch(h->graph, h->work));
   }
-  MMN_CUDA_TRY(cudaGraphLaunch(h->graph, h->ctx.stream));
-  return MMN_OK;
+  MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->work));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->ctx.stream, h->out_ev, 0));
+  return rc;
 }
 
 extern "C" int mmn_optim_sync(mmn_optim_t* h) {

@@ -48,13 +48,21 @@ def _mem_ptr(x, writable: bool):
     return ctypes.c_void_p(x.ctypes.data), N.MEM_HOST, tuple(x.shape)
 
 
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream
+
+
 def _stream_of(device: int, stream):
-    if stream is not None:
-        return ctypes.c_void_p(int(stream))
-    torch = _torch()
-    if torch is not None and torch.cuda.is_available():
-        return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
-    return ctypes.c_void_p(0)
+    """The cudaStream_t to hand to the library. torch reports its default
+    stream as 0, which the C ABI would read as "no stream given" (the library
+    would then use a stream of its own, unordered with torch's work), so the
+    default stream is passed explicitly as cudaStreamLegacy."""
+    if stream is None:
+        torch = _torch()
+        if torch is None or not torch.cuda.is_available():
+            return ctypes.c_void_p(0)
+        stream = torch.cuda.current_stream(device).cuda_stream
+    stream = int(stream)
+    return ctypes.c_void_p(stream if stream != 0 else _CUDA_STREAM_LEGACY)
 
 
 def is_available() -> bool:
