@@ -32,6 +32,16 @@ sys.path.insert(0, ROOT)
 METRIC = "hybrid AdamW+Muon step params/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+# DRAM bytes (read + write) per algorithmic Newton-Schulz flop of the three GEMM
+# kernels of one reference-mode iteration, from the ncu capture of the 8 x
+# [2048, 8192] profiling case (profiles/ns_gemm_probe_full.md): 1101.2 MB per
+# 1.2370e12 flop. Traffic grows with the flops of a class, so the per-step
+# traffic of a workload is this ratio times its Newton-Schulz flops.
+NS_DRAM_BYTES_PER_FLOP = 1101.2e6 / 1.2370e12
+# DRAM bytes per element of the isolated AdamW kernel measured by ncu on the
+# 2^28 arena: read p, g, m, v and write p, m, v (profiles/adamw_arena.md).
+ADAMW_DRAM_BYTES_PER_PARAM = 28.0
+
 
 def peaks():
     try:
@@ -342,18 +352,27 @@ def run_ours(args, rank, world, local_rank):
                           "TFLOP/s": (ns_flops / (med["newton_schulz"] / 1e3) / 1e12)
                           if med["newton_schulz"] else None},
         "muon_momentum_ms": med["muon_momentum"], "muon_update_ms": med["muon_update"],
+        "note": "AdamW runs on a side stream concurrently with the Newton-Schulz GEMMs, so in "
+                "hybrid workloads its event time includes waiting for SMs; its kernel rate is "
+                "the adamw_arena workload's",
     }
     if n_muon and med["newton_schulz"] > 0:
         ach = ns_flops / (med["newton_schulz"] / 1e3) / 1e12
         peak = pk["bf16_tflops_sustained"] if args.workload.startswith("hybrid") else pk["bf16_tflops"]
         roof = {"bound": "tensor", "kernel": "ns_gemm (tcgen05, Gram + Square + Poly per iteration)",
                 "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                "peak_source": pk_kind, "traffic": None}
+                "peak_source": pk_kind,
+                "traffic": ns_flops * NS_DRAM_BYTES_PER_FLOP if args.ns_mode == "reference" else None,
+                "traffic_unit": "DRAM bytes per step of the NS kernels (ncu ratio of the "
+                                "8 x [2048,8192] capture, scaled by flops)",
+                "flops_per_step": ns_flops}
     else:
         ach = a_bytes_per * a_elems_rank / (med["adamw"] / 1e3) / 1e9
         roof = {"bound": "hbm", "kernel": "adamw_kernel", "achieved": ach, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "peak_source": pk_kind,
-                "traffic": None}
+                "traffic": ADAMW_DRAM_BYTES_PER_PARAM * a_elems_rank,
+                "traffic_unit": "DRAM bytes per launch (ncu: 28 B per param on the 2^28 arena)",
+                "algorithmic_bytes": a_bytes_per * a_elems_rank}
     launches_per_step = 5 + 15 * len({(min(s), max(s)) for _, s, r in model if r == "muon"})
     line = {
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
