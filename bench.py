@@ -254,7 +254,11 @@ def run_ours(args, rank, world, local_rank):
 
     gl = step.gather_layout()
     gathers = []
-    if world > 1:
+    fused = world > 1 and args.exchange == "fused"
+    if fused:
+        # the step's own kernels store this rank's parameters into every peer
+        step.connect_peers()
+    elif world > 1:
         import torch.distributed as dist
         from magicmindnet_b200.step import _view
 
@@ -267,6 +271,8 @@ def run_ours(args, rank, world, local_rank):
 
     def one_step():
         step.step(divisor)
+        if fused:
+            step.exchange_fence()
         if gathers:
             import torch.distributed as dist
 
@@ -383,6 +389,8 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": args.workload, "desc": spec["desc"], "params": n_total,
                    "adamw_params": n_adamw, "muon_params": n_muon, "ns_mode": args.ns_mode,
                    "parallelism": f"shard{world}" if world > 1 else "single",
+                   "exchange": ("fused NVLink stores + 1-element all-reduce fence" if fused else
+                                "NCCL all-gather of the parameter arenas") if world > 1 else None,
                    "l2": "inputs larger than L2 (no flush needed)"},
         "roofline": roof, "components": comp, "clocks": clk, "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
@@ -431,6 +439,9 @@ def main():
     ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="multi-GPU parameter exchange: stores fused into the step's kernels "
+                         "(NVLink, CUDA IPC) or an NCCL all-gather after the step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -306,6 +306,22 @@ int mmn_optim_plan(const int64_t *shapes, const int *ndims, const int *routes, i
                    int use_hybrid, int ns_steps, int world_size, int *owner, int64_t *offset,
                    int64_t *adamw_region, int64_t *muon_region);
 
+/* Parameter exchange fused into the step (world_size > 1), in place of a
+ * post-step all-gather. After mmn_optim_connect_peers the kernels that
+ * produce final parameter values (AdamW and the last Newton-Schulz iteration)
+ * also store each value into every peer's arena at the same offset, over
+ * NVLink through CUDA IPC mappings: fp32 params, or only the bf16 copies when
+ * bf16_param_shadow is on (the fp32 master then stays with its owner). Every
+ * rank must finish its step before any rank reads parameters or starts the
+ * next step: order the ranks after each mmn_optim_step (for example a
+ * one-element all-reduce on the same stream).
+ * mmn_optim_export_ipc writes this rank's MMN_IPC_BLOB_BYTES-byte blob;
+ * mmn_optim_connect_peers takes the world_size blobs back to back in rank
+ * order (exchanged by the caller, e.g. with an all-gather). */
+#define MMN_IPC_BLOB_BYTES 512
+int mmn_optim_export_ipc(mmn_optim_t *h, void *blob);
+int mmn_optim_connect_peers(mmn_optim_t *h, const void *blobs);
+
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
 

@@ -127,6 +127,8 @@ SIGNATURES = {
     "mmn_optim_slot_owner": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "mmn_optim_get_gather_layout": (_i, [_vp, ctypes.POINTER(GatherLayoutC)]),
     "mmn_optim_param_counts": (_i, [_vp, _i64p, _i64p, _i64p]),
+    "mmn_optim_export_ipc": (_i, [_vp, _vp]),
+    "mmn_optim_connect_peers": (_i, [_vp, ctypes.c_char_p]),
     "mmn_optim_plan": (_i, [_i64p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, _i, _i, _i,
                             ctypes.POINTER(_i), _i64p, _i64p, _i64p]),
     "mmn_optim_ns_flops": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),

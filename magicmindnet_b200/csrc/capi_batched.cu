@@ -175,6 +175,9 @@ struct mmn_optim {
   float* d_partials = nullptr;
   float* d_norms = nullptr;
   NsApply* d_apply = nullptr;   // per owned matrix, indexed like the norms
+  // fused exchange: IPC mappings of the other ranks' parameter arenas
+  PeerArenas peer_adamw, peer_muon;
+  std::vector<void*> peer_maps;
   std::vector<int> cls_base;    // first norm / apply slot of every class
   int total_tiles = 0;
   double ns_flops = 0.0;
@@ -262,6 +265,7 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   cudaStreamSynchronize(h->ctx.stream);
   if (h->graph) cudaGraphExecDestroy(h->graph);
   for (auto& c : h->classes) ns_class_free(c);
+  for (void* p : h->peer_maps) cudaIpcCloseMemHandle(p);
   for (void* p : h->allocs) cudaFree(p);
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
@@ -675,6 +679,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   a.wd = h->cfg.adamw.weight_decay;
   a.grad_divisor = divisor;
   a.fresh_state = h->cfg.fresh_state;
+  a.peers = h->peer_adamw;
   launch_adamw(a, h->ctx.num_sms, h->side);
   MMN_CUDA_TRY(cudaGetLastError());
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
@@ -715,6 +720,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
       f.p = h->mp;
       f.p_bf16 = h->mp16;
       f.apply = h->d_apply + h->cls_base[k];
+      f.peers = h->peer_muon;
       std::string err;
       if (ns_class_run(h->classes[k], h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status,
                        h->ctx.num_sms, s, &err, fuse ? &f : nullptr, skip) < 0)
@@ -822,6 +828,97 @@ extern "C" int mmn_optim_get_gather_layout(mmn_optim_t* h, mmn_optim_gather_layo
   out->muon_param = h->mp;
   out->muon_param_bf16 = h->mp16;
   out->muon_region = h->m_region;
+  return MMN_OK;
+}
+
+namespace {
+// What one rank publishes for the fused exchange.
+struct IpcBlob {
+  uint32_t magic;
+  int32_t rank, world;
+  int32_t shadow;
+  int64_t a_total4, m_total;
+  cudaIpcMemHandle_t ap, mp, ap16, mp16;
+};
+static_assert(sizeof(IpcBlob) <= MMN_IPC_BLOB_BYTES, "IPC blob size");
+constexpr uint32_t kIpcMagic = 0x4D4D4E31u;  // "MMN1"
+}  // namespace
+
+extern "C" int mmn_optim_export_ipc(mmn_optim_t* h, void* blob) {
+  if (!h || !blob) return fail(MMN_E_INVALID, "null argument");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  DevGuard g(h->ctx.device);
+  IpcBlob b;
+  memset(&b, 0, sizeof(b));
+  b.magic = kIpcMagic;
+  b.rank = h->cfg.rank;
+  b.world = h->cfg.world_size;
+  b.shadow = h->cfg.bf16_param_shadow;
+  b.a_total4 = h->a_total4;
+  b.m_total = h->m_total;
+  MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ap, h->ap));
+  MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.mp, h->mp));
+  if (b.shadow) {
+    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ap16, h->ap16));
+    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.mp16, h->mp16));
+  }
+  memset(blob, 0, MMN_IPC_BLOB_BYTES);
+  memcpy(blob, &b, sizeof(b));
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
+  if (!h || !blobs) return fail(MMN_E_INVALID, "null argument");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  const int W = h->cfg.world_size, R = h->cfg.rank;
+  if (W - 1 > kMaxPeers) return fail(MMN_E_UNSUPPORTED, "at most 8 ranks share the exchange");
+  if (h->cfg.muon.ns_steps < 1 && !h->mats.empty())
+    return fail(MMN_E_UNSUPPORTED, "the fused exchange rides on the last Newton-Schulz "
+                                   "iteration: ns_steps must be >= 1");
+  if (!h->peer_maps.empty()) return fail(MMN_E_STATE, "peers already connected");
+  DevGuard g(h->ctx.device);
+  const uint8_t* raw = static_cast<const uint8_t*>(blobs);
+  PeerArenas pa, pm;
+  std::vector<void*> maps;
+  auto open = [&](const cudaIpcMemHandle_t& hd, void** out) -> int {
+    cudaError_t e = cudaIpcOpenMemHandle(out, hd, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    maps.push_back(*out);
+    return MMN_OK;
+  };
+  int rc = MMN_OK;
+  for (int r = 0; r < W && rc == MMN_OK; ++r) {
+    IpcBlob b;
+    memcpy(&b, raw + (size_t)r * MMN_IPC_BLOB_BYTES, sizeof(b));
+    if (b.magic != kIpcMagic || b.rank != r || b.world != W ||
+        b.shadow != h->cfg.bf16_param_shadow || b.a_total4 != h->a_total4 ||
+        b.m_total != h->m_total) {
+      rc = fail(MMN_E_INVALID, "peer blob does not match this rank's layout");
+      break;
+    }
+    if (r == R) continue;
+    void *ap = nullptr, *mp = nullptr;
+    if (h->cfg.bf16_param_shadow) {
+      if ((rc = open(b.ap16, &ap)) != MMN_OK || (rc = open(b.mp16, &mp)) != MMN_OK) break;
+      pa.p16[pa.n++] = static_cast<__nv_bfloat16*>(ap);
+      pm.p16[pm.n++] = static_cast<__nv_bfloat16*>(mp);
+    } else {
+      if ((rc = open(b.ap, &ap)) != MMN_OK || (rc = open(b.mp, &mp)) != MMN_OK) break;
+      pa.p[pa.n++] = static_cast<float*>(ap);
+      pm.p[pm.n++] = static_cast<float*>(mp);
+    }
+  }
+  if (rc != MMN_OK) {
+    for (void* p : maps) cudaIpcCloseMemHandle(p);
+    return rc;
+  }
+  h->peer_maps = maps;
+  h->peer_adamw = pa;
+  h->peer_muon = pm;
+  if (h->graph) {  // the captured step must be re-captured with the peers
+    cudaGraphExecDestroy(h->graph);
+    h->graph = nullptr;
+  }
   return MMN_OK;
 }
 

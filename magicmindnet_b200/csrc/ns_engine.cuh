@@ -9,6 +9,8 @@
 #include <string>
 #include <vector>
 
+#include "elementwise.cuh"
+
 namespace mmn {
 
 enum NsMode : int {
@@ -57,6 +59,7 @@ struct NsFused {
   float* p = nullptr;
   __nv_bfloat16* p_bf16 = nullptr;
   const NsApply* apply = nullptr;
+  PeerArenas peers;  // the same values also go to these ranks' arenas
 };
 
 // Runs `steps` iterations on every matrix of the class; X starts in x[0] with

@@ -216,6 +216,34 @@ class OptimizerStep:
         N.check(N.lib().mmn_optim_get_gather_layout(self._h, ctypes.byref(g)))
         return {k: getattr(g, k) for k, _ in N.GatherLayoutC._fields_}
 
+    IPC_BLOB_BYTES = 512
+
+    def connect_peers(self, group=None) -> None:
+        """Fused exchange (world_size > 1): every rank publishes IPC handles of
+        its parameter arenas (one all-gather of 512-byte blobs over the given
+        torch.distributed group) and maps its peers', after which each step
+        also stores this rank's final values into every peer. Order the ranks
+        after each step (e.g. ``exchange_fence``) before reading parameters."""
+        import torch
+        import torch.distributed as dist
+
+        blob = (ctypes.c_uint8 * self.IPC_BLOB_BYTES)()
+        N.check(N.lib().mmn_optim_export_ipc(self._h, blob))
+        dev = torch.device(f"cuda:{self.device}")
+        mine = torch.tensor(bytearray(blob), dtype=torch.uint8, device=dev)
+        world = dist.get_world_size(group)
+        everyone = torch.empty(world * self.IPC_BLOB_BYTES, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(everyone, mine, group=group)
+        N.check(N.lib().mmn_optim_connect_peers(self._h, everyone.cpu().numpy().tobytes()))
+        self._fence = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def exchange_fence(self, group=None) -> None:
+        """Orders the ranks after a fused-exchange step: a one-element
+        all-reduce queued on the current stream after the step."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._fence, group=group)
+
     def param_counts(self):
         t, a, m = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
         N.check(N.lib().mmn_optim_param_counts(self._h, ctypes.byref(t), ctypes.byref(a),

@@ -30,7 +30,7 @@ def _fill(step, model, seed):
         step.grad(k).normal_(0, 1e-3, generator=gen)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, exchange):
     import sys
 
     sys.path.insert(0, ROOT)
@@ -53,8 +53,13 @@ def _worker(rank, world, port, q):
         step = mmn.OptimizerStep(model, cfg, device=rank,
                                  stream=torch.cuda.current_stream(rank).cuda_stream)
         _fill(step, model, 0)
+        if exchange == "fused":
+            step.connect_peers()
         for _ in range(2):
             step.step()
+            if exchange == "fused":
+                step.exchange_fence()
+                continue
             gl = step.gather_layout()
             for key, reg in (("adamw_param", "adamw_region"), ("muon_param", "muon_region")):
                 full = _view(gl[key], (gl[reg] * world,), "f32", rank)
@@ -69,7 +74,8 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_sharded_step_equals_single_gpu(mmn):
+@pytest.mark.parametrize("exchange", ["nccl", "fused"])
+def test_sharded_step_equals_single_gpu(mmn, exchange):
     import torch
     import torch.multiprocessing as mp
 
@@ -90,7 +96,7 @@ def test_sharded_step_equals_single_gpu(mmn):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     got = q.get(timeout=600)
