@@ -307,10 +307,13 @@ int mmn_optim_plan(const int64_t *shapes, const int *ndims, const int *routes, i
                    int64_t *adamw_region, int64_t *muon_region);
 
 /* Parameter exchange fused into the step (world_size > 1), in place of a
- * post-step all-gather. After mmn_optim_connect_peers the kernels that
- * produce final parameter values (AdamW and the last Newton-Schulz iteration)
- * also store each value into every peer's arena at the same offset, over
- * NVLink through CUDA IPC mappings: fp32 params, or only the bf16 copies when
+ * post-step all-gather. After mmn_optim_connect_peers the step pushes each
+ * finished piece of this rank's regions into every peer's arena at the same
+ * offset, over NVLink through CUDA IPC mappings, on a transfer stream of its
+ * own: the AdamW range once its kernel ends, and the Newton-Schulz matrices in
+ * chunks (runs of at most 16 matrices of one shape, largest first), each as
+ * soon as its last iteration ends, so the copies overlap the chunks still
+ * computing. fp32 params are sent, or only the bf16 copies when
  * bf16_param_shadow is on (the fp32 master then stays with its owner). Every
  * rank must finish its step before any rank reads parameters or starts the
  * next step: order the ranks after each mmn_optim_step (for example a

@@ -51,7 +51,8 @@ struct ShardPlan {
 //    ranges, rank r stepping range r.
 //  - Muon matrices go whole to a rank by longest-processing-time bin packing
 //    on their Newton-Schulz flops (ties to the lower rank), and are stored
-//    grouped by owner so each rank's matrices form one equal-size region.
+//    grouped by owner so each rank's matrices form one equal-size region,
+//    largest first inside it.
 // The plan depends only on the shapes, routes, world size and step count, so
 // every rank computes the same plan without communicating.
 void make_shard_plan(const std::vector<ShardTensor>& ts, int world, int ns_steps, ShardPlan* p) {
@@ -85,8 +86,19 @@ void make_shard_plan(const std::vector<ShardTensor>& ts, int world, int ns_steps
     p->owner[i] = best;
     load[best] += cost(i);
   }
+  // Inside a region the matrices run by cost, largest first, equal shapes
+  // together (oriented, so a matrix and its transpose share a Newton-Schulz
+  // batch), then registration order.
+  auto shape_key = [&](size_t i) {
+    return std::make_pair(std::min(ts[i].rows, ts[i].cols), std::max(ts[i].rows, ts[i].cols));
+  };
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) {
+    const double ca = cost(a), cb = cost(b);
+    if (ca != cb) return ca > cb;
+    return shape_key(a) < shape_key(b);
+  });
   std::vector<int64_t> used((size_t)world, 0);
-  for (size_t i : muon) {
+  for (size_t i : order) {
     p->off[i] = used[p->owner[i]];
     used[p->owner[i]] = align_up(used[p->owner[i]] + ts[i].numel, 64);
   }
@@ -175,9 +187,16 @@ struct mmn_optim {
   float* d_partials = nullptr;
   float* d_norms = nullptr;
   NsApply* d_apply = nullptr;   // per owned matrix, indexed like the norms
-  // fused exchange: IPC mappings of the other ranks' parameter arenas
-  PeerArenas peer_adamw, peer_muon;
+  std::vector<int64_t> chunk_begin, chunk_end;  // Muon arena range of every NS chunk
+  // peer exchange: IPC mappings of the other ranks' parameter arenas (fp32,
+  // or the bf16 copies when they are kept), filled by copy engines per chunk
+  int n_peers = 0;
+  void* peer_a[8] = {};
+  void* peer_m[8] = {};
   std::vector<void*> peer_maps;
+  cudaStream_t xfer = nullptr;
+  std::vector<cudaEvent_t> chunk_ev;
+  cudaEvent_t adamw_ev = nullptr, xfer_done = nullptr;
   std::vector<int> cls_base;    // first norm / apply slot of every class
   int total_tiles = 0;
   double ns_flops = 0.0;
@@ -272,6 +291,10 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   if (h->fork) cudaEventDestroy(h->fork);
   if (h->join) cudaEventDestroy(h->join);
   if (h->side) cudaStreamDestroy(h->side);
+  if (h->xfer) cudaStreamDestroy(h->xfer);
+  for (auto e : h->chunk_ev) cudaEventDestroy(e);
+  if (h->adamw_ev) cudaEventDestroy(h->adamw_ev);
+  if (h->xfer_done) cudaEventDestroy(h->xfer_done);
   if (h->work) cudaStreamDestroy(h->work);
   if (h->in_ev) cudaEventDestroy(h->in_ev);
   if (h->out_ev) cudaEventDestroy(h->out_ev);
@@ -367,22 +390,32 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
     chunk_seg[c] = (int)k;
   }
 
-  // ---- Newton-Schulz shape classes over the matrices this rank owns.
+  // ---- Newton-Schulz chunks over the matrices this rank owns, in arena order
+  // (largest shapes first): runs of one shape, at most kNsChunk matrices each.
+  // Chunks run one after another, so with the peer exchange each finished
+  // chunk's parameters cross NVLink while the following chunks compute. A
+  // single rank keeps whole shape classes (fewer, fuller launches).
+  const int kNsChunk = W > 1 ? 16 : 1 << 30;
+  std::vector<int> owned;
+  for (int i : muon_idx)
+    if (h->slots[i].owner == R) owned.push_back(i);
+  std::stable_sort(owned.begin(), owned.end(),
+                   [&](int a, int b) { return h->slots[a].off < h->slots[b].off; });
   std::vector<std::pair<int, int>> cls_shapes;
   std::vector<int> cls_count;
   int tiles = 0;
-  for (int i : muon_idx) {
+  for (int i : owned) {
     auto& s = h->slots[i];
-    if (s.owner != R) continue;
     const int n = std::min(s.rows, s.cols), m = std::max(s.rows, s.cols);
-    int ci = -1;
-    for (int k = 0; k < (int)cls_shapes.size(); ++k)
-      if (cls_shapes[k] == std::make_pair(n, m)) ci = k;
-    if (ci < 0) {
-      ci = (int)cls_shapes.size();
+    if (cls_shapes.empty() || cls_shapes.back() != std::make_pair(n, m) ||
+        cls_count.back() == kNsChunk) {
       cls_shapes.emplace_back(n, m);
       cls_count.push_back(0);
+      h->chunk_begin.push_back(s.off);
+      h->chunk_end.push_back(s.off);
     }
+    const int ci = (int)cls_shapes.size() - 1;
+    h->chunk_end[ci] = s.off + s.numel;
     MuonMat mm{};
     mm.off = s.off;
     mm.rows = s.rows;
@@ -624,6 +657,19 @@ extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
   return MMN_OK;
 }
 
+// Copies elements [lo, hi) of a local parameter arena (fp32, or bf16 when the
+// copies are kept) into the same range of every peer's arena on the transfer
+// stream (copy engines over NVLink through the IPC mappings).
+static int copy_to_peers(mmn_optim_t* h, void* local, void* const* peers, int64_t lo, int64_t hi) {
+  if (hi <= lo) return MMN_OK;
+  const size_t es = h->cfg.bf16_param_shadow ? 2 : 4;
+  const uint8_t* src = static_cast<const uint8_t*>(local) + (size_t)lo * es;
+  for (int r = 0; r < h->n_peers; ++r)
+    MMN_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(peers[r]) + (size_t)lo * es, src,
+                                 (size_t)(hi - lo) * es, cudaMemcpyDeviceToDevice, h->xfer));
+  return MMN_OK;
+}
+
 // Enqueues the whole step on the handle's stream (AdamW forked onto a side
 // stream so it overlaps the Newton-Schulz GEMMs).
 static int enqueue_step(mmn_optim_t* h, float divisor) {
@@ -679,11 +725,20 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   a.wd = h->cfg.adamw.weight_decay;
   a.grad_divisor = divisor;
   a.fresh_state = h->cfg.fresh_state;
-  a.peers = h->peer_adamw;
   launch_adamw(a, h->ctx.num_sms, h->side);
   MMN_CUDA_TRY(cudaGetLastError());
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
   MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
+  if (h->n_peers) {
+    // this rank's AdamW range goes to every peer while the Muon work runs
+    const int64_t lo = std::min<int64_t>(h->a_region4 * R, h->a_used4) * 4;
+    const int64_t hi = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) * 4;
+    MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
+    int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->ap16 : (void*)h->ap, h->peer_a,
+                           lo, hi);
+    if (rc != MMN_OK) return rc;
+  }
 
   // ---- Muon on the main stream
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[3], s));
@@ -720,17 +775,34 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
       f.p = h->mp;
       f.p_bf16 = h->mp16;
       f.apply = h->d_apply + h->cls_base[k];
-      f.peers = h->peer_muon;
       std::string err;
       if (ns_class_run(h->classes[k], h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status,
                        h->ctx.num_sms, s, &err, fuse ? &f : nullptr, skip) < 0)
         return fail(MMN_E_CUDA, err);
+      if (h->n_peers && fuse) {
+        // the chunk's parameters are final: copy engines push them over NVLink
+        // while the next chunk computes
+        MMN_CUDA_TRY(cudaEventRecord(h->chunk_ev[k], s));
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->chunk_ev[k], 0));
+        int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
+                               h->peer_m, h->chunk_begin[k], h->chunk_end[k]);
+        if (rc != MMN_OK) return rc;
+      }
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
     if (!fuse) {
       m.cls = h->d_cls_out;
       launch_muon_apply(m, h->ctx.num_sms, s);
       MMN_CUDA_TRY(cudaGetLastError());
+      if (h->n_peers && !h->chunk_ev.empty()) {
+        MMN_CUDA_TRY(cudaEventRecord(h->chunk_ev[0], s));
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->chunk_ev[0], 0));
+        for (size_t k = 0; k < h->chunk_begin.size(); ++k) {
+          int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
+                                 h->peer_m, h->chunk_begin[k], h->chunk_end[k]);
+          if (rc != MMN_OK) return rc;
+        }
+      }
     }
   } else if (tm) {
     MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
@@ -738,6 +810,10 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   }
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[6], s));
   MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->join, 0));
+  if (h->n_peers) {
+    MMN_CUDA_TRY(cudaEventRecord(h->xfer_done, h->xfer));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->xfer_done, 0));
+  }
   StepTail t{};
   t.step_counter = h->d_step;
   t.adamw_calls = h->n_adamw;
@@ -871,14 +947,14 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
   if (!h || !blobs) return fail(MMN_E_INVALID, "null argument");
   if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
   const int W = h->cfg.world_size, R = h->cfg.rank;
+  constexpr int kMaxPeers = 7;
   if (W - 1 > kMaxPeers) return fail(MMN_E_UNSUPPORTED, "at most 8 ranks share the exchange");
-  if (h->cfg.muon.ns_steps < 1 && !h->mats.empty())
-    return fail(MMN_E_UNSUPPORTED, "the fused exchange rides on the last Newton-Schulz "
-                                   "iteration: ns_steps must be >= 1");
   if (!h->peer_maps.empty()) return fail(MMN_E_STATE, "peers already connected");
   DevGuard g(h->ctx.device);
   const uint8_t* raw = static_cast<const uint8_t*>(blobs);
-  PeerArenas pa, pm;
+  int n_peers = 0;
+  void* peer_a[8] = {};
+  void* peer_m[8] = {};
   std::vector<void*> maps;
   auto open = [&](const cudaIpcMemHandle_t& hd, void** out) -> int {
     cudaError_t e = cudaIpcOpenMemHandle(out, hd, cudaIpcMemLazyEnablePeerAccess);
@@ -898,23 +974,35 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     }
     if (r == R) continue;
     void *ap = nullptr, *mp = nullptr;
-    if (h->cfg.bf16_param_shadow) {
-      if ((rc = open(b.ap16, &ap)) != MMN_OK || (rc = open(b.mp16, &mp)) != MMN_OK) break;
-      pa.p16[pa.n++] = static_cast<__nv_bfloat16*>(ap);
-      pm.p16[pm.n++] = static_cast<__nv_bfloat16*>(mp);
-    } else {
-      if ((rc = open(b.ap, &ap)) != MMN_OK || (rc = open(b.mp, &mp)) != MMN_OK) break;
-      pa.p[pa.n++] = static_cast<float*>(ap);
-      pm.p[pm.n++] = static_cast<float*>(mp);
-    }
+    const bool sh = h->cfg.bf16_param_shadow;
+    if ((rc = open(sh ? b.ap16 : b.ap, &ap)) != MMN_OK || (rc = open(sh ? b.mp16 : b.mp, &mp)) != MMN_OK)
+      break;
+    peer_a[n_peers] = ap;
+    peer_m[n_peers] = mp;
+    ++n_peers;
   }
-  if (rc != MMN_OK) {
+  auto undo = [&](int code) {
     for (void* p : maps) cudaIpcCloseMemHandle(p);
-    return rc;
+    return code;
+  };
+  if (rc != MMN_OK) return undo(rc);
+  if (!h->xfer) {
+    cudaError_t e = cudaStreamCreateWithFlags(&h->xfer, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->adamw_ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->xfer_done, cudaEventDisableTiming);
+    for (size_t k = h->chunk_ev.size(); e == cudaSuccess && k < h->chunk_begin.size(); ++k) {
+      cudaEvent_t ev = nullptr;
+      e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      if (e == cudaSuccess) h->chunk_ev.push_back(ev);
+    }
+    if (e != cudaSuccess) return undo(cuda_fail(e, "transfer stream setup"));
   }
   h->peer_maps = maps;
-  h->peer_adamw = pa;
-  h->peer_muon = pm;
+  h->n_peers = n_peers;
+  for (int k = 0; k < n_peers; ++k) {
+    h->peer_a[k] = peer_a[k];
+    h->peer_m[k] = peer_m[k];
+  }
   if (h->graph) {  // the captured step must be re-captured with the peers
     cudaGraphExecDestroy(h->graph);
     h->graph = nullptr;

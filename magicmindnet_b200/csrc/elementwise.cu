@@ -106,10 +106,6 @@ __device__ __forceinline__ void adamw_store(const AdamwArgs& a, long long i, con
     out.x = *reinterpret_cast<uint32_t*>(&h0);
     out.y = *reinterpret_cast<uint32_t*>(&h1);
     __stcs(reinterpret_cast<uint2*>(a.p_bf16) + i, out);
-    // fused exchange: the peers receive only the bf16 copy
-    for (int r = 0; r < a.peers.n; ++r) reinterpret_cast<uint2*>(a.peers.p16[r])[i] = out;
-  } else {
-    for (int r = 0; r < a.peers.n; ++r) reinterpret_cast<float4*>(a.peers.p[r])[i] = q.p;
   }
 }
 
@@ -165,8 +161,6 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamwArgs a) {
       adamw_store<FRESH, SHADOW>(a, i1, q1);
     }
   }
-  // stores into peer arenas are ordered before the caller's cross-rank fence
-  if (a.peers.n) __threadfence_system();
 }
 
 // Index of the matrix owning tile t: the last k with mats[k].tile0 <= t.

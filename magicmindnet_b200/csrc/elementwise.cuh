@@ -7,15 +7,6 @@
 
 namespace mmn {
 
-// Peer arenas (other ranks' copies of the same layout) that final parameter
-// values are also stored into: fp32 params, or bf16 copies when p16 is used.
-constexpr int kMaxPeers = 7;
-struct PeerArenas {
-  int n = 0;
-  float* p[kMaxPeers] = {};
-  __nv_bfloat16* p16[kMaxPeers] = {};
-};
-
 // One tensor of the flat AdamW arena, in float4 units. Segments tile the arena
 // contiguously: seg[k].end4 == seg[k+1].start4.
 struct AdamwSeg {
@@ -45,7 +36,6 @@ struct AdamwArgs {
   float lr, b1, b2, eps, wd;
   float grad_divisor;         // GradAccumulator averaging divisor (1 = none)
   int fresh_state;            // m and v read as zero and not stored
-  PeerArenas peers;           // AdamW arenas of the other ranks (fused exchange)
 };
 
 constexpr long long kAdamwChunk4 = 2048;  // float4 per chunk-table entry

@@ -269,7 +269,6 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
     g.p = fused->p;
     g.p_bf16 = fused->p_bf16;
     g.apply = fused->apply;
-    g.peers = fused->peers;
   }
   if (mode == kNsBf16) {
     g.tiles_n = (c.m + 255) / 256;

@@ -9,8 +9,6 @@
 #include <string>
 #include <vector>
 
-#include "elementwise.cuh"
-
 namespace mmn {
 
 enum NsMode : int {
@@ -59,7 +57,6 @@ struct NsFused {
   float* p = nullptr;
   __nv_bfloat16* p_bf16 = nullptr;
   const NsApply* apply = nullptr;
-  PeerArenas peers;  // the same values also go to these ranks' arenas
 };
 
 // Runs `steps` iterations on every matrix of the class; X starts in x[0] with

@@ -28,7 +28,6 @@
 #pragma once
 #include <cuda.h>
 
-#include "elementwise.cuh"
 #include "mmn_ptx.cuh"
 
 namespace mmn {
@@ -70,7 +69,6 @@ struct NsGemmArgs {
   __nv_bfloat16* p_bf16;     // optional bf16 copy of the updated params
   const NsApply* apply;      // per batch item, used when p is set
   const int* skip;           // device non-finite flag: when set the launch does nothing
-  PeerArenas peers;          // fused exchange: other ranks' Muon arenas
 };
 
 template <int BN, bool DUAL, bool B_MN, bool PAIR>
@@ -134,17 +132,6 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   }
 }
 
-// Fused exchange: the final value of parameter element idx also goes to every
-// peer rank's arena (bf16 copy only when the bf16 shadow is kept).
-__device__ __forceinline__ void store_to_peers(const NsGemmArgs& args, long long idx, float pn) {
-  for (int pr = 0; pr < args.peers.n; ++pr) {
-    if (args.p_bf16)
-      args.peers.p16[pr][idx] = __float2bfloat16_rn(pn);
-    else
-      args.peers.p[pr][idx] = pn;
-  }
-}
-
 // Last step of every Poly epilogue for one row r and 32 columns c0..c0+31,
 // given bx = (b*A X + c*A2 X) or Bm X: o = bf16((X/s)*a + bx/s), stored as X'
 // or, in the last iteration, applied as p -= lr*scale*o in the parameter's
@@ -199,11 +186,6 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
           u.x = pack_bf16x2(pv.x, pv.y);
           u.y = pack_bf16x2(pv.z, pv.w);
           *reinterpret_cast<uint2*>(args.p_bf16 + base + q * 4) = u;
-          for (int pr = 0; pr < args.peers.n; ++pr)
-            *reinterpret_cast<uint2*>(args.peers.p16[pr] + base + q * 4) = u;
-        } else {
-          for (int pr = 0; pr < args.peers.n; ++pr)
-            *reinterpret_cast<float4*>(args.peers.p[pr] + base + q * 4) = pv;
         }
       }
     } else if (row_ok) {
@@ -213,7 +195,6 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
           const float pn = __fsub_rn(prow[j], __fmul_rn(ls, v[j]));
           prow[j] = pn;
           if (args.p_bf16) args.p_bf16[base + j] = __float2bfloat16_rn(pn);
-          store_to_peers(args, base + j, pn);
         }
     }
   } else if (row_ok) {
@@ -225,7 +206,6 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
         const float pn = __fsub_rn(args.p[idx], __fmul_rn(ls, v[j]));
         args.p[idx] = pn;
         if (args.p_bf16) args.p_bf16[idx] = __float2bfloat16_rn(pn);
-        store_to_peers(args, idx, pn);
       }
   }
 }
@@ -558,8 +538,6 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   if (PAIR) cluster_sync_all();  // peer loads landed, remote arrivals done, MMAs retired
-  // stores into peer arenas are ordered before the caller's cross-rank fence
-  if (args.peers.n && warp >= 2) __threadfence_system();
   if (*abort_flag && threadIdx.x == 0) atomicExch(args.status, kDevWaitTimeout);
   if (warp == 1) {
     tc_fence_after();
