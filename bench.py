@@ -317,30 +317,65 @@ def run_ours(args, rank, world, local_rank):
     value = n_total / (ms / 1e3)
 
     # --- e2e: host grads in, host params out through the public API
+    # (mmn_optim_step_host: the copies are pipelined with the compute per chunk).
+    # Each rank copies in the grads it steps and copies back the params it
+    # stepped; with the peer exchange the device arenas are complete as well.
     e2e = None
-    if args.e2e and world == 1:
-        pin_g = [torch.empty(s, dtype=step.grad(k).dtype, pin_memory=True)
+    if args.e2e:
+        plan = mmn.shard_plan([(k, s, r) for k, (_, s, r) in enumerate(model)], world)
+        areg = plan["adamw_region"]
+        stepped = []  # elements of every slot this rank steps
+        for k, (_, s, r) in enumerate(model):
+            n = int(np.prod(s))
+            if plan["owner"][k] >= 0:
+                stepped.append(n if plan["owner"][k] == rank else 0)
+            else:
+                off = plan["offset"][k]
+                stepped.append(max(0, min(off + n, (rank + 1) * areg) - max(off, rank * areg)))
+        gsz = 2 if spec["grad"] == "bf16" else 4
+        pin_g = [step.grad(k).cpu().pin_memory() if stepped[k] or (is_8b and world > 1) else None
+                 for k in range(len(model))]
+        pin_p = [torch.empty(s, dtype=torch.float32).pin_memory() if stepped[k] else None
                  for k, (_, s, _) in enumerate(model)]
-        pin_p = [torch.empty(s, dtype=torch.float32, pin_memory=True) for _, s, _ in model]
-        for k in range(len(model)):
-            pin_g[k].copy_(step.grad(k))
-        views_g = [step.grad(k) for k in range(len(model))]
-        views_p = [step.param(k) for k in range(len(model))]
-        bi = sum(t.numel() * t.element_size() for t in pin_g)
-        bo = sum(t.numel() * 4 for t in pin_p)
+        full_in = is_8b and world > 1  # the non-finite scan reads every grad
+        bi = sum((int(np.prod(s)) if full_in else stepped[k]) * gsz
+                 for k, (_, s, _) in enumerate(model))
+        bo = sum(stepped) * 4
+
+        def host_step():
+            step.step_host(pin_g, pin_p, divisor)
+            if fused:
+                step.exchange_fence()
+            if gathers:
+                import torch.distributed as dist
+
+                for full, mine in gathers:
+                    dist.all_gather_into_tensor(full, mine)
+                torch.cuda.current_stream(dev).synchronize()
+
+        for _ in range(2):
+            host_step()
         e_steps = max(1, min(args.steps, 10))
-        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
         t0 = time.perf_counter()
         for _ in range(e_steps):
-            for k in range(len(model)):
-                views_g[k].copy_(pin_g[k], non_blocking=True)
-            step.step(divisor)
-            for k in range(len(model)):
-                pin_p[k].copy_(views_p[k], non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
+            host_step()
         e_ms = (time.perf_counter() - t0) * 1e3 / e_steps
+        if world > 1:
+            import torch.distributed as dist
+
+            tt = torch.tensor([e_ms, bi, bo], dtype=torch.float64, device=f"cuda:{dev}")
+            mx = tt.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+            e_ms, bi, bo = float(mx[0]), int(tt[1]), int(tt[2])
         e2e = {"value": n_total / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
-               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+               "api": "mmn_optim_step_host (pinned host buffers, synchronous)",
+               "timing": "host wall clock per step, max over ranks"}
 
     pk, pk_kind = peaks()
     med = {k: (statistics.median(v) if v else 0.0) for k, v in phase.items()}
@@ -389,7 +424,8 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": args.workload, "desc": spec["desc"], "params": n_total,
                    "adamw_params": n_adamw, "muon_params": n_muon, "ns_mode": args.ns_mode,
                    "parallelism": f"shard{world}" if world > 1 else "single",
-                   "exchange": ("fused NVLink stores + 1-element all-reduce fence" if fused else
+                   "exchange": ("copy-engine pushes over NVLink per chunk + 1-element all-reduce fence"
+                                if fused else
                                 "NCCL all-gather of the parameter arenas") if world > 1 else None,
                    "l2": "inputs larger than L2 (no flush needed)"},
         "roofline": roof, "components": comp, "clocks": clk, "e2e": e2e,

@@ -269,6 +269,21 @@ int mmn_optim_get_adamw_step(mmn_optim_t *h, uint64_t *step);
  * GradAccumulator's micro-batch count (1 = none). Asynchronous. */
 int mmn_optim_step(mmn_optim_t *h, float grad_divisor);
 
+/* One step from host memory, the batched form of the reference's
+ * optim_step_weight calls on host arrays (crates/mmn-models/src/chatbot.rs:208-227
+ * calling HybridOptimizer::step, crates/mmn-optim/src/lib.rs:221-245).
+ * grads[slot] (host, grad_dtype, numel elements) are copied in, the step runs,
+ * and the updated fp32 params go to params[slot] (host); the device copy stays
+ * the master. Either array may hold null entries (that slot's copy is skipped:
+ * its grad is already on the device / its params are not read back). With
+ * world_size > 1 a rank copies only what it steps (its Muon matrices and its
+ * AdamW range; every grad when loss_scaling is on, for the non-finite scan).
+ * The copies run on two copy streams in chunks, overlapped with the compute
+ * and with each other; pinned (page-locked) host memory lets them overlap.
+ * Synchronous: returns once params[] hold the step's result. */
+int mmn_optim_step_host(mmn_optim_t *h, const void *const *grads, float *const *params,
+                        float grad_divisor);
+
 /* Wait for the handle's stream; reports MMN_E_TIMEOUT if a kernel gave up. */
 int mmn_optim_sync(mmn_optim_t *h);
 

@@ -9,9 +9,10 @@ from ._native import CUDAError, KernelTimeoutError, MmnError, ShapeError  # noqa
 from .optim import (AdamW, AdamWConfig, GradAccumulator, HybridOptimizer, Muon,  # noqa: F401
                     MuonConfig, ParamKind, is_available, newton_schulz5, require_cuda)
 from .step import (OptimizerStep, StepConfig, TrainConfig, chatbot_param_order,  # noqa: F401
-                   step_config_for)
+                   shard_plan, step_config_for)
 
 __all__ = ["AdamW", "AdamWConfig", "Muon", "MuonConfig", "HybridOptimizer", "ParamKind",
            "GradAccumulator", "newton_schulz5", "is_available", "require_cuda", "OptimizerStep",
-           "StepConfig", "TrainConfig", "step_config_for", "chatbot_param_order", "MmnError",
+           "StepConfig", "TrainConfig", "step_config_for", "chatbot_param_order", "shard_plan",
+           "MmnError",
            "CUDAError", "ShapeError", "KernelTimeoutError"]

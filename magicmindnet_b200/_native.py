@@ -122,6 +122,7 @@ SIGNATURES = {
     "mmn_optim_set_adamw_step": (_i, [_vp, _u64]),
     "mmn_optim_get_adamw_step": (_i, [_vp, ctypes.POINTER(_u64)]),
     "mmn_optim_step": (_i, [_vp, _f]),
+    "mmn_optim_step_host": (_i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _f]),
     "mmn_optim_sync": (_i, [_vp]),
     "mmn_optim_loss_scale": (_i, [_vp, ctypes.POINTER(_f), ctypes.POINTER(_i64)]),
     "mmn_optim_slot_owner": (_i, [_vp, _i, ctypes.POINTER(_i)]),

@@ -188,6 +188,24 @@ struct mmn_optim {
   float* d_norms = nullptr;
   NsApply* d_apply = nullptr;   // per owned matrix, indexed like the norms
   std::vector<int64_t> chunk_begin, chunk_end;  // Muon arena range of every NS chunk
+  std::vector<int> chunk_mat0, chunk_tile0;     // first matrix / 64x64 tile of every
+                                                // chunk (one past the end appended)
+  std::vector<std::vector<int>> chunk_slots;    // slots of every chunk
+  // Order of the step's jobs: >= 0 is NS chunk k, < 0 is AdamW part -1 - p
+  // (host-memory steps step the AdamW range in parts; the device step in one
+  // launch). Compute-heavy and copy-heavy chunks alternate.
+  std::vector<int> jobs;
+  struct Piece {
+    int slot;
+    int64_t lo, hi;  // element range of the slot
+  };
+  std::vector<int64_t> apart_begin4, apart_end4;
+  std::vector<std::vector<Piece>> apart_pieces;  // AdamW slots' ranges inside every part
+  // host-memory steps: grads in and params out on two copy streams, per job
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  std::vector<cudaEvent_t> h2d_ev;              // [j] job j's grads landed, back() all grads
+  std::vector<cudaEvent_t> apart_ev;            // AdamW part p stepped
+  cudaEvent_t d2h_done = nullptr;
   // peer exchange: IPC mappings of the other ranks' parameter arenas (fp32,
   // or the bf16 copies when they are kept), filled by copy engines per chunk
   int n_peers = 0;
@@ -292,9 +310,17 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   if (h->join) cudaEventDestroy(h->join);
   if (h->side) cudaStreamDestroy(h->side);
   if (h->xfer) cudaStreamDestroy(h->xfer);
-  for (auto e : h->chunk_ev) cudaEventDestroy(e);
+  if (h->h2d) cudaStreamDestroy(h->h2d);
+  if (h->d2h) cudaStreamDestroy(h->d2h);
+  for (auto e : h->chunk_ev)
+    if (e) cudaEventDestroy(e);
+  for (auto e : h->h2d_ev)
+    if (e) cudaEventDestroy(e);
+  for (auto e : h->apart_ev)
+    if (e) cudaEventDestroy(e);
   if (h->adamw_ev) cudaEventDestroy(h->adamw_ev);
   if (h->xfer_done) cudaEventDestroy(h->xfer_done);
+  if (h->d2h_done) cudaEventDestroy(h->d2h_done);
   if (h->work) cudaStreamDestroy(h->work);
   if (h->in_ev) cudaEventDestroy(h->in_ev);
   if (h->out_ev) cudaEventDestroy(h->out_ev);
@@ -391,11 +417,15 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   }
 
   // ---- Newton-Schulz chunks over the matrices this rank owns, in arena order
-  // (largest shapes first): runs of one shape, at most kNsChunk matrices each.
+  // (largest shapes first): runs of one shape, at most kNsChunk matrices and
+  // kChunkElems elements each (256 MB of fp32: big enough to fill the GPU with
+  // tiles, small enough that a chunk's PCIe or NVLink copy is short).
   // Chunks run one after another, so with the peer exchange each finished
-  // chunk's parameters cross NVLink while the following chunks compute. A
-  // single rank keeps whole shape classes (fewer, fuller launches).
-  const int kNsChunk = W > 1 ? 16 : 1 << 30;
+  // chunk's parameters cross NVLink while the following chunks compute, and a
+  // step from host memory overlaps each chunk's copies with its neighbours'
+  // compute.
+  constexpr int kNsChunk = 16;
+  constexpr int64_t kChunkElems = int64_t(1) << 26;
   std::vector<int> owned;
   for (int i : muon_idx)
     if (h->slots[i].owner == R) owned.push_back(i);
@@ -408,14 +438,19 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
     auto& s = h->slots[i];
     const int n = std::min(s.rows, s.cols), m = std::max(s.rows, s.cols);
     if (cls_shapes.empty() || cls_shapes.back() != std::make_pair(n, m) ||
-        cls_count.back() == kNsChunk) {
+        cls_count.back() == kNsChunk ||
+        s.off + s.numel - h->chunk_begin.back() > kChunkElems) {
       cls_shapes.emplace_back(n, m);
       cls_count.push_back(0);
       h->chunk_begin.push_back(s.off);
       h->chunk_end.push_back(s.off);
+      h->chunk_mat0.push_back((int)h->mats.size());
+      h->chunk_tile0.push_back(tiles);
+      h->chunk_slots.emplace_back();
     }
     const int ci = (int)cls_shapes.size() - 1;
     h->chunk_end[ci] = s.off + s.numel;
+    h->chunk_slots[ci].push_back(i);
     MuonMat mm{};
     mm.off = s.off;
     mm.rows = s.rows;
@@ -430,6 +465,56 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
     h->ns_flops += (double)steps * (4.0 * n * (double)n * m + 2.0 * (double)n * n * n);
   }
   h->total_tiles = tiles;
+  h->chunk_mat0.push_back((int)h->mats.size());
+  h->chunk_tile0.push_back(tiles);
+
+  // ---- AdamW parts of at most kChunkElems elements over this rank's range
+  {
+    const int64_t lo4 = std::min<int64_t>(h->a_region4 * R, h->a_used4);
+    const int64_t hi4 = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4);
+    const int64_t n4 = hi4 - lo4;
+    const int64_t parts = n4 > 0 ? (n4 * 4 + kChunkElems - 1) / kChunkElems : 0;
+    for (int64_t p = 0; p < parts; ++p) {
+      const int64_t b4 = lo4 + n4 * p / parts, e4 = lo4 + n4 * (p + 1) / parts;
+      h->apart_begin4.push_back(b4);
+      h->apart_end4.push_back(e4);
+      std::vector<mmn_optim::Piece> pcs;
+      for (size_t i = 0; i < h->slots.size(); ++i) {
+        const auto& sl = h->slots[i];
+        if (sl.route != MMN_ROUTE_ADAMW) continue;
+        const int64_t l = std::max<int64_t>(b4 * 4, sl.off) - sl.off;
+        const int64_t u = std::min<int64_t>(e4 * 4, sl.off + sl.numel) - sl.off;
+        if (u > l) pcs.push_back({(int)i, l, u});
+      }
+      h->apart_pieces.push_back(pcs);
+    }
+  }
+  // ---- job order: chunks zipped from the most and the least flops per element
+  // (4n + 2n^2/m for an n x m chunk), AdamW parts first and last and spread
+  // between (a part's compute is short and runs beside the GEMMs, so it makes
+  // the shortest pipeline head and tail)
+  {
+    const int nck = (int)cls_shapes.size();
+    std::vector<int> ck(nck);
+    for (int k = 0; k < nck; ++k) ck[k] = k;
+    auto per_elem = [&](int k) {
+      const double n = cls_shapes[k].first, m = cls_shapes[k].second;
+      return 4.0 * n + 2.0 * n * n / m;
+    };
+    std::stable_sort(ck.begin(), ck.end(), [&](int a, int b) { return per_elem(a) > per_elem(b); });
+    std::vector<int> zig;
+    for (int lo = 0, hi = nck - 1, front = 1; lo <= hi; front ^= 1) zig.push_back(front ? ck[lo++] : ck[hi--]);
+    const int P = (int)h->apart_begin4.size();
+    std::vector<std::vector<int>> before(zig.size() + 1);  // AdamW parts placed before zig[i]
+    for (int p = 0; p < P; ++p) {
+      const size_t pos = P == 1 ? zig.size() : (size_t)((double)p * zig.size() / (P - 1) + 0.5);
+      before[std::min(pos, zig.size())].push_back(-1 - p);
+    }
+    for (size_t i = 0; i <= zig.size(); ++i) {
+      for (int j : before[i]) h->jobs.push_back(j);
+      if (i < zig.size()) h->jobs.push_back(zig[i]);
+    }
+  }
   if (!h->mats.empty()) {
     std::string e = ns_gemm_setup();
     if (!e.empty()) return fail(MMN_E_CUDA, e);
@@ -512,6 +597,18 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming));
   for (auto& e : h->ev) MMN_CUDA_TRY(cudaEventCreate(&e));
+  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->xfer, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->h2d, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->d2h, cudaStreamNonBlocking));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->adamw_ev, cudaEventDisableTiming));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->xfer_done, cudaEventDisableTiming));
+  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->d2h_done, cudaEventDisableTiming));
+  h->chunk_ev.assign(h->chunk_begin.size(), nullptr);
+  for (auto& e : h->chunk_ev) MMN_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  h->h2d_ev.assign(h->jobs.size() + 1, nullptr);
+  for (auto& e : h->h2d_ev) MMN_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  h->apart_ev.assign(h->apart_begin4.size(), nullptr);
+  for (auto& e : h->apart_ev) MMN_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaDeviceSynchronize());
   h->finalized = true;
   return MMN_OK;
@@ -670,17 +767,103 @@ static int copy_to_peers(mmn_optim_t* h, void* local, void* const* peers, int64_
   return MMN_OK;
 }
 
-// Enqueues the whole step on the handle's stream (AdamW forked onto a side
-// stream so it overlaps the Newton-Schulz GEMMs).
-static int enqueue_step(mmn_optim_t* h, float divisor) {
+// Host buffers of a step from host memory, indexed by slot: grads in the grad
+// dtype, params fp32. A null entry skips that slot's copy.
+struct HostIO {
+  const void* const* grads;
+  float* const* params;
+};
+
+// The elements [lo, hi) of a slot that this rank steps: a whole Muon matrix
+// it owns, or the overlap of an AdamW tensor with its AdamW range. Returns
+// false (lo == hi == 0) when it steps none of the slot.
+static bool stepped_range(const mmn_optim_t* h, const mmn_optim::Slot& s, int64_t* lo,
+                          int64_t* hi) {
+  *lo = *hi = 0;
+  if (s.route == MMN_ROUTE_MUON) {
+    if (s.owner != h->cfg.rank) return false;
+    *hi = s.numel;
+    return true;
+  }
+  const int R = h->cfg.rank;
+  const int64_t rlo = std::min<int64_t>(h->a_region4 * R, h->a_used4) * 4;
+  const int64_t rhi = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) * 4;
+  const int64_t l = std::max<int64_t>(rlo, s.off) - s.off;
+  const int64_t u = std::min<int64_t>(rhi, s.off + s.numel) - s.off;
+  if (u <= l) return false;
+  *lo = l;
+  *hi = u;
+  return true;
+}
+
+// Host grads[slot][lo, hi) -> the slot's device grads, on the h2d stream.
+static int grad_in(mmn_optim_t* h, const HostIO* io, int i, int64_t lo, int64_t hi) {
+  const auto& s = h->slots[i];
+  if (!io->grads[i] || hi <= lo) return MMN_OK;
+  const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
+  uint8_t* dst = static_cast<uint8_t*>(s.route == MMN_ROUTE_ADAMW ? h->ag : h->mg) +
+                 (size_t)(s.off + lo) * gsz;
+  const uint8_t* src = static_cast<const uint8_t*>(io->grads[i]) + (size_t)lo * gsz;
+  MMN_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)(hi - lo) * gsz, cudaMemcpyHostToDevice, h->h2d));
+  return MMN_OK;
+}
+
+// Device params of slot i, elements [lo, hi) -> host params[slot], on the d2h stream.
+static int param_out(mmn_optim_t* h, const HostIO* io, int i, int64_t lo, int64_t hi) {
+  if (!io->params[i] || hi <= lo) return MMN_OK;
+  MMN_CUDA_TRY(cudaMemcpyAsync(io->params[i] + lo, slot_param(h, h->slots[i]) + lo,
+                               (size_t)(hi - lo) * 4, cudaMemcpyDeviceToHost, h->d2h));
+  return MMN_OK;
+}
+
+#define MMN_TRY_RC(x)            \
+  do {                           \
+    const int rc_ = (x);         \
+    if (rc_ != MMN_OK) return rc_; \
+  } while (0)
+
+// Enqueues the whole step on the handle's work stream: AdamW forked onto a
+// side stream so it overlaps the Newton-Schulz GEMMs, the Muon matrices in
+// chunks. With `io` the grads come from host memory and the stepped params go
+// back to it, on two copy streams: grads cross in the order the step consumes
+// them (AdamW's, then each chunk's, largest chunk first), each group's compute
+// starts when its copy lands, and each finished group's params start back at
+// once, so the PCIe transfers in both directions overlap the compute.
+static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   cudaStream_t s = h->work;
-  const bool tm = h->timing;
+  const bool tm = h->timing && !io;
   const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
   const int R = h->cfg.rank;
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[0], s));
+
+  // ---- grads in (host steps), job by job
+  if (io) {
+    MMN_CUDA_TRY(cudaStreamWaitEvent(h->h2d, h->in_ev, 0));
+    for (size_t j = 0; j < h->jobs.size(); ++j) {
+      const int job = h->jobs[j];
+      if (job >= 0) {
+        for (int i : h->chunk_slots[job]) MMN_TRY_RC(grad_in(h, io, i, 0, h->slots[i].numel));
+      } else {
+        for (const auto& pc : h->apart_pieces[-1 - job]) MMN_TRY_RC(grad_in(h, io, pc.slot, pc.lo, pc.hi));
+      }
+      MMN_CUDA_TRY(cudaEventRecord(h->h2d_ev[j], h->h2d));
+    }
+    if (h->cfg.loss_scaling && h->cfg.world_size > 1) {
+      // the non-finite scan reads every grad: the peers' parts come in too
+      int64_t lo, hi;
+      for (size_t i = 0; i < h->slots.size(); ++i) {
+        stepped_range(h, h->slots[i], &lo, &hi);
+        MMN_TRY_RC(grad_in(h, io, (int)i, 0, lo));
+        MMN_TRY_RC(grad_in(h, io, (int)i, hi, h->slots[i].numel));
+      }
+    }
+    MMN_CUDA_TRY(cudaEventRecord(h->h2d_ev.back(), h->h2d));
+  }
+
   if (h->cfg.loss_scaling) {
     // Every rank scans every grad (grads are replicated), so all ranks reach
     // the same skip decision without a collective.
+    if (io) MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->h2d_ev.back(), 0));
     MMN_CUDA_TRY(cudaMemsetAsync(h->d_skip, 0, sizeof(int), s));
     const int64_t a_n = h->a_used4 * 4;
     if (bf) {
@@ -698,7 +881,8 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   const int* skip = h->cfg.loss_scaling ? h->d_skip : nullptr;
   const float* gscale = h->cfg.loss_scaling ? h->d_scale : nullptr;
 
-  // ---- AdamW on the side stream
+  // ---- AdamW on the side stream: one launch over this rank's range, or (host
+  // steps) one per part, each after its grads landed
   MMN_CUDA_TRY(cudaEventRecord(h->fork, s));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->fork, 0));
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[1], h->side));
@@ -711,8 +895,6 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   a.p_bf16 = h->ap16;
   a.segs = h->d_segs;
   a.chunk_seg = h->d_chunk_seg;
-  a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
-  a.end4 = std::min<long long>(h->a_region4 * (R + 1), h->a_used4);
   a.bc_table = h->bc.dev;
   a.t_sat = h->bc.t_sat;
   a.step_base = h->d_step;
@@ -725,22 +907,38 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
   a.wd = h->cfg.adamw.weight_decay;
   a.grad_divisor = divisor;
   a.fresh_state = h->cfg.fresh_state;
-  launch_adamw(a, h->ctx.num_sms, h->side);
-  MMN_CUDA_TRY(cudaGetLastError());
+  void* a_src = h->cfg.bf16_param_shadow ? (void*)h->ap16 : (void*)h->ap;
+  if (io) {
+    for (size_t j = 0; j < h->jobs.size(); ++j) {
+      if (h->jobs[j] >= 0) continue;
+      const int p = -1 - h->jobs[j];
+      MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->h2d_ev[j], 0));
+      a.begin4 = h->apart_begin4[p];
+      a.end4 = h->apart_end4[p];
+      launch_adamw(a, h->ctx.num_sms, h->side);
+      MMN_CUDA_TRY(cudaGetLastError());
+      MMN_CUDA_TRY(cudaEventRecord(h->apart_ev[p], h->side));
+      if (h->n_peers) {
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->apart_ev[p], 0));
+        MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
+      }
+    }
+  } else {
+    a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
+    a.end4 = std::min<long long>(h->a_region4 * (R + 1), h->a_used4);
+    launch_adamw(a, h->ctx.num_sms, h->side);
+    MMN_CUDA_TRY(cudaGetLastError());
+    if (h->n_peers) {
+      // this rank's AdamW range goes to every peer while the Muon work runs
+      MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
+      MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
+      MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
+    }
+  }
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
   MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
-  if (h->n_peers) {
-    // this rank's AdamW range goes to every peer while the Muon work runs
-    const int64_t lo = std::min<int64_t>(h->a_region4 * R, h->a_used4) * 4;
-    const int64_t hi = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) * 4;
-    MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
-    MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
-    int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->ap16 : (void*)h->ap, h->peer_a,
-                           lo, hi);
-    if (rc != MMN_OK) return rc;
-  }
 
-  // ---- Muon on the main stream
+  // ---- Muon on the work stream, chunk by chunk
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[3], s));
   if (!h->mats.empty()) {
     MuonArgs m{};
@@ -749,9 +947,6 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
     m.g_bf16 = bf ? static_cast<const __nv_bfloat16*>(h->mg) : nullptr;
     m.vel = h->mvel;
     m.p_bf16 = h->mp16;
-    m.mats = h->d_mats;
-    m.nmat = (int)h->mats.size();
-    m.total_tiles = h->total_tiles;
     m.cls = h->d_cls_in;
     m.partials = h->d_partials;
     m.norms = h->d_norms;
@@ -763,14 +958,25 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
     m.fresh_state = h->cfg.fresh_state;
     m.apply_divides_norm = h->cfg.muon.ns_steps == 0;
     m.vec_ok = 1;  // arena bases come from cudaMalloc; offsets are 64-element aligned
-    launch_muon_momentum(m, h->ctx.num_sms, s);
-    launch_muon_norms(m, s);
-    MMN_CUDA_TRY(cudaGetLastError());
-    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
+    auto select = [&](size_t k) {
+      m.mats = h->d_mats + h->chunk_mat0[k];
+      m.nmat = h->chunk_mat0[k + 1] - h->chunk_mat0[k];
+      m.tile_begin = h->chunk_tile0[k];
+      m.total_tiles = h->chunk_tile0[k + 1] - h->chunk_tile0[k];
+    };
+    // momentum, bf16 cast and norms of chunk k
+    auto prologue = [&](size_t k) -> int {
+      select(k);
+      m.cls = h->d_cls_in;
+      launch_muon_momentum(m, h->ctx.num_sms, s);
+      launch_muon_norms(m, s);
+      MMN_CUDA_TRY(cudaGetLastError());
+      return MMN_OK;
+    };
     // The last Newton-Schulz iteration applies p -= lr*scale*O itself
     // (lib.rs:169-174); with zero iterations the update kernel does it.
     const bool fuse = h->cfg.muon.ns_steps >= 1;
-    for (size_t k = 0; k < h->classes.size(); ++k) {
+    auto newton_schulz = [&](size_t k) -> int {
       NsFused f;
       f.p = h->mp;
       f.p_bf16 = h->mp16;
@@ -779,36 +985,58 @@ static int enqueue_step(mmn_optim_t* h, float divisor) {
       if (ns_class_run(h->classes[k], h->cfg.muon.ns_steps, h->cfg.ns_mode, h->ctx.status,
                        h->ctx.num_sms, s, &err, fuse ? &f : nullptr, skip) < 0)
         return fail(MMN_E_CUDA, err);
-      if (h->n_peers && fuse) {
+      if (!fuse) {
+        select(k);
+        m.cls = h->d_cls_out;
+        launch_muon_apply(m, h->ctx.num_sms, s);
+        MMN_CUDA_TRY(cudaGetLastError());
+      }
+      if (h->n_peers || io) MMN_CUDA_TRY(cudaEventRecord(h->chunk_ev[k], s));
+      if (h->n_peers) {
         // the chunk's parameters are final: copy engines push them over NVLink
         // while the next chunk computes
-        MMN_CUDA_TRY(cudaEventRecord(h->chunk_ev[k], s));
         MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->chunk_ev[k], 0));
-        int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
-                               h->peer_m, h->chunk_begin[k], h->chunk_end[k]);
-        if (rc != MMN_OK) return rc;
+        MMN_TRY_RC(copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
+                                 h->peer_m, h->chunk_begin[k], h->chunk_end[k]));
       }
+      return MMN_OK;
+    };
+    if (io) {
+      for (size_t j = 0; j < h->jobs.size(); ++j) {
+        if (h->jobs[j] < 0) continue;
+        MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->h2d_ev[j], 0));
+        MMN_TRY_RC(prologue(h->jobs[j]));
+        MMN_TRY_RC(newton_schulz(h->jobs[j]));
+      }
+    } else {
+      for (int k : h->jobs)
+        if (k >= 0) MMN_TRY_RC(prologue(k));
+      if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
+      for (int k : h->jobs)
+        if (k >= 0) MMN_TRY_RC(newton_schulz(k));
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
-    if (!fuse) {
-      m.cls = h->d_cls_out;
-      launch_muon_apply(m, h->ctx.num_sms, s);
-      MMN_CUDA_TRY(cudaGetLastError());
-      if (h->n_peers && !h->chunk_ev.empty()) {
-        MMN_CUDA_TRY(cudaEventRecord(h->chunk_ev[0], s));
-        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->chunk_ev[0], 0));
-        for (size_t k = 0; k < h->chunk_begin.size(); ++k) {
-          int rc = copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
-                                 h->peer_m, h->chunk_begin[k], h->chunk_end[k]);
-          if (rc != MMN_OK) return rc;
-        }
-      }
-    }
   } else if (tm) {
     MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
     MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
   }
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[6], s));
+
+  // ---- params out (host steps), job by job, queued after all compute so that
+  // a copy into pageable memory, which blocks the host, cannot hold back a launch
+  if (io) {
+    for (int job : h->jobs) {
+      if (job >= 0) {
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->d2h, h->chunk_ev[job], 0));
+        for (int i : h->chunk_slots[job]) MMN_TRY_RC(param_out(h, io, i, 0, h->slots[i].numel));
+      } else {
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->d2h, h->apart_ev[-1 - job], 0));
+        for (const auto& pc : h->apart_pieces[-1 - job]) MMN_TRY_RC(param_out(h, io, pc.slot, pc.lo, pc.hi));
+      }
+    }
+    MMN_CUDA_TRY(cudaEventRecord(h->d2h_done, h->d2h));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->d2h_done, 0));
+  }
   MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->join, 0));
   if (h->n_peers) {
     MMN_CUDA_TRY(cudaEventRecord(h->xfer_done, h->xfer));
@@ -841,7 +1069,7 @@ extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
   int rc = MMN_OK;
   if (!h->cfg.use_graph || h->timing) {
-    rc = enqueue_step(h, grad_divisor);
+    rc = enqueue_step(h, grad_divisor, nullptr);
   } else {
     if (h->graph && h->graph_divisor != grad_divisor) {
       cudaGraphExecDestroy(h->graph);
@@ -850,7 +1078,7 @@ extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
     if (!h->graph) {
       cudaGraph_t graph = nullptr;
       MMN_CUDA_TRY(cudaStreamBeginCapture(h->work, cudaStreamCaptureModeThreadLocal));
-      rc = enqueue_step(h, grad_divisor);
+      rc = enqueue_step(h, grad_divisor, nullptr);
       cudaError_t e = cudaStreamEndCapture(h->work, &graph);
       if (rc != MMN_OK) {
         if (graph) cudaGraphDestroy(graph);
@@ -867,6 +1095,30 @@ extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
   MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->work));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->ctx.stream, h->out_ev, 0));
   return rc;
+}
+
+extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
+                                   float* const* params, float grad_divisor) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
+  if (!grads || !params) return fail(MMN_E_INVALID, "grads and params must be slot arrays");
+  if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
+  HostIO io{grads, params};
+  const int rc = enqueue_step(h, grad_divisor, &io);
+  // join the copy streams back even after an enqueue error, so that nothing
+  // still in flight outlives the call unordered
+  MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->h2d));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->out_ev, 0));
+  MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->d2h));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->out_ev, 0));
+  MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->work));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->ctx.stream, h->out_ev, 0));
+  if (rc != MMN_OK) return rc;
+  MMN_CUDA_TRY(cudaEventSynchronize(h->out_ev));
+  return h->ctx.check_status();
 }
 
 extern "C" int mmn_optim_sync(mmn_optim_t* h) {
@@ -986,17 +1238,6 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     return code;
   };
   if (rc != MMN_OK) return undo(rc);
-  if (!h->xfer) {
-    cudaError_t e = cudaStreamCreateWithFlags(&h->xfer, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->adamw_ev, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->xfer_done, cudaEventDisableTiming);
-    for (size_t k = h->chunk_ev.size(); e == cudaSuccess && k < h->chunk_begin.size(); ++k) {
-      cudaEvent_t ev = nullptr;
-      e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-      if (e == cudaSuccess) h->chunk_ev.push_back(ev);
-    }
-    if (e != cudaSuccess) return undo(cuda_fail(e, "transfer stream setup"));
-  }
   h->peer_maps = maps;
   h->n_peers = n_peers;
   for (int k = 0; k < n_peers; ++k) {

@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
   const float mu = a.momentum;
   const float one_m = __fsub_rn(1.0f, mu);
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
-  for (int t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
+  for (int t = a.tile_begin + blockIdx.x; t < a.tile_begin + a.total_tiles; t += gridDim.x) {
     const int k = find_mat(a.mats, a.nmat, t);
     const MuonMat mm = a.mats[k];
     const int tiles_c = (mm.cols + kTile - 1) / kTile;
@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   if (a.skip && *a.skip) return;
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
-  for (int t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
+  for (int t = a.tile_begin + blockIdx.x; t < a.tile_begin + a.total_tiles; t += gridDim.x) {
     const int k = find_mat(a.mats, a.nmat, t);
     const MuonMat mm = a.mats[k];
     const int tiles_c = (mm.cols + kTile - 1) / kTile;

@@ -67,9 +67,10 @@ struct MuonArgs {
   const __nv_bfloat16* g_bf16;
   float* vel;
   __nv_bfloat16* p_bf16;
-  const MuonMat* mats;
+  const MuonMat* mats;   // the matrices of this launch (a contiguous run of the table)
   int nmat;
-  int total_tiles;
+  int tile_begin;        // mats[0].tile0: the launch covers tiles
+  int total_tiles;       // [tile_begin, tile_begin + total_tiles)
   const MuonClassPtr* cls;
   float* partials;      // one fp32 sum of squares per tile
   float* norms;         // clamped Frobenius norms, slot mats[k].norm_idx

@@ -107,6 +107,23 @@ def step_config_for(train: TrainConfig, **overrides) -> StepConfig:
     return cfg
 
 
+def _host_ptr(buf, numel: int, itemsize: int, what: str, slot: int, writable: bool = False):
+    """Address of a contiguous host buffer of numel items of itemsize bytes
+    (numpy array or CPU torch tensor), or None for a None entry."""
+    if buf is None:
+        return None
+    if isinstance(buf, np.ndarray):
+        ok = buf.flags.c_contiguous and (buf.flags.writeable or not writable)
+        size, isz, ptr = buf.size, buf.itemsize, buf.ctypes.data
+    else:  # torch tensor
+        ok = (not buf.is_cuda) and buf.is_contiguous()
+        size, isz, ptr = buf.numel(), buf.element_size(), buf.data_ptr()
+    if not ok or size != numel or isz != itemsize:
+        raise ValueError(f"{what} {slot}: need a contiguous host buffer of {numel} items of "
+                         f"{itemsize} bytes")
+    return ptr
+
+
 class OptimizerStep:
     """Whole-model optimizer step on one GPU (or one rank's shard of it)."""
 
@@ -193,6 +210,23 @@ class OptimizerStep:
     # -- stepping ------------------------------------------------------------------
     def step(self, grad_divisor: float = 1.0) -> None:
         N.check(N.lib().mmn_optim_step(self._h, grad_divisor))
+
+    def step_host(self, grads, params, grad_divisor: float = 1.0) -> None:
+        """One step from host memory (mmn_optim_step_host): grads[slot] are copied
+        in, params[slot] receive the updated fp32 values. Entries are numpy arrays
+        or CPU torch tensors (pinned ones let the copies overlap the compute), or
+        None to skip that slot's copy. Returns when params hold the result."""
+        n = len(self.shapes)
+        if len(grads) != n or len(params) != n:
+            raise ValueError(f"need {n} grads and {n} params (one per slot)")
+        gsz = 2 if self.config.grad_dtype == "bf16" else 4
+        gp = (ctypes.c_void_p * n)()
+        pp = (ctypes.c_void_p * n)()
+        for k in range(n):
+            numel = int(np.prod(self.shapes[k], dtype=np.int64))
+            gp[k] = _host_ptr(grads[k], numel, gsz, "grad", k)
+            pp[k] = _host_ptr(params[k], numel, 4, "param", k, writable=True)
+        N.check(N.lib().mmn_optim_step_host(self._h, gp, pp, grad_divisor))
 
     def sync(self) -> None:
         N.check(N.lib().mmn_optim_sync(self._h))

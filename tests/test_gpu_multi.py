@@ -30,6 +30,45 @@ def _fill(step, model, seed):
         step.grad(k).normal_(0, 1e-3, generator=gen)
 
 
+def _host_grads(model, it):
+    rng = np.random.default_rng(100 + it)
+    return [rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3) for _, s, _ in model]
+
+
+def _host_worker(rank, world, step, model, mmn, q):
+    """Each rank steps its shard from host grads and writes back only what it
+    stepped; the single-GPU step from the same host grads (run here, on this
+    rank's GPU) must agree on every element written, and the device arenas,
+    completed by the exchange, must agree everywhere."""
+    import torch
+
+    single = mmn.OptimizerStep(model, mmn.StepConfig(use_graph=False), device=rank,
+                               stream=torch.cuda.current_stream(rank).cuda_stream)
+    _fill(single, model, 0)
+    step.connect_peers()
+    written = 0
+    for it in range(2):
+        grads = _host_grads(model, it)
+        outs = [np.full(s, np.nan, np.float32) for _, s, _ in model]
+        step.step_host(grads, outs)
+        step.exchange_fence()
+        want = [np.empty(s, np.float32) for _, s, _ in model]
+        single.step_host(grads, want)
+        for k in range(len(model)):
+            hit = ~np.isnan(outs[k])
+            np.testing.assert_array_equal(outs[k][hit].view(np.uint32), want[k][hit].view(np.uint32),
+                                          err_msg=f"rank {rank} step {it} slot {k}")
+            if it == 1:
+                written += int(hit.sum())
+    step.sync()
+    torch.cuda.synchronize()
+    for k in range(len(model)):
+        np.testing.assert_array_equal(step.param(k).cpu().numpy().view(np.uint32),
+                                      want[k].view(np.uint32), err_msg=f"rank {rank} arena slot {k}")
+    single.close()
+    q.put((rank, written))
+
+
 def _worker(rank, world, port, q, exchange):
     import sys
 
@@ -53,6 +92,14 @@ def _worker(rank, world, port, q, exchange):
         step = mmn.OptimizerStep(model, cfg, device=rank,
                                  stream=torch.cuda.current_stream(rank).cuda_stream)
         _fill(step, model, 0)
+        if exchange == "host":
+            try:
+                _host_worker(rank, world, step, model, mmn, q)
+            except Exception as e:  # reported to the parent, which fails at once
+                q.put((rank, f"{type(e).__name__}: {e}"))
+                raise
+            step.close()
+            return
         if exchange == "fused":
             step.connect_peers()
         for _ in range(2):
@@ -74,7 +121,7 @@ def _worker(rank, world, port, q, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "fused"])
+@pytest.mark.parametrize("exchange", ["nccl", "fused", "host"])
 def test_sharded_step_equals_single_gpu(mmn, exchange):
     import torch
     import torch.multiprocessing as mp
@@ -83,6 +130,9 @@ def test_sharded_step_equals_single_gpu(mmn, exchange):
     if world < 2:
         pytest.skip("needs two or more GPUs")
     model = _model()
+    if exchange == "host":
+        _run_host(model, world)
+        return
     single = mmn.OptimizerStep(model, mmn.StepConfig(use_graph=False), device=0)
     _fill(single, model, 0)
     single.step()
@@ -105,3 +155,29 @@ def test_sharded_step_equals_single_gpu(mmn, exchange):
         assert p.exitcode == 0
     for k, (a, b) in enumerate(zip(got, want)):
         np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32), err_msg=str(k))
+
+
+def _spawn(world, exchange):
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
+    for p in procs:
+        p.start()
+    return procs, q
+
+
+def _run_host(model, world):
+    procs, q = _spawn(world, "host")
+    got = dict(q.get(timeout=900) for _ in range(world))
+    bad = {r: v for r, v in got.items() if not isinstance(v, int)}
+    assert not bad, bad
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # every element was written back by exactly one rank (outputs are NaN-filled)
+    assert sum(got.values()) == sum(int(np.prod(s)) for _, s, _ in model)
