@@ -94,12 +94,14 @@ std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
   if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, batch, c.ld_a, 64)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, batch, c.ld_a, 64)).empty()) return err;
   return "";
 }
 
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
 cudaError_t set_smem() {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI == kEpiPolyDualT>;
   return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
 }
@@ -107,7 +109,7 @@ cudaError_t set_smem() {
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
 cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
                    const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI == kEpiPolyDualT>;
   if (args.num_tiles <= 0) return cudaSuccess;
   if (!PAIR) {
     const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
@@ -157,6 +159,7 @@ std::string ns_gemm_setup() {
   MMN_SET(128, true, true, kEpiPolyDual)
   MMN_SET(256, false, true, kEpiPolySingle)
 #undef MMN_SET
+  if (e == cudaSuccess) e = set_smem<128, true, false, kEpiPolyDualT, true>();
   if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
   return get_encode();
 }
@@ -280,6 +283,14 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
   // Two accumulators of 128 columns, double-buffered in TMEM. Measured against
   // 256-column dual tiles (single-buffered TMEM) and a stacked A|A2 pair that
   // swaps accumulator halves through shared memory, this shape was fastest.
+  if (PAIR) {
+    // transposed: 256 columns of X by 128 rows of A / A2 per tile
+    g.tiles_n = (c.n + 127) / 128;
+    g.tiles_per_matrix = ((c.m + 255) / 256) * g.tiles_n;
+    g.num_tiles = g.tiles_per_matrix * c.batch;
+    return launch<128, true, false, kEpiPolyDualT, true>(c.tm_x_mn[cur], c.tm_a2_n, c.tm_a_n, g,
+                                                         num_sms, stream);
+  }
   g.tiles_n = (c.m + 127) / 128;
   g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
   g.num_tiles = g.tiles_per_matrix * c.batch;

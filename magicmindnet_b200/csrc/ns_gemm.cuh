@@ -10,7 +10,14 @@
 //   Poly   : X'  = bf16((X/s)*a + (b*(A X) + c*(A2 X))/s)   M=n, N=m, K=n
 //            two TMEM accumulators share each X tile, so the reference's fp32
 //            B = b*A + c*A2 never has to be rounded to feed the tensor cores
-//            (bf16 mode: X' = bf16((X/s)*a + (Bm X)/s), one accumulator)
+//            (bf16 mode: X' = bf16((X/s)*a + (Bm X)/s), one accumulator).
+//            On CTA pairs the product is computed transposed, X'^T = X^T [A | A2]
+//            (A and A2 are symmetric): X^T is the MN-major A operand (a
+//            256-column strip of X), and 64 rows of A stacked on the same 64
+//            rows of A2 form each CTA's half of one N = 256 K-major B operand,
+//            so both accumulators come from one MMA per K step and sit side by
+//            side in TMEM. A stage holds 32 KB per 512 tensor clocks instead of
+//            40 KB, with half the MMA instructions.
 //
 // s is the per-matrix Frobenius norm in the first iteration (lib.rs:109-110)
 // and 1 afterwards. All operand values are exactly bf16, so the tensor-core
@@ -38,6 +45,7 @@ enum NsEpilogue : int {
   kEpiSquareBf16 = 2,
   kEpiPolyDual = 3,
   kEpiPolySingle = 4,
+  kEpiPolyDualT = 5,  // PolyDual computed as X'^T = X^T [A | A2] (pairs only)
 };
 
 constexpr int kBM = 128;  // rows per CTA (TMEM lanes)
@@ -71,14 +79,16 @@ struct NsGemmArgs {
   const int* skip;           // device non-finite flag: when set the launch does nothing
 };
 
-template <int BN, bool DUAL, bool B_MN, bool PAIR>
+// SWAP: one A operand (X^T, MN-major) and two B operands (A and A2 rows).
+template <int BN, bool DUAL, bool B_MN, bool PAIR, bool SWAP = false>
 struct NsGemmShape {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kTileM = kBM * kCtas;        // output rows per tile
   static constexpr int kBNc = BN / kCtas;           // B columns loaded by one CTA
   static constexpr int kABytes = kBM * kBK * 2;     // 16 KB per A operand
   static constexpr int kBBytes = kBNc * kBK * 2;
-  static constexpr int kStageBytes = kABytes * (DUAL ? 2 : 1) + kBBytes;
+  static constexpr int kStageBytes =
+      SWAP ? kABytes + 2 * kBBytes : kABytes * (DUAL ? 2 : 1) + kBBytes;
   static constexpr int kStages = (204800 / kStageBytes) < 8 ? (204800 / kStageBytes) : 8;
   static constexpr int kAccCols = BN * (DUAL ? 2 : 1);  // per accumulator buffer
   // two accumulator buffers when they fit in TMEM's 512 columns, else one
@@ -87,11 +97,14 @@ struct NsGemmShape {
   static constexpr int kTmemCols = kAccBufs * kAccCols;
   static constexpr int kBarBytes = 1024;
   static constexpr int kEpiStride = 40;  // bf16 per staging row: 80 B keeps v4 reads conflict-free
-  static constexpr int kEpiBytes = 4 * 32 * kEpiStride * 2;
+  // per epilogue warp: a 32 x 32 bf16 tile at stride kEpiStride, or (SWAP) a
+  // 32 x 33 fp32 tile that turns lane-per-column values into lane-per-row ones
+  static constexpr int kEpiBytes = SWAP ? 4 * 32 * 33 * 4 : 4 * 32 * kEpiStride * 2;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiBytes + 1024;
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kStages >= 2, "pipeline needs two stages");
   static_assert(!B_MN || kBNc % 64 == 0, "MN-major B is loaded in 64-column boxes");
+  static_assert(!SWAP || (DUAL && !B_MN && PAIR && kBNc == 64), "transposed Poly: pairs, dual");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
@@ -215,7 +228,8 @@ __global__ void __launch_bounds__(192, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR>;
+  constexpr bool kSwap = EPI == kEpiPolyDualT;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, kSwap>;
   constexpr int STAGES = S::kStages;
   constexpr bool kSym = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -311,7 +325,15 @@ __global__ void __launch_bounds__(192, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], S::kStageBytes * S::kCtas);
           const int k0 = kb * kBK;
           uint8_t* sb = st + S::kABytes * (DUAL ? 2 : 1);
-          if (PAIR) {
+          if (kSwap) {
+            // A side: X^T rows row0.. = X columns, two 64-column MN-major boxes;
+            // B side: rows col0.. of A (tm_b) and of A2 (tm_a2), K-major.
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_3d_pair(st, &tm_a1, fb, row0, k0, b);
+            tma_load_3d_pair(st + kBK * 128, &tm_a1, fb, row0 + 64, k0, b);
+            tma_load_3d_pair(st + S::kABytes, &tm_b, fb, k0, col0, b);
+            tma_load_3d_pair(st + S::kABytes + S::kBBytes, &tm_a2, fb, k0, col0, b);
+          } else if (PAIR) {
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             tma_load_3d_pair(st, &tm_a1, fb, k0, row0, b);
             if (DUAL) tma_load_3d_pair(st + S::kABytes, &tm_a2, fb, k0, row0, b);
@@ -360,7 +382,8 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = umma_idesc_bf16(S::kTileM, BN, false, B_MN);
+      // (transposed Poly: one N = 2*BN MMA over the stacked [A rows | A2 rows])
+      constexpr uint32_t idesc = umma_idesc_bf16(S::kTileM, kSwap ? 2 * BN : BN, kSwap, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -381,8 +404,21 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a1 = smem_u32(tiles + stage * S::kStageBytes);
           const uint32_t a2 = a1 + S::kABytes;
           const uint32_t bb = a1 + S::kABytes * (DUAL ? 2 : 1);
+          if (kSwap) {
+            // The CTA's A box and A2 box lie back to back: one 128-row K-major B
+            // operand per CTA, 256 rows for the pair. Accumulator columns:
+            // [A X | A2 X] for the leader's 64 rows of A, then the same for the
+            // peer's 64 rows.
+            const uint32_t b1 = a1 + S::kABytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t da = umma_desc_sw128(a1 + kk * 2048, kBK * 128, 1024);
+              const uint64_t db = umma_desc_sw128(b1 + kk * 32, 16, 1024);
+              tc_mma_bf16_pair(d1, da, db, idesc, (kb | kk) != 0);
+            }
+          }
+#pragma unroll
+          for (int kk = 0; kk < (kSwap ? 0 : kBK / 16); ++kk) {
             const uint64_t da1 = umma_desc_sw128(a1 + kk * 32, 16, 1024);
             const uint64_t db = B_MN ? umma_desc_sw128(bb + kk * 2048, kBK * 128, 1024)
                                      : umma_desc_sw128(bb + kk * 32, 16, 1024);
@@ -452,17 +488,28 @@ __global__ void __launch_bounds__(192, 1)
       const float s = args.norms ? args.norms[b] : 1.0f;
       __nv_bfloat16* out = args.out + (long long)b * args.out_bstride;
       const __nv_bfloat16* aux = args.aux ? args.aux + (long long)b * args.aux_bstride : nullptr;
-      const bool row_ok = r < args.M;
-      const bool rows_full = rw + 32 <= args.M;
+      // (transposed Poly: the TMEM lanes run along X' columns, the
+      // accumulator columns along X' rows)
+      const int lane_dim = kSwap ? args.N : args.M, col_dim = kSwap ? args.M : args.N;
+      const bool row_ok = r < lane_dim;
+      const bool rows_full = rw + 32 <= lane_dim;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int c0 = tn * BN + ch * 32;
-        if (c0 >= args.N) break;  // whole chunk beyond the matrix (uniform over the warp)
-        const bool cols_full = c0 + 32 <= args.N;
+        if (c0 >= col_dim) break;  // whole chunk beyond the matrix (uniform over the warp)
+        const bool cols_full = c0 + 32 <= col_dim;
         float v[32];
-        tmem_ld_32x32b_x32(tbase + ch * 32, v);
         float w[32];
-        if (DUAL) tmem_ld_32x32b_x32(tbase + BN + ch * 32, w);
+        if (kSwap) {
+          // rows tn*BN + ch*32 .. +31 of A X at column (ch/2)*128 + (ch%2)*32,
+          // of A2 X 64 columns further
+          const uint32_t col = (uint32_t)((ch >> 1) * 128 + (ch & 1) * 32);
+          tmem_ld_32x32b_x32(tbase + col, v);
+          tmem_ld_32x32b_x32(tbase + col + 64, w);
+        } else {
+          tmem_ld_32x32b_x32(tbase + ch * 32, v);
+          if (DUAL) tmem_ld_32x32b_x32(tbase + BN + ch * 32, w);
+        }
         tmem_ld_wait();
         if (kSym) {
           // This tile owns the symmetric entries with col >= row and writes each
@@ -520,7 +567,22 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (DUAL) v[j] = __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j]));
-          poly_finish(args, b, r, c0, row_ok, cols_full, s, v);
+          if (kSwap) {
+            // v[j] is X' element (c0 + j, r): transpose the warp's 32 x 32 block
+            // through shared memory so that lane L holds row c0 + L, columns
+            // rw .. rw + 31, and finish it like the row-major Poly.
+            float* tst = reinterpret_cast<float*>(epi_stage) + (warp - 2) * 32 * 33;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) tst[j * 33 + lane] = v[j];
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = tst[lane * 33 + j];
+            __syncwarp();
+            const int xr = c0 + lane;
+            poly_finish(args, b, xr, rw, xr < args.M, rw + 32 <= args.N, s, v);
+          } else {
+            poly_finish(args, b, r, c0, row_ok, cols_full, s, v);
+          }
         }
       }
       tc_fence_before();
