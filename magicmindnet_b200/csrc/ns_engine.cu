@@ -113,11 +113,12 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
   if (args.num_tiles <= 0) return cudaSuccess;
   if (!PAIR) {
     const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
-    ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR><<<grid, 192, S::kSmemBytes, stream>>>(a1, a2, b, args);
+    ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR><<<grid, S::kThreads, S::kSmemBytes, stream>>>(a1, a2,
+                                                                                       b, args);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(S::kThreads, 1, 1);
   cfg.dynamicSmemBytes = S::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

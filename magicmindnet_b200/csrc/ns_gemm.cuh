@@ -25,8 +25,9 @@
 // In the last iteration the Poly epilogue can apply the Muon update
 // p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
-// Roles (192 threads per CTA): warp 0 issues TMA loads, warp 1 owns TMEM and
-// one lane issues tcgen05.mma, warps 2-5 drain TMEM and run the epilogue.
+// Roles: warp 0 issues TMA loads, warp 1 owns TMEM and one lane issues
+// tcgen05.mma, warps 2-5 (2-9 for the transposed Poly, whose epilogue reads and
+// writes the most per MMA cycle) drain TMEM and run the epilogue.
 // PAIR=true runs one 256-row tile on a CTA pair (cluster of 2, cta_group::2):
 // each CTA loads its 128 rows of A and half of B's columns, the leader CTA
 // issues the MMAs for both and commits to both CTAs' barriers. No TMA load
@@ -99,7 +100,12 @@ struct NsGemmShape {
   static constexpr int kEpiStride = 40;  // bf16 per staging row: 80 B keeps v4 reads conflict-free
   // per epilogue warp: a 32 x 32 bf16 tile at stride kEpiStride, or (SWAP) a
   // 32 x 33 fp32 tile that turns lane-per-column values into lane-per-row ones
-  static constexpr int kEpiBytes = SWAP ? 4 * 32 * 33 * 4 : 4 * 32 * kEpiStride * 2;
+  // The transposed Poly runs eight epilogue warps (two per TMEM lane quarter,
+  // each taking half of a tile's column chunks), the others four.
+  static constexpr int kEpiWarps = SWAP ? 8 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kEpiBytes =
+      kEpiWarps * (SWAP ? 32 * 33 * 4 : 32 * kEpiStride * 2);
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiBytes + 1024;
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kStages >= 2, "pipeline needs two stages");
@@ -224,7 +230,7 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
 }
 
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
@@ -264,7 +270,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128 * S::kCtas);
+      mbar_init(&tempty[b], 32 * S::kEpiWarps * S::kCtas);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -470,6 +476,9 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
+    // column chunks of a tile this warp finishes: [ch_lo, ch_hi)
+    constexpr int kChunksPerWarp = (BN / 32) / (S::kEpiWarps / 4);
+    const int ch_lo = ((warp - 2) >> 2) * kChunksPerWarp, ch_hi = ch_lo + kChunksPerWarp;
     __nv_bfloat16* stg = epi_stage + (warp - 2) * 32 * S::kEpiStride;
     const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
@@ -477,6 +486,26 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = group; tile < args.num_tiles; tile += groups) {
       int b, tm, tn;
       decode(tile, b, tm, tn);
+      if (kSwap && args.p) {
+        // Last iteration: the epilogue reads and writes the fp32 parameters,
+        // which sit in DRAM. Their lines for this tile go to L2 while the MMAs
+        // still run (one 128-byte line per lane and chunk).
+        const NsApply ap = args.apply[b];
+        const int rw0 = tm * S::kTileM + (int)rank * kBM + sub * 32;
+#pragma unroll
+        for (int ch = ch_lo; ch < ch_hi; ++ch) {
+          const int n0 = tn * BN + ch * 32;
+          if (!ap.transposed) {
+            const int n = n0 + lane;
+            if (n < args.M && rw0 < args.N)
+              prefetch_l2(args.p + ap.off + (long long)n * args.N + rw0);
+          } else {
+            const int m = rw0 + lane;
+            if (m < args.N && n0 < args.M)
+              prefetch_l2(args.p + ap.off + (long long)m * args.M + n0);
+          }
+        }
+      }
       // tcgen05.ld is warp-collective: the warp proceeds only if every lane saw
       // the accumulator become ready.
       const bool ready = mbar_wait(&tfull[acc], acc_phase, abort_flag);
@@ -494,7 +523,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool row_ok = r < lane_dim;
       const bool rows_full = rw + 32 <= lane_dim;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int ch = ch_lo; ch < ch_hi; ++ch) {
         const int c0 = tn * BN + ch * 32;
         if (c0 >= col_dim) break;  // whole chunk beyond the matrix (uniform over the warp)
         const bool cols_full = c0 + 32 <= col_dim;
