@@ -88,6 +88,9 @@ WORKLOADS = {
     "ns_probe": dict(model=lambda: [(f"ffn{i}", (2048, 8192), "muon") for i in range(8)],
                      grad="f32", desc="Newton-Schulz on 8 x [2048,8192] (profiling case: "
                                       "X is 268 MB, larger than L2; about 1.5 GB on the device)"),
+    "ns_probe_sq": dict(model=lambda: [(f"sq{i}", (2048, 2048), "muon") for i in range(32)],
+                        grad="f32", desc="Newton-Schulz on 32 x [2048,2048] (profiling case: "
+                                         "X is 268 MB, larger than L2; about 1.5 GB on the device)"),
 }
 
 

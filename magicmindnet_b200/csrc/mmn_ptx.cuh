@@ -101,6 +101,36 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* desc, ui
       : "memory");
 }
 
+// 3-D tiled store from this CTA's shared memory (bulk-group completion). x
+// follows the same 16-byte rule as the loads; a box reaching past the tensor's
+// extent is clipped. The writes to `smem_src` must be made visible to the async
+// proxy first (fence_proxy_async_smem by every writer, then a barrier).
+__device__ __forceinline__ void tma_store_3d(const void* desc, const void* smem_src, int x, int y,
+                                             int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(smem_src)), "r"(x), "r"(y),
+               "r"(z)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// The committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// The committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // 3-D tiled load for a CTA pair (cta_group::2): the data lands in this CTA's
 // shared memory and the completion is signalled on `bar_cluster`, a
 // shared::cluster address that may be the peer CTA's barrier. No multicast.

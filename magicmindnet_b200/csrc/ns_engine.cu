@@ -41,6 +41,21 @@ std::string encode_3d(CUtensorMap* map, const void* base, int inner, int rows, i
   return "";
 }
 
+// 3-D bf16 map for TMA stores of 32 x 32 blocks (unswizzled, row-major stage).
+std::string encode_3d_store(CUtensorMap* map, const void* base, int inner, int rows, int batch,
+                            int ld) {
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+  return "";
+}
+
 int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
 // Tiles of an n x n symmetric output that touch the upper triangle, for
@@ -96,12 +111,14 @@ std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
   if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, batch, c.ld_a, 64)).empty()) return err;
   if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, batch, c.ld_a, 64)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a_out, c.a, n, n, batch, c.ld_a)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a2_out, c.a2, n, n, batch, c.ld_a)).empty()) return err;
   return "";
 }
 
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
 cudaError_t set_smem() {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI == kEpiPolyDualT>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
   return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
 }
@@ -109,7 +126,7 @@ cudaError_t set_smem() {
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
 cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
                    const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI == kEpiPolyDualT>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
   if (args.num_tiles <= 0) return cudaSuccess;
   if (!PAIR) {
     const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
@@ -239,7 +256,7 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
   // B is the same X rows: 128 rows per CTA of a pair, 256 for a single CTA.
   const CUtensorMap& xb = PAIR ? c.tm_x_a[cur] : c.tm_x_b[cur];
   cudaError_t e =
-      launch<256, false, false, kEpiGram, PAIR>(c.tm_x_a[cur], c.tm_x_a[cur], xb, g, num_sms, stream);
+      launch<256, false, false, kEpiGram, PAIR>(c.tm_x_a[cur], c.tm_a_out, xb, g, num_sms, stream);
   if (e != cudaSuccess) return e;
 
   // A2 = bf16(A A)   or   Bm = bf16(b*A + c*bf16(A A))
@@ -251,9 +268,10 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
     g.aux = c.a;
     g.aux_bstride = (long long)c.n * c.ld_a;
     g.aux_ld = c.ld_a;
-    e = launch<256, false, false, kEpiSquareBf16, PAIR>(c.tm_a_a, c.tm_a_a, ab, g, num_sms, stream);
+    e = launch<256, false, false, kEpiSquareBf16, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
+                                                       stream);
   } else {
-    e = launch<256, false, false, kEpiSquare, PAIR>(c.tm_a_a, c.tm_a_a, ab, g, num_sms, stream);
+    e = launch<256, false, false, kEpiSquare, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms, stream);
   }
   if (e != cudaSuccess) return e;
 

@@ -32,6 +32,7 @@ struct NsClass {
   CUtensorMap tm_x_a[2], tm_x_b[2], tm_x_mn[2];
   CUtensorMap tm_a_a, tm_a_b, tm_a2_a;
   CUtensorMap tm_a_n, tm_a2_n;  // A / A2 rows in 64-row boxes (B operands of the transposed Poly)
+  CUtensorMap tm_a_out, tm_a2_out;  // 32 x 32 store boxes of the symmetric outputs
   bool owns_memory = false;
 
   size_t x_elems() const { return (size_t)batch * n * ld_x; }

@@ -25,9 +25,8 @@
 // In the last iteration the Poly epilogue can apply the Muon update
 // p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
-// Roles: warp 0 issues TMA loads, warp 1 owns TMEM and one lane issues
-// tcgen05.mma, warps 2-5 (2-9 for the transposed Poly, whose epilogue reads and
-// writes the most per MMA cycle) drain TMEM and run the epilogue.
+// Roles (320 threads per CTA): warp 0 issues TMA loads, warp 1 owns TMEM and
+// one lane issues tcgen05.mma, warps 2-9 drain TMEM and run the epilogue.
 // PAIR=true runs one 256-row tile on a CTA pair (cluster of 2, cta_group::2):
 // each CTA loads its 128 rows of A and half of B's columns, the leader CTA
 // issues the MMAs for both and commits to both CTAs' barriers. No TMA load
@@ -80,9 +79,12 @@ struct NsGemmArgs {
   const int* skip;           // device non-finite flag: when set the launch does nothing
 };
 
-// SWAP: one A operand (X^T, MN-major) and two B operands (A and A2 rows).
-template <int BN, bool DUAL, bool B_MN, bool PAIR, bool SWAP = false>
+template <int BN, bool DUAL, bool B_MN, bool PAIR, int EPI>
 struct NsGemmShape {
+  // transposed Poly: one A operand (X^T, MN-major) and a B operand of stacked
+  // A and A2 rows
+  static constexpr bool SWAP = EPI == kEpiPolyDualT;
+  static constexpr bool SYM = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kTileM = kBM * kCtas;        // output rows per tile
   static constexpr int kBNc = BN / kCtas;           // B columns loaded by one CTA
@@ -97,15 +99,15 @@ struct NsGemmShape {
   static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
   static constexpr int kTmemCols = kAccBufs * kAccCols;
   static constexpr int kBarBytes = 1024;
-  static constexpr int kEpiStride = 40;  // bf16 per staging row: 80 B keeps v4 reads conflict-free
-  // per epilogue warp: a 32 x 32 bf16 tile at stride kEpiStride, or (SWAP) a
-  // 32 x 33 fp32 tile that turns lane-per-column values into lane-per-row ones
-  // The transposed Poly runs eight epilogue warps (two per TMEM lane quarter,
-  // each taking half of a tile's column chunks), the others four.
-  static constexpr int kEpiWarps = SWAP ? 8 : 4;
+  // Eight epilogue warps: two per TMEM lane quarter, each finishing half of a
+  // tile's column chunks, so that the epilogue keeps pace with short K loops.
+  static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  // per epilogue warp: two 32 x 32 bf16 blocks (symmetric outputs: the direct
+  // and the mirrored block for TMA stores), or (SWAP) a 32 x 33 fp32 tile that
+  // turns lane-per-column values into lane-per-row ones
   static constexpr int kEpiBytes =
-      kEpiWarps * (SWAP ? 32 * 33 * 4 : 32 * kEpiStride * 2);
+      kEpiWarps * (SWAP ? 32 * 33 * 4 : (SYM ? 2 * 32 * 32 * 2 : 0));
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiBytes + 1024;
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kStages >= 2, "pipeline needs two stages");
@@ -230,12 +232,12 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
 }
 
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
-__global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
+__global__ void __launch_bounds__(320, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
   constexpr bool kSwap = EPI == kEpiPolyDualT;
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, kSwap>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
   constexpr int STAGES = S::kStages;
   constexpr bool kSym = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a1);
-    if (DUAL) tma_prefetch_desc(&tm_a2);
+    if (DUAL || kSym) tma_prefetch_desc(&tm_a2);
     tma_prefetch_desc(&tm_b);
   }
   if (warp == 1) {
@@ -479,7 +481,8 @@ __global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
     // column chunks of a tile this warp finishes: [ch_lo, ch_hi)
     constexpr int kChunksPerWarp = (BN / 32) / (S::kEpiWarps / 4);
     const int ch_lo = ((warp - 2) >> 2) * kChunksPerWarp, ch_hi = ch_lo + kChunksPerWarp;
-    __nv_bfloat16* stg = epi_stage + (warp - 2) * 32 * S::kEpiStride;
+    // symmetric outputs: two 32 x 32 bf16 blocks per warp (direct, mirror)
+    __nv_bfloat16* stg = epi_stage + (warp - 2) * 2 * 32 * 32;
     const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -563,33 +566,36 @@ __global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
               for (int j = 0; j < 32; ++j) v[j] = __fdiv_rn(__fdiv_rn(v[j], s), s);
             }
           }
-          // direct write (r, c), c >= r
-          __nv_bfloat16* orow = out + (long long)r * args.out_ld + c0;
-          if (rows_full && cols_full && c0 >= rw + 31) {
-            store_bf16x32(orow, v);
-          } else {
+          // The warp's 32 x 32 block (rows rw.., columns c0..; c0 and rw are
+          // multiples of 32, so it lies on or above the diagonal) is staged
+          // row-major in shared memory and written by one TMA store, and its
+          // transpose, the block (c0.., rw..), by a second. A diagonal block
+          // takes its lower triangle from the mirrored values so that the
+          // output is exactly symmetric. The stores clip at the matrix edge.
+          const bool diag = c0 == rw;
+          if (lane == 0) bulk_wait_read_all();  // this warp's previous stores read their stage
+          __syncwarp();
+          uint4* drow = reinterpret_cast<uint4*>(stg + lane * 32);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (row_ok && c0 + j < args.N && c0 + j >= r) orow[j] = __float2bfloat16_rn(v[j]);
+          for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+            u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+            u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+            u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+            drow[q] = u;
           }
-          // mirror write (c, r), c > r: stage transposed, then lane L writes row c0 + L
-          if (c0 + 31 > rw) {
+          __nv_bfloat16* mir = diag ? stg : stg + 32 * 32;
+          if (diag) __syncwarp();  // the lower triangle overwrites direct values
 #pragma unroll
-            for (int j = 0; j < 32; ++j) stg[j * S::kEpiStride + lane] = __float2bfloat16_rn(v[j]);
-            __syncwarp();
-            const int c = c0 + lane;
-            const __nv_bfloat16* srow = stg + lane * S::kEpiStride;
-            __nv_bfloat16* mrow = out + (long long)c * args.out_ld + rw;
-            if (rows_full && cols_full && c0 >= rw + 32) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                *reinterpret_cast<uint4*>(mrow + q * 8) =
-                    *reinterpret_cast<const uint4*>(srow + q * 8);
-            } else if (c < args.N) {
-              for (int i = 0; i < 32; ++i)
-                if (c > rw + i && rw + i < args.M) mrow[i] = srow[i];
-            }
-            __syncwarp();
+          for (int j = 0; j < 32; ++j)
+            if (!diag || j > lane) mir[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tm_a2, stg, c0, rw, b);
+            if (!diag) tma_store_3d(&tm_a2, stg + 32 * 32, rw, c0, b);
+            bulk_commit();
           }
         } else {
           // Poly: bx = b*D1 + c*D2 (reference mode) or D (bf16 mode)
@@ -624,6 +630,8 @@ __global__ void __launch_bounds__(EPI == kEpiPolyDualT ? 320 : 192, 1)
         acc_phase ^= 1u;
       }
     }
+    // the stage must outlive the TMA stores that read it
+    if (kSym && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
