@@ -32,12 +32,13 @@ sys.path.insert(0, ROOT)
 METRIC = "hybrid AdamW+Muon step params/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes (read + write) per algorithmic Newton-Schulz flop of the three GEMM
-# kernels of one reference-mode iteration, from the ncu capture of the 8 x
-# [2048, 8192] profiling case (profiles/ns_gemm_probe_full.md): 1101.2 MB per
-# 1.2370e12 flop. Traffic grows with the flops of a class, so the per-step
-# traffic of a workload is this ratio times its Newton-Schulz flops.
-NS_DRAM_BYTES_PER_FLOP = 1101.2e6 / 1.2370e12
+# DRAM bytes (read + write) per algorithmic Newton-Schulz flop of the GEMM
+# kernels of one reference-mode optimizer step (5 iterations, the last one fused
+# with the parameter update), from the ncu capture of the 8 x [2048, 8192]
+# profiling case (profiles/ns_gemm_probe_full.md): 5763.1 MB per 6.1848e12 flop.
+# Traffic grows with the flops of a class, so the per-step traffic of a workload
+# is this ratio times its Newton-Schulz flops.
+NS_DRAM_BYTES_PER_FLOP = 5763.1e6 / 6.1848e12
 # DRAM bytes per element of the isolated AdamW kernel measured by ncu on the
 # 2^28 arena: read p, g, m, v and write p, m, v (profiles/adamw_arena.md).
 ADAMW_DRAM_BYTES_PER_PARAM = 28.0
