@@ -10,10 +10,15 @@ Workloads (synthetic, seeded; shapes from the reference model family):
   adamw_arena isolated fused AdamW over 2^28 fp32 params (t = 10, wd 0.1, divisor 4).
   ns_batch    isolated Newton-Schulz on 64 x [4096, 4096] + 32 x [4096, 14336].
   chatbot     the Chatbot(vocab 512, 2 layers, d_model 64) step (latency-bound).
+  ns_probe, ns_probe_sq
+              small profiling cases (8 x [2048, 8192], 32 x [2048, 2048]).
 
 Rank 0 prints one JSON line. Multi-GPU runs use torchrun (one process per GPU):
 Muon matrices are owned whole by one rank, the AdamW arena is split evenly, and
-the updated params are all-gathered (NCCL) inside the timed region.
+inside the timed region every rank's results reach every other rank: by default
+the step itself pushes each finished chunk into the peers' arenas over NVLink
+(--exchange fused), or NCCL all-gathers the arenas after the step (--exchange
+nccl). The e2e number steps from pinned host buffers through mmn_optim_step_host.
 """
 from __future__ import annotations
 
