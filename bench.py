@@ -235,11 +235,10 @@ def run_ours(args, rank, world, local_rank):
         adamw = mmn.AdamWConfig()
     cfg = mmn.StepConfig(adamw=adamw, muon=mmn.MuonConfig(), ns_mode=args.ns_mode,
                          grad_dtype=spec["grad"], bf16_param_shadow=is_8b, loss_scaling=is_8b,
-                         rank=rank, world_size=world, use_graph=False)
+                         rank=rank, world_size=world, use_graph=True)
     stream = torch.cuda.current_stream(dev)
     step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg, device=dev,
                              stream=stream.cuda_stream)
-    step.enable_timing(True)
     # seeded synthetic values, generated on the device
     gen = torch.Generator(device=f"cuda:{dev}").manual_seed(0)
     for k, (_, s, _) in enumerate(model):
@@ -313,9 +312,14 @@ def run_ours(args, rank, world, local_rank):
     ev1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    # per-kernel device times of the last timed step (CUDA events the library
-    # records on the streams its kernels run on)
+    # per-kernel device times from one more step, outside the timed region, with
+    # CUDA events the library records on the streams its kernels run on (the
+    # timed steps replay the captured CUDA graph, which holds no events)
+    step.enable_timing(True)
+    one_step()
+    torch.cuda.synchronize()
     phase = {k2: [v] for k2, v in step.last_timing().items()}
+    step.enable_timing(False)
     ms = ev0.elapsed_time(ev1) / args.steps
     if world > 1:
         import torch.distributed as dist
