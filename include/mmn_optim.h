@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MMN_OPTIM_ABI_VERSION 1
+#define MMN_OPTIM_ABI_VERSION 2
 
 /* status codes */
 #define MMN_OK 0
@@ -229,6 +229,10 @@ typedef struct {
     int32_t rank;             /* shard of the step this process owns (0 .. world_size-1) */
     int32_t world_size;       /* 1 = unsharded */
     int32_t use_graph;        /* 1: capture the step in a CUDA graph at first use */
+    int32_t reduce_grads;     /* 1: every rank holds its own local grads and
+                                 mmn_optim_reduce_grads sums them across ranks before
+                                 each step (data parallelism); the step then takes its
+                                 skip decision from that call instead of scanning */
 } mmn_optim_config;
 
 /* Defaults: AdamW/Muon defaults, hybrid, reference NS, persistent state, f32
@@ -339,6 +343,23 @@ int mmn_optim_plan(const int64_t *shapes, const int *ndims, const int *routes, i
 #define MMN_IPC_BLOB_BYTES 512
 int mmn_optim_export_ipc(mmn_optim_t *h, void *blob);
 int mmn_optim_connect_peers(mmn_optim_t *h, const void *blobs);
+
+/* Data-parallel grad reduction fused with the non-finite scan, over NVLink
+ * (config.reduce_grads = 1, world_size > 1, after mmn_optim_connect_peers).
+ * This is the all-reduce (or reduce-scatter) of the local grads that a
+ * data-parallel trainer runs before the optimizer step; the reference trains
+ * on one process and has none. Every rank holds its own local grads for every
+ * slot; the call makes this rank's regions (its Muon matrices and its AdamW
+ * range, all its step reads) hold the sum over ranks, accumulated in fp32 in
+ * rank order 0, 1, ..., world_size-1 (bf16 grads: the fp32 sum rounded to bf16
+ * once), by loading the peers' grads directly from their memory. Other regions
+ * keep this rank's local grads. Averaging is the step's grad_divisor. With
+ * loss_scaling, a non-finite sum anywhere sets every rank's skip flag, and the
+ * next mmn_optim_step skips on every rank without a scan. The ranks must be
+ * ordered before the call (every rank's grads final) and between the call and
+ * mmn_optim_step (every rank's loads and flags done), e.g. with one-element
+ * all-reduces on the same stream. Asynchronous. */
+int mmn_optim_reduce_grads(mmn_optim_t *h);
 
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);

@@ -212,6 +212,13 @@ struct mmn_optim {
   void* peer_a[8] = {};
   void* peer_m[8] = {};
   std::vector<void*> peer_maps;
+  // data-parallel grad reduction: every rank's grad arenas and skip flag in
+  // rank order (this rank's own at [rank]), and this rank's Muon range
+  const void* rank_ga[8] = {};
+  const void* rank_gm[8] = {};
+  int* rank_skip[8] = {};
+  bool reduce_ready = false;
+  int64_t m_own_begin = 0, m_own_end = 0;
   cudaStream_t xfer = nullptr;
   std::vector<cudaEvent_t> chunk_ev;
   cudaEvent_t adamw_ev = nullptr, xfer_done = nullptr;
@@ -264,6 +271,7 @@ extern "C" mmn_optim_config mmn_optim_config_default(void) {
   c.rank = 0;
   c.world_size = 1;
   c.use_graph = 1;
+  c.reduce_grads = 0;
   return c;
 }
 
@@ -465,6 +473,9 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
     h->ns_flops += (double)steps * (4.0 * n * (double)n * m + 2.0 * (double)n * n * n);
   }
   h->total_tiles = tiles;
+  h->m_own_begin = (int64_t)R * h->m_region;
+  h->m_own_end = h->m_own_begin;
+  for (int64_t e : h->chunk_end) h->m_own_end = std::max(h->m_own_end, align_up(e, 64));
   h->chunk_mat0.push_back((int)h->mats.size());
   h->chunk_tile0.push_back(tiles);
 
@@ -860,9 +871,10 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     MMN_CUDA_TRY(cudaEventRecord(h->h2d_ev.back(), h->h2d));
   }
 
-  if (h->cfg.loss_scaling) {
+  if (h->cfg.loss_scaling && !h->cfg.reduce_grads) {
     // Every rank scans every grad (grads are replicated), so all ranks reach
-    // the same skip decision without a collective.
+    // the same skip decision without a collective. (With reduce_grads the
+    // reduction already set the flag on every rank.)
     if (io) MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->h2d_ev.back(), 0));
     MMN_CUDA_TRY(cudaMemsetAsync(h->d_skip, 0, sizeof(int), s));
     const int64_t a_n = h->a_used4 * 4;
@@ -1045,7 +1057,8 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   StepTail t{};
   t.step_counter = h->d_step;
   t.adamw_calls = h->n_adamw;
-  t.skip = skip;
+  t.skip = h->cfg.loss_scaling ? h->d_skip : nullptr;
+  t.reset_skip = h->cfg.reduce_grads;
   t.grad_scale = h->cfg.loss_scaling ? h->d_scale : nullptr;
   t.good_steps = h->d_good;
   t.growth_interval = h->cfg.growth_interval > 0 ? h->cfg.growth_interval : 2000;
@@ -1103,6 +1116,8 @@ extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
   if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
   if (!grads || !params) return fail(MMN_E_INVALID, "grads and params must be slot arrays");
   if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
+  if (h->cfg.reduce_grads)
+    return fail(MMN_E_UNSUPPORTED, "a step from host memory takes already-reduced grads");
   DevGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
@@ -1166,7 +1181,9 @@ struct IpcBlob {
   int32_t rank, world;
   int32_t shadow;
   int64_t a_total4, m_total;
+  int32_t grad_dtype, reduce_grads;
   cudaIpcMemHandle_t ap, mp, ap16, mp16;
+  cudaIpcMemHandle_t ga, gm, skip;  // grad arenas and skip flag (reduce_grads)
 };
 static_assert(sizeof(IpcBlob) <= MMN_IPC_BLOB_BYTES, "IPC blob size");
 constexpr uint32_t kIpcMagic = 0x4D4D4E31u;  // "MMN1"
@@ -1184,11 +1201,18 @@ extern "C" int mmn_optim_export_ipc(mmn_optim_t* h, void* blob) {
   b.shadow = h->cfg.bf16_param_shadow;
   b.a_total4 = h->a_total4;
   b.m_total = h->m_total;
+  b.grad_dtype = h->cfg.grad_dtype;
+  b.reduce_grads = h->cfg.reduce_grads;
   MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ap, h->ap));
   MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.mp, h->mp));
   if (b.shadow) {
     MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ap16, h->ap16));
     MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.mp16, h->mp16));
+  }
+  if (b.reduce_grads) {
+    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ga, h->ag));
+    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.gm, h->mg));
+    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.skip, h->d_skip));
   }
   memset(blob, 0, MMN_IPC_BLOB_BYTES);
   memcpy(blob, &b, sizeof(b));
@@ -1207,6 +1231,9 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
   int n_peers = 0;
   void* peer_a[8] = {};
   void* peer_m[8] = {};
+  const void* rank_ga[8] = {};
+  const void* rank_gm[8] = {};
+  int* rank_skip[8] = {};
   std::vector<void*> maps;
   auto open = [&](const cudaIpcMemHandle_t& hd, void** out) -> int {
     cudaError_t e = cudaIpcOpenMemHandle(out, hd, cudaIpcMemLazyEnablePeerAccess);
@@ -1220,11 +1247,17 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     memcpy(&b, raw + (size_t)r * MMN_IPC_BLOB_BYTES, sizeof(b));
     if (b.magic != kIpcMagic || b.rank != r || b.world != W ||
         b.shadow != h->cfg.bf16_param_shadow || b.a_total4 != h->a_total4 ||
-        b.m_total != h->m_total) {
+        b.m_total != h->m_total || b.grad_dtype != h->cfg.grad_dtype ||
+        b.reduce_grads != h->cfg.reduce_grads) {
       rc = fail(MMN_E_INVALID, "peer blob does not match this rank's layout");
       break;
     }
-    if (r == R) continue;
+    if (r == R) {
+      rank_ga[r] = h->ag;
+      rank_gm[r] = h->mg;
+      rank_skip[r] = h->d_skip;
+      continue;
+    }
     void *ap = nullptr, *mp = nullptr;
     const bool sh = h->cfg.bf16_param_shadow;
     if ((rc = open(sh ? b.ap16 : b.ap, &ap)) != MMN_OK || (rc = open(sh ? b.mp16 : b.mp, &mp)) != MMN_OK)
@@ -1232,6 +1265,15 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     peer_a[n_peers] = ap;
     peer_m[n_peers] = mp;
     ++n_peers;
+    if (h->cfg.reduce_grads) {
+      void *ga = nullptr, *gm = nullptr, *sk = nullptr;
+      if ((rc = open(b.ga, &ga)) != MMN_OK || (rc = open(b.gm, &gm)) != MMN_OK ||
+          (rc = open(b.skip, &sk)) != MMN_OK)
+        break;
+      rank_ga[r] = ga;
+      rank_gm[r] = gm;
+      rank_skip[r] = static_cast<int*>(sk);
+    }
   }
   auto undo = [&](int code) {
     for (void* p : maps) cudaIpcCloseMemHandle(p);
@@ -1244,10 +1286,50 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     h->peer_a[k] = peer_a[k];
     h->peer_m[k] = peer_m[k];
   }
+  for (int r = 0; r < W; ++r) {
+    h->rank_ga[r] = rank_ga[r];
+    h->rank_gm[r] = rank_gm[r];
+    h->rank_skip[r] = rank_skip[r];
+  }
+  h->reduce_ready = h->cfg.reduce_grads != 0;
   if (h->graph) {  // the captured step must be re-captured with the peers
     cudaGraphExecDestroy(h->graph);
     h->graph = nullptr;
   }
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_reduce_grads(mmn_optim_t* h) {
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  if (!h->cfg.reduce_grads || h->cfg.world_size < 2)
+    return fail(MMN_E_STATE, "create the handle with reduce_grads = 1 and world_size > 1");
+  if (!h->reduce_ready) return fail(MMN_E_STATE, "connect the peers first");
+  DevGuard g(h->ctx.device);
+  const int W = h->cfg.world_size, R = h->cfg.rank;
+  MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
+  GradReduceArgs a{};
+  a.world = W;
+  a.bf16 = h->cfg.grad_dtype == MMN_DTYPE_BF16;
+  a.scan = h->cfg.loss_scaling;
+  for (int r = 0; r < W; ++r) a.skip_flags[r] = h->rank_skip[r];
+  // this rank's AdamW range
+  for (int r = 0; r < W; ++r) a.src[r] = h->rank_ga[r];
+  a.dst = h->ag;
+  a.begin = std::min<int64_t>(h->a_region4 * R, h->a_used4) * 4;
+  a.end = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) * 4;
+  launch_grad_reduce(a, h->ctx.num_sms, h->work);
+  MMN_CUDA_TRY(cudaGetLastError());
+  // this rank's Muon matrices
+  for (int r = 0; r < W; ++r) a.src[r] = h->rank_gm[r];
+  a.dst = h->mg;
+  a.begin = h->m_own_begin;
+  a.end = h->m_own_end;
+  launch_grad_reduce(a, h->ctx.num_sms, h->work);
+  MMN_CUDA_TRY(cudaGetLastError());
+  MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->work));
+  MMN_CUDA_TRY(cudaStreamWaitEvent(h->ctx.stream, h->out_ev, 0));
   return MMN_OK;
 }
 

@@ -435,6 +435,95 @@ __global__ void __launch_bounds__(256) nonfinite_kernel(const float* g32, long l
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
 }
 
+// fp32: four elements per vector; every rank's vector is loaded before the
+// rank-ordered sum, so the NVLink loads of one thread are in flight together.
+template <int W>
+__global__ void __launch_bounds__(256) grad_reduce_f32_kernel(const GradReduceArgs a) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long b4 = a.begin / 4, e4 = a.end / 4;
+  bool bad = false;
+  float4* dst = reinterpret_cast<float4*>(a.dst);
+  for (long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e4; i += stride) {
+    float4 v[W];
+#pragma unroll
+    for (int r = 0; r < W; ++r) v[r] = __ldcs(reinterpret_cast<const float4*>(a.src[r]) + i);
+    float4 s = v[0];
+#pragma unroll
+    for (int r = 1; r < W; ++r) {
+      s.x = __fadd_rn(s.x, v[r].x);
+      s.y = __fadd_rn(s.y, v[r].y);
+      s.z = __fadd_rn(s.z, v[r].z);
+      s.w = __fadd_rn(s.w, v[r].w);
+    }
+    bad |= nonfinite_bits(__float_as_uint(s.x)) | nonfinite_bits(__float_as_uint(s.y)) |
+           nonfinite_bits(__float_as_uint(s.z)) | nonfinite_bits(__float_as_uint(s.w));
+    dst[i] = s;
+  }
+  // scalar tail (end not a multiple of 4)
+  for (long long i = e4 * 4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.end;
+       i += stride) {
+    float s = reinterpret_cast<const float*>(a.src[0])[i];
+    for (int r = 1; r < W; ++r) s = __fadd_rn(s, reinterpret_cast<const float*>(a.src[r])[i]);
+    bad |= nonfinite_bits(__float_as_uint(s));
+    reinterpret_cast<float*>(a.dst)[i] = s;
+  }
+  if (__syncthreads_or(bad) && a.scan && threadIdx.x == 0) {
+    for (int r = 0; r < a.world; ++r) *(volatile int*)a.skip_flags[r] = 1;
+    __threadfence_system();
+  }
+}
+
+// bf16: eight elements per vector, summed in fp32, rounded once.
+template <int W>
+__global__ void __launch_bounds__(256) grad_reduce_bf16_kernel(const GradReduceArgs a) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long b8 = a.begin / 8, e8 = a.end / 8;
+  bool bad = false;
+  uint4* dst = reinterpret_cast<uint4*>(a.dst);
+  for (long long i = b8 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e8; i += stride) {
+    uint4 v[W];
+#pragma unroll
+    for (int r = 0; r < W; ++r) v[r] = __ldcs(reinterpret_cast<const uint4*>(a.src[r]) + i);
+    float s[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&v[0])[e]);
+      s[2 * e] = f.x;
+      s[2 * e + 1] = f.y;
+    }
+#pragma unroll
+    for (int r = 1; r < W; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&v[r])[e]);
+        s[2 * e] = __fadd_rn(s[2 * e], f.x);
+        s[2 * e + 1] = __fadd_rn(s[2 * e + 1], f.y);
+      }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(s[2 * e], s[2 * e + 1]);
+      ow[e] = *reinterpret_cast<uint32_t*>(&h);
+      bad |= ((ow[e] & 0x7F80u) == 0x7F80u) | ((ow[e] & 0x7F800000u) == 0x7F800000u);
+    }
+    dst[i] = o;
+  }
+  for (long long i = e8 * 8 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.end;
+       i += stride) {
+    float s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.src[0])[i]);
+    for (int r = 1; r < W; ++r)
+      s = __fadd_rn(s, __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.src[r])[i]));
+    const __nv_bfloat16 h = __float2bfloat16_rn(s);
+    bad |= nonfinite_bits((uint32_t)__bfloat16_as_ushort(h) << 16);
+    reinterpret_cast<__nv_bfloat16*>(a.dst)[i] = h;
+  }
+  if (__syncthreads_or(bad) && a.scan && threadIdx.x == 0) {
+    for (int r = 0; r < a.world; ++r) *(volatile int*)a.skip_flags[r] = 1;
+    __threadfence_system();
+  }
+}
+
 __global__ void step_tail_kernel(const StepTail t) {
   const bool skipped = t.skip && *t.skip;
   if (!skipped) *t.step_counter += t.adamw_calls;
@@ -448,6 +537,7 @@ __global__ void step_tail_kernel(const StepTail t) {
       *t.good_steps = 0;
     }
   }
+  if (t.reset_skip && t.skip) *t.skip = 0;
 }
 
 int grid_for(long long work_items, int threads, int num_sms, int per_sm) {
@@ -499,6 +589,29 @@ void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream) {
     muon_apply_kernel<true><<<grid, 256, 0, stream>>>(a);
   else
     muon_apply_kernel<false><<<grid, 256, 0, stream>>>(a);
+}
+
+void launch_grad_reduce(const GradReduceArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.end <= a.begin || a.world < 2 || a.world > kMaxRanks) return;
+  const long long vecs = (a.end - a.begin) / (a.bf16 ? 8 : 4) + 1;
+  const int grid = grid_for(vecs, 256, num_sms, 8);
+#define MMN_GR(W)                                                                 \
+  case W:                                                                         \
+    if (a.bf16)                                                                   \
+      grad_reduce_bf16_kernel<W><<<grid, 256, 0, stream>>>(a);                    \
+    else                                                                          \
+      grad_reduce_f32_kernel<W><<<grid, 256, 0, stream>>>(a);                     \
+    break;
+  switch (a.world) {
+    MMN_GR(2)
+    MMN_GR(3)
+    MMN_GR(4)
+    MMN_GR(5)
+    MMN_GR(6)
+    MMN_GR(7)
+    MMN_GR(8)
+  }
+#undef MMN_GR
 }
 
 void launch_nonfinite_scan(const float* g32, long long n32, const __nv_bfloat16* g16,

@@ -93,11 +93,29 @@ void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream);
 void launch_nonfinite_scan(const float* g32, long long n32, const __nv_bfloat16* g16,
                            long long n16, int* flag, int num_sms, cudaStream_t stream);
 
+// Data-parallel grad reduction over peer memory: dst[i] = src[0][i] + src[1][i]
+// + ... + src[world-1][i] for i in [begin, end), accumulated in fp32 in rank
+// order (bf16 grads: the fp32 sum rounded to bf16 once). src[rank] is this
+// rank's own arena (== dst); the others are IPC mappings of the peers' arenas.
+// With `scan`, any non-finite sum sets every rank's skip flag.
+constexpr int kMaxRanks = 8;
+struct GradReduceArgs {
+  const void* src[kMaxRanks];
+  void* dst;
+  long long begin, end;   // elements; begin is a multiple of 8
+  int world;
+  int bf16;
+  int scan;
+  int* skip_flags[kMaxRanks];  // every rank's skip flag (this rank's own at [rank])
+};
+void launch_grad_reduce(const GradReduceArgs& a, int num_sms, cudaStream_t stream);
+
 // End of step: advance the AdamW counter unless skipped; dynamic loss scale.
 struct StepTail {
   long long* step_counter;
   long long adamw_calls;  // AdamW tensors per step
-  const int* skip;
+  int* skip;
+  int reset_skip;         // clear *skip after use (grads reduced across ranks)
   float* grad_scale;      // nullptr when no loss scaling
   int* good_steps;
   int growth_interval;

@@ -71,6 +71,7 @@ class StepConfig:
     rank: int = 0
     world_size: int = 1
     use_graph: bool = True
+    reduce_grads: bool = False
 
     def c(self) -> N.OptimConfigC:
         c = N.lib().mmn_optim_config_default()
@@ -87,6 +88,7 @@ class StepConfig:
         c.rank = self.rank
         c.world_size = self.world_size
         c.use_graph = int(self.use_graph)
+        c.reduce_grads = int(self.reduce_grads)
         return c
 
 
@@ -276,6 +278,17 @@ class OptimizerStep:
         all-reduce queued on the current stream after the step."""
         import torch.distributed as dist
 
+        dist.all_reduce(self._fence, group=group)
+
+    def reduce_grads(self, group=None) -> None:
+        """Data-parallel grad reduction (mmn_optim_reduce_grads; needs
+        StepConfig(reduce_grads=True) and connect_peers): this rank's regions
+        become the rank-ordered sum of every rank's local grads, read over NVLink.
+        Fenced on both sides with one-element all-reduces, as the call requires."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._fence, group=group)
+        N.check(N.lib().mmn_optim_reduce_grads(self._h))
         dist.all_reduce(self._fence, group=group)
 
     def param_counts(self):

@@ -181,3 +181,145 @@ def _run_host(model, world):
         assert p.exitcode == 0
     # every element was written back by exactly one rank (outputs are NaN-filled)
     assert sum(got.values()) == sum(int(np.prod(s)) for _, s, _ in model)
+
+
+# ------------------------------------------------------------------ grad reduction
+def _local_grads(model, world, bf16):
+    """Every rank's local grads (rank r from seed 500 + r), generated alike on
+    every process, and their rank-ordered fp32 sum (rounded to bf16 once)."""
+    import torch
+
+    per_rank = []
+    for r in range(world):
+        gen = torch.Generator(device="cuda").manual_seed(500 + r)
+        gs = []
+        for _, s, _ in model:
+            g = torch.empty(s, device="cuda").normal_(0, 1e-3, generator=gen)
+            gs.append((g * 1024.0).bfloat16() if bf16 else g)
+        per_rank.append(gs)
+    sums = []
+    for k in range(len(model)):
+        acc = per_rank[0][k].float()
+        for r in range(1, world):
+            acc = acc + per_rank[r][k].float()
+        sums.append(acc.bfloat16() if bf16 else acc)
+    return per_rank, sums
+
+
+def _reduce_cfg(mmn, bf16, **kw):
+    if bf16:
+        return mmn.StepConfig(grad_dtype="bf16", loss_scaling=True, loss_scale_init=1024.0,
+                              use_graph=False, **kw)
+    return mmn.StepConfig(use_graph=False, **kw)
+
+
+def _reduce_worker(rank, world, port, q, bf16):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import magicmindnet_b200 as mmn
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        model = _model()
+        step = mmn.OptimizerStep(model, _reduce_cfg(mmn, bf16, rank=rank, world_size=world,
+                                                    reduce_grads=True),
+                                 device=rank, stream=torch.cuda.current_stream(rank).cuda_stream)
+        _fill(step, model, 0)
+        per_rank, _ = _local_grads(model, world, bf16)
+        for k in range(len(model)):
+            step.grad(k).copy_(per_rank[rank][k])
+        step.connect_peers()
+        step.reduce_grads()
+        step.step()
+        step.exchange_fence()
+        out = [step.param(k).cpu().numpy().copy() for k in range(len(model))]
+        skipped = None
+        if bf16:
+            # a +inf in the last rank's local grad of a matrix rank 0 owns: the
+            # sum there is +inf, so every rank skips the next step
+            plan = mmn.shard_plan(model, world)
+            k0 = next(k for k, o in enumerate(plan["owner"]) if o == 0)
+            for k in range(len(model)):
+                step.grad(k).copy_(per_rank[rank][k])
+            if rank == world - 1:
+                step.grad(k0).view(-1)[7] = float("inf")
+            before = [step.param(k).clone() for k in range(len(model))]
+            step.reduce_grads()
+            step.step()
+            step.exchange_fence()
+            torch.cuda.synchronize()
+            same = all(torch.equal(step.param(k), before[k]) for k in range(len(model)))
+            skipped = (same, step.loss_scale())
+        step.sync()
+        q.put((rank, out, skipped))
+        step.close()
+    except Exception as e:  # reported to the parent, which fails at once
+        q.put((rank, f"{type(e).__name__}: {e}", None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_reduced_grads_step_equals_single_gpu_on_summed_grads(mmn, bf16):
+    """Data parallelism end to end: each rank holds its own local grads, the
+    fused reduction sums them over NVLink in rank order, each rank steps its
+    shard and pushes it to the peers. Every rank's parameters must equal, bit
+    for bit, one GPU stepping the rank-ordered sum of the grads. With bf16 grads
+    and loss scaling, a +inf in one rank's local grads skips the step on every
+    rank and halves every rank's scale."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    model = _model()
+    single = mmn.OptimizerStep(model, _reduce_cfg(mmn, bf16), device=0)
+    _fill(single, model, 0)
+    _, sums = _local_grads(model, world, bf16)
+    for k in range(len(model)):
+        single.grad(k).copy_(sums[k])
+    single.step()
+    single.sync()
+    want = [single.param(k).cpu().numpy().copy() for k in range(len(model))]
+    scale0 = single.loss_scale()[0]
+    single.close()
+    del sums
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, q, bf16))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, out, skipped = q.get(timeout=900)
+        got[r] = (out, skipped)
+    for p in procs:
+        p.join(timeout=120)
+    for r, (out, skipped) in got.items():
+        assert not isinstance(out, str), (r, out)
+        for k, (a, b) in enumerate(zip(out, want)):
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32),
+                                          err_msg=f"rank {r} slot {k}")
+        if bf16:
+            same, (scale, nskip) = skipped
+            assert same, r
+            assert (scale, nskip) == (scale0 / 2, 1), r
+    for p in procs:
+        assert p.exitcode == 0
