@@ -233,9 +233,11 @@ def run_ours(args, rank, world, local_rank):
         adamw = mmn.AdamWConfig(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
     else:
         adamw = mmn.AdamWConfig()
+    dp = world > 1 and args.grad_reduce != "none"
     cfg = mmn.StepConfig(adamw=adamw, muon=mmn.MuonConfig(), ns_mode=args.ns_mode,
                          grad_dtype=spec["grad"], bf16_param_shadow=is_8b, loss_scaling=is_8b,
-                         rank=rank, world_size=world, use_graph=True)
+                         rank=rank, world_size=world, use_graph=True,
+                         reduce_grads=dp and args.grad_reduce == "fused")
     stream = torch.cuda.current_stream(dev)
     step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg, device=dev,
                              stream=stream.cuda_stream)
@@ -262,7 +264,8 @@ def run_ours(args, rank, world, local_rank):
 
     gl = step.gather_layout()
     gathers = []
-    fused = world > 1 and args.exchange == "fused"
+    reduces = []
+    fused = world > 1 and (args.exchange == "fused" or args.grad_reduce == "fused")
     if fused:
         # the step's own kernels store this rank's parameters into every peer
         step.connect_peers()
@@ -276,8 +279,28 @@ def run_ours(args, rank, world, local_rank):
             if ptr and gl[region]:
                 full = _view(ptr, (gl[region] * world,), "bf16" if use16 else "f32", dev)
                 gathers.append((full, full[rank * gl[region]:(rank + 1) * gl[region]]))
+    if dp and args.grad_reduce == "nccl":
+        # NCCL baseline of the grad reduction: an in-place reduce-scatter of each
+        # grad arena into this rank's region (the arenas are rank-major)
+        from magicmindnet_b200.step import _view
+
+        plan = mmn.shard_plan([(k, s, r) for k, (_, s, r) in enumerate(model)], world)
+        gdt, gsz = ("bf16", 2) if spec["grad"] == "bf16" else ("f32", 4)
+        for route, region in (("adamw", "adamw_region"), ("muon", "muon_region")):
+            ks = [k for k, (_, _, r) in enumerate(model) if r == route]
+            if ks and gl[region]:
+                base = step.grad(ks[0]).data_ptr() - plan["offset"][ks[0]] * gsz
+                full = _view(base, (gl[region] * world,), gdt, dev)
+                reduces.append((full, full[rank * gl[region]:(rank + 1) * gl[region]]))
 
     def one_step():
+        if dp and args.grad_reduce == "fused":
+            step.reduce_grads()
+        elif reduces:
+            import torch.distributed as dist
+
+            for full, mine in reduces:
+                dist.reduce_scatter_tensor(mine, full)
         step.step(divisor)
         if fused:
             step.exchange_fence()
@@ -334,7 +357,7 @@ def run_ours(args, rank, world, local_rank):
     # Each rank copies in the grads it steps and copies back the params it
     # stepped; with the peer exchange the device arenas are complete as well.
     e2e = None
-    if args.e2e:
+    if args.e2e and not dp:
         plan = mmn.shard_plan([(k, s, r) for k, (_, s, r) in enumerate(model)], world)
         areg = plan["adamw_region"]
         stepped = []  # elements of every slot this rank steps
@@ -427,7 +450,8 @@ def run_ours(args, rank, world, local_rank):
                 "traffic": ADAMW_DRAM_BYTES_PER_PARAM * a_elems_rank,
                 "traffic_unit": "DRAM bytes per launch (ncu: 28 B per param on the 2^28 arena)",
                 "algorithmic_bytes": a_bytes_per * a_elems_rank}
-    launches_per_step = 5 + 15 * len({(min(s), max(s)) for _, s, r in model if r == "muon"})
+    per_step, per_reduce = step.kernel_launches()
+    launches_per_step = per_step + (per_reduce if dp and args.grad_reduce == "fused" else 0)
     line = {
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -440,6 +464,11 @@ def run_ours(args, rank, world, local_rank):
                    "exchange": ("copy-engine pushes over NVLink per chunk + 1-element all-reduce fence"
                                 if fused else
                                 "NCCL all-gather of the parameter arenas") if world > 1 else None,
+                   "grad_reduce": ({"fused": "mmn_optim_reduce_grads: rank-ordered sum over "
+                                             "NVLink fused with the non-finite scan",
+                                    "nccl": "NCCL reduce-scatter of the grad arenas"}
+                                   [args.grad_reduce] if dp else
+                                   "none (grads already reduced, as the configurations assume)"),
                    "l2": "inputs larger than L2 (no flush needed)"},
         "roofline": roof, "components": comp, "clocks": clk, "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
@@ -489,8 +518,13 @@ def main():
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
-                    help="multi-GPU parameter exchange: stores fused into the step's kernels "
-                         "(NVLink, CUDA IPC) or an NCCL all-gather after the step")
+                    help="multi-GPU parameter exchange: copy-engine pushes over NVLink inside "
+                         "the step (CUDA IPC) or an NCCL all-gather after the step")
+    ap.add_argument("--grad-reduce", default="none", choices=["none", "fused", "nccl"],
+                    help="multi-GPU: also time the data-parallel grad reduction before each "
+                         "step (fused: mmn_optim_reduce_grads over NVLink; nccl: "
+                         "reduce-scatter). Default: grads are already reduced, as the "
+                         "benchmark configurations assume")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -368,6 +368,10 @@ int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64
  * (ns_steps * (4 n^2 m + 2 n^3) per owned matrix, n <= m). */
 int mmn_optim_ns_flops(mmn_optim_t *h, double *flops);
 
+/* Kernel launches one mmn_optim_step enqueues on this rank, and one
+ * mmn_optim_reduce_grads (0 unless reduce_grads). */
+int mmn_optim_kernel_launches(mmn_optim_t *h, int64_t *per_step, int64_t *per_reduce);
+
 /* Per-step device-time breakdown of the last synchronised step, in ms:
  * [0] AdamW kernel, [1] Muon momentum+norm, [2] Newton-Schulz GEMMs,
  * [3] Muon update, [4] whole step. Needs timing enabled. */

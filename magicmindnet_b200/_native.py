@@ -135,6 +135,7 @@ SIGNATURES = {
     "mmn_optim_plan": (_i, [_i64p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, _i, _i, _i,
                             ctypes.POINTER(_i), _i64p, _i64p, _i64p]),
     "mmn_optim_ns_flops": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),
+    "mmn_optim_kernel_launches": (_i, [_vp, _i64p, _i64p]),
     "mmn_optim_enable_timing": (_i, [_vp, _i]),
     "mmn_optim_last_timing": (_i, [_vp, ctypes.POINTER(_f)]),
 }

@@ -1348,6 +1348,22 @@ extern "C" int mmn_optim_ns_flops(mmn_optim_t* h, double* flops) {
   return MMN_OK;
 }
 
+extern "C" int mmn_optim_kernel_launches(mmn_optim_t* h, int64_t* per_step,
+                                         int64_t* per_reduce) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  const int R = h->cfg.rank;
+  const bool adamw = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) >
+                     std::min<int64_t>(h->a_region4 * R, h->a_used4);
+  const int steps = h->cfg.muon.ns_steps;
+  int64_t n = (adamw ? 1 : 0) + 1;  // AdamW, step tail
+  if (h->cfg.loss_scaling && !h->cfg.reduce_grads) n += 2;  // non-finite scans
+  // per chunk: momentum, norms, 3 GEMMs per iteration (or the update kernel)
+  n += (int64_t)h->chunk_begin.size() * (2 + (steps >= 1 ? 3 * steps : 1));
+  if (per_step) *per_step = n;
+  if (per_reduce) *per_reduce = h->cfg.reduce_grads ? 2 : 0;
+  return MMN_OK;
+}
+
 extern "C" int mmn_optim_enable_timing(mmn_optim_t* h, int enable) {
   if (!h) return fail(MMN_E_INVALID, "null handle");
   h->timing = enable != 0;

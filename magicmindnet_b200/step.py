@@ -297,6 +297,12 @@ class OptimizerStep:
                                                ctypes.byref(m)))
         return t.value, a.value, m.value
 
+    def kernel_launches(self):
+        """(launches per step, launches per reduce_grads) on this rank."""
+        a, b = ctypes.c_int64(), ctypes.c_int64()
+        N.check(N.lib().mmn_optim_kernel_launches(self._h, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+
     def ns_flops(self) -> float:
         f = ctypes.c_double()
         N.check(N.lib().mmn_optim_ns_flops(self._h, ctypes.byref(f)))
