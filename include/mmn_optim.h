@@ -294,6 +294,13 @@ int mmn_optim_sync(mmn_optim_t *h);
 /* Loss-scaling state (after mmn_optim_sync): current scale, steps skipped. */
 int mmn_optim_loss_scale(mmn_optim_t *h, float *scale, int64_t *skipped_steps);
 
+/* The whole loss-scaling state, for checkpoints: scale, steps skipped so far
+ * and clean steps since the scale last changed. Synchronous. */
+int mmn_optim_get_loss_state(mmn_optim_t *h, float *scale, int64_t *skipped_steps,
+                             int32_t *good_steps);
+int mmn_optim_set_loss_state(mmn_optim_t *h, float scale, int64_t skipped_steps,
+                             int32_t good_steps);
+
 /* Sharding plan (world_size > 1). A Muon matrix is stepped whole by one rank,
  * chosen by longest-processing-time bin packing on its Newton-Schulz flops;
  * the flat AdamW arena is cut into world_size equal element ranges.

@@ -126,6 +126,9 @@ SIGNATURES = {
     "mmn_optim_step_host": (_i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _f]),
     "mmn_optim_sync": (_i, [_vp]),
     "mmn_optim_loss_scale": (_i, [_vp, ctypes.POINTER(_f), ctypes.POINTER(_i64)]),
+    "mmn_optim_get_loss_state": (_i, [_vp, ctypes.POINTER(_f), ctypes.POINTER(_i64),
+                                      ctypes.POINTER(ctypes.c_int32)]),
+    "mmn_optim_set_loss_state": (_i, [_vp, _f, _i64, ctypes.c_int32]),
     "mmn_optim_slot_owner": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "mmn_optim_get_gather_layout": (_i, [_vp, ctypes.POINTER(GatherLayoutC)]),
     "mmn_optim_param_counts": (_i, [_vp, _i64p, _i64p, _i64p]),

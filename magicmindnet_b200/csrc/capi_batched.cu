@@ -5,6 +5,7 @@
 // tensors keep the reference's call order, which fixes each AdamW tensor's
 // step count t (crates/mmn-optim/src/lib.rs:41-43).
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <unordered_set>
 
@@ -1152,6 +1153,39 @@ extern "C" int mmn_optim_loss_scale(mmn_optim_t* h, float* scale, int64_t* skipp
   MMN_CUDA_TRY(cudaMemcpy(&sk, h->d_skipped, sizeof(int), cudaMemcpyDeviceToHost));
   if (scale) *scale = sc;
   if (skipped_steps) *skipped_steps = sk;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_get_loss_state(mmn_optim_t* h, float* scale, int64_t* skipped_steps,
+                                        int32_t* good_steps) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  DevGuard g(h->ctx.device);
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
+  float sc = 0.0f;
+  int sk = 0, gd = 0;
+  MMN_CUDA_TRY(cudaMemcpy(&sc, h->d_scale, sizeof(float), cudaMemcpyDeviceToHost));
+  MMN_CUDA_TRY(cudaMemcpy(&sk, h->d_skipped, sizeof(int), cudaMemcpyDeviceToHost));
+  MMN_CUDA_TRY(cudaMemcpy(&gd, h->d_good, sizeof(int), cudaMemcpyDeviceToHost));
+  if (scale) *scale = sc;
+  if (skipped_steps) *skipped_steps = sk;
+  if (good_steps) *good_steps = gd;
+  return MMN_OK;
+}
+
+extern "C" int mmn_optim_set_loss_state(mmn_optim_t* h, float scale, int64_t skipped_steps,
+                                        int32_t good_steps) {
+  if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
+  if (!(scale > 0.0f) || skipped_steps < 0 || skipped_steps > INT32_MAX || good_steps < 0)
+    return fail(MMN_E_INVALID, "bad loss-scaling state");
+  DevGuard g(h->ctx.device);
+  const int sk = (int)skipped_steps, gd = good_steps;
+  MMN_CUDA_TRY(cudaMemcpyAsync(h->d_scale, &scale, sizeof(float), cudaMemcpyHostToDevice,
+                               h->ctx.stream));
+  MMN_CUDA_TRY(cudaMemcpyAsync(h->d_skipped, &sk, sizeof(int), cudaMemcpyHostToDevice,
+                               h->ctx.stream));
+  MMN_CUDA_TRY(cudaMemcpyAsync(h->d_good, &gd, sizeof(int), cudaMemcpyHostToDevice,
+                               h->ctx.stream));
+  MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   return MMN_OK;
 }
 

@@ -141,9 +141,12 @@ class OptimizerStep:
         self._h = h
         self.shapes = []
         self.routes = []
+        self._spec = []
+        self._plan = None
         for p in params:
             pid, shape = p[0], tuple(int(s) for s in p[1])
             route = p[2] if len(p) > 2 else "auto"
+            self._spec.append((pid, shape, route))
             slot = ctypes.c_int()
             N.check(N.lib().mmn_optim_add_param(h, pid, N.shape_array(shape), len(shape),
                                                 ROUTES[route], ctypes.byref(slot)))
@@ -232,6 +235,33 @@ class OptimizerStep:
 
     def sync(self) -> None:
         N.check(N.lib().mmn_optim_sync(self._h))
+
+    def stepped_range(self, slot: int):
+        """Element range [lo, hi) of a slot that this rank steps (and whose
+        optimizer state it holds): a whole Muon matrix it owns, or the overlap
+        of an AdamW tensor with its AdamW range; (0, 0) for none."""
+        cfg = self.config
+        if self._plan is None:
+            steps = (cfg.muon or MuonConfig()).ns_steps
+            self._plan = shard_plan(self._spec, cfg.world_size, cfg.use_hybrid, steps)
+        n = int(np.prod(self.shapes[slot], dtype=np.int64))
+        owner = self._plan["owner"][slot]
+        if owner >= 0:
+            return (0, n) if owner == cfg.rank else (0, 0)
+        off, reg = self._plan["offset"][slot], self._plan["adamw_region"]
+        lo = max(off, cfg.rank * reg) - off
+        hi = min(off + n, (cfg.rank + 1) * reg) - off
+        return (lo, hi) if hi > lo else (0, 0)
+
+    def loss_state(self):
+        """(scale, skipped steps, clean steps since the scale last changed)."""
+        s, k, g = ctypes.c_float(), ctypes.c_int64(), ctypes.c_int32()
+        N.check(N.lib().mmn_optim_get_loss_state(self._h, ctypes.byref(s), ctypes.byref(k),
+                                                 ctypes.byref(g)))
+        return s.value, k.value, g.value
+
+    def set_loss_state(self, scale: float, skipped_steps: int, good_steps: int) -> None:
+        N.check(N.lib().mmn_optim_set_loss_state(self._h, scale, skipped_steps, good_steps))
 
     def loss_scale(self):
         s, k = ctypes.c_float(), ctypes.c_int64()
