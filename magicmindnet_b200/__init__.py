@@ -10,12 +10,13 @@ from ._native import CUDAError, KernelTimeoutError, MmnError, ShapeError  # noqa
 from .optim import (AdamW, AdamWConfig, GradAccumulator, HybridOptimizer, Muon,  # noqa: F401
                     MuonConfig, ParamKind, is_available, newton_schulz5, require_cuda)
 from .step import (OptimizerStep, StepConfig, TrainConfig, chatbot_param_order,  # noqa: F401
-                   shard_plan, step_config_for)
+                   classifier_param_order, diffusion_param_order, shard_plan, step_config_for)
 from .checkpoint import load_state, save_state  # noqa: F401
 
 __all__ = ["AdamW", "AdamWConfig", "Muon", "MuonConfig", "HybridOptimizer", "ParamKind",
            "GradAccumulator", "newton_schulz5", "is_available", "require_cuda", "OptimizerStep",
            "StepConfig", "TrainConfig", "step_config_for", "chatbot_param_order", "shard_plan",
+           "classifier_param_order", "diffusion_param_order",
            "save_state", "load_state",
            "MmnError",
            "CUDAError", "ShapeError", "KernelTimeoutError"]

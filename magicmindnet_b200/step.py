@@ -392,3 +392,20 @@ def chatbot_param_order(vocab_size: int, n_layer: int, d_model: int, ffn_mult: i
     if pos_embed_len:
         out.append(("pos_embed", (pos_embed_len, d)))
     return out
+
+
+def classifier_param_order(num_labels: int, input_dim: int):
+    """(name, shape) of the Classifier's trained weights in the order its step
+    calls AdamW (crates/mmn-models/src/chatbot.rs:1483-1548: head, then backbone;
+    backbone input_dim -> 128, head 128 -> labels, :1399-1400). The classifier is
+    stepped with AdamW only (use_hybrid = False)."""
+    return [("head", (max(num_labels, 1), 128)), ("backbone", (128, input_dim))]
+
+
+def diffusion_param_order():
+    """(name, shape) of the diffusion UNet's conv weights in the order
+    train_step_denoise calls AdamW (crates/mmn-models/src/chatbot.rs:2311-2320:
+    down, mid, up; [out_ch, in_ch, k, k] as crates/mmn-nn/src/lib.rs:1989-1991
+    builds them with UNet2D::new, :2167-2171). AdamW only."""
+    return [("unet.down", (64, 4, 3, 3)), ("unet.mid", (64, 64, 3, 3)),
+            ("unet.up", (4, 64, 3, 3))]

@@ -323,3 +323,106 @@ def test_reduced_grads_step_equals_single_gpu_on_summed_grads(mmn, bf16):
             assert (scale, nskip) == (scale0 / 2, 1), r
     for p in procs:
         assert p.exitcode == 0
+
+
+# ------------------------------------------------------------------ checkpoints
+def _ckpt_worker(rank, world, port, q, path):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import magicmindnet_b200 as mmn
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        model = _model()
+        names = [f"t{k}" for k in range(len(model))]
+        stream = torch.cuda.current_stream(rank).cuda_stream
+
+        def make():
+            s = mmn.OptimizerStep(model, mmn.StepConfig(rank=rank, world_size=world,
+                                                        use_graph=False),
+                                  device=rank, stream=stream)
+            s.connect_peers()
+            return s
+
+        def grads(step, seed):
+            gen = torch.Generator(device="cuda").manual_seed(seed)
+            for k, (_, s, _) in enumerate(model):
+                step.grad(k).normal_(0, 1e-3, generator=gen)
+
+        a = make()
+        _fill(a, model, 0)
+        for it in range(2):
+            grads(a, 10 + it)
+            a.step()
+            a.exchange_fence()
+        a.sync()
+        mmn.save_state(a, f"{path}.{rank}", names)
+        b = make()
+        for k in range(len(model)):
+            b.param(k).copy_(a.param(k))
+        mmn.load_state(b, f"{path}.{rank}", names)
+        for it in range(2):
+            for s in (a, b):
+                grads(s, 20 + it)
+                s.step()
+                s.exchange_fence()
+        a.sync()
+        b.sync()
+        torch.cuda.synchronize()
+        bad = [k for k in range(len(model)) if not torch.equal(a.param(k), b.param(k))]
+        for k in range(len(model)):
+            lo, hi = a.stepped_range(k)
+            if hi <= lo:
+                continue
+            which = ("m", "v") if a.routes[k] == "adamw" else ("velocity",)
+            for w in which:
+                sa = a.get_state(k, w).reshape(-1)[lo:hi]
+                sb = b.get_state(k, w).reshape(-1)[lo:hi]
+                if not np.array_equal(sa.view(np.uint32), sb.view(np.uint32)):
+                    bad.append((k, w))
+        q.put((rank, bad))
+        a.close()
+        b.close()
+    except Exception as e:  # reported to the parent, which fails at once
+        q.put((rank, f"{type(e).__name__}: {e}"))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_checkpoint_resume_is_bit_exact(tmp_path):
+    """Each rank saves what it steps (its Muon matrices, its AdamW slices) and a
+    fresh sharded handle resumes from it: the next steps match bit for bit."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    path = str(tmp_path / "optim.safetensors")
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, world, port, q, path))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=900) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    for r, bad in got.items():
+        assert bad == [], (r, bad)
+    for p in procs:
+        assert p.exitcode == 0
