@@ -128,36 +128,41 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
                    const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
   using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
   if (args.num_tiles <= 0) return cudaSuccess;
-  if (!PAIR) {
-    const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
-    ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR><<<grid, S::kThreads, S::kSmemBytes, stream>>>(a1, a2,
-                                                                                       b, args);
-    return cudaGetLastError();
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(S::kThreads, 1, 1);
   cfg.dynamicSmemBytes = S::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // A persistent grid must not exceed the clusters that fit at once: a
-  // cluster scheduled late would run its whole tile list after the others.
-  static int max_pairs = 0;
-  if (max_pairs == 0) {
-    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-    int n = 0;
-    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
-                                                   &cfg);
-    if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
-    max_pairs = n < num_sms / 2 ? n : num_sms / 2;
+  int grid;
+  if (!PAIR) {
+    grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
+  } else {
+    // A persistent grid must not exceed the clusters that fit at once: a
+    // cluster scheduled late would run its whole tile list after the others.
+    static int max_pairs = 0;
+    if (max_pairs == 0) {
+      cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
+                                                     &cfg);
+      if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
+      max_pairs = n < num_sms / 2 ? n : num_sms / 2;
+    }
+    grid = 2 * (args.num_tiles < max_pairs ? args.num_tiles : max_pairs);
   }
-  const int pairs = args.num_tiles < max_pairs ? args.num_tiles : max_pairs;
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
+  // Programmatic dependent launch: this grid may be scheduled while the previous
+  // kernel on the stream drains (its CTAs take SMs as the previous ones exit);
+  // the kernel's first instruction waits until that kernel has completed.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>, a1, a2, b, args);
 }
 

@@ -255,6 +255,11 @@ __global__ void __launch_bounds__(320, 1)
   __nv_bfloat16* epi_stage =
       reinterpret_cast<__nv_bfloat16*>(smem + STAGES * S::kStageBytes + S::kBarBytes);
 
+  // Launched as a programmatic dependent: nothing of the previous kernel's output
+  // (X, A, A2, the skip flag) is read before it has completed. The next kernel
+  // may then be scheduled; it waits the same way.
+  griddep_wait();
+  griddep_launch_dependents();
   // A skipped step (non-finite grads) leaves every buffer untouched. Both CTAs
   // of a pair read the same flag, so both leave before any cluster barrier.
   if (args.skip && *args.skip) return;
