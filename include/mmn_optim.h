@@ -98,6 +98,13 @@ const char *mmn_last_error(void);
 /* MMN_OPTIM_ABI_VERSION of the loaded library. */
 int mmn_abi_version(void);
 
+/* Failure-detection self-test: one kernel waits on an mbarrier phase that
+ * nothing completes, through the bounded wait every pipelined kernel uses,
+ * with a limit of limit_ns (at most 2 s). Returns MMN_E_TIMEOUT when the wait
+ * gave up and reported it (the expected outcome; the device stays usable),
+ * MMN_OK if it did not time out. No counterpart in the reference. */
+int mmn_selftest_bounded_wait(int device, uint64_t limit_ns);
+
 /* AdamWConfig::default() / MuonConfig::default() (lib.rs:13-21, 71-80). */
 mmn_adamw_config mmn_adamw_config_default(void);
 mmn_muon_config mmn_muon_config_default(void);

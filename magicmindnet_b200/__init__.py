@@ -12,11 +12,12 @@ from .optim import (AdamW, AdamWConfig, GradAccumulator, HybridOptimizer, Muon, 
 from .step import (OptimizerStep, StepConfig, TrainConfig, chatbot_param_order,  # noqa: F401
                    classifier_param_order, diffusion_param_order, shard_plan, step_config_for)
 from .checkpoint import load_state, save_state  # noqa: F401
+from .failure import RankFailure, RankMonitor, RankTimeout  # noqa: F401
 
 __all__ = ["AdamW", "AdamWConfig", "Muon", "MuonConfig", "HybridOptimizer", "ParamKind",
            "GradAccumulator", "newton_schulz5", "is_available", "require_cuda", "OptimizerStep",
            "StepConfig", "TrainConfig", "step_config_for", "chatbot_param_order", "shard_plan",
            "classifier_param_order", "diffusion_param_order",
-           "save_state", "load_state",
+           "save_state", "load_state", "RankMonitor", "RankFailure", "RankTimeout",
            "MmnError",
            "CUDAError", "ShapeError", "KernelTimeoutError"]

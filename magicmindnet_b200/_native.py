@@ -83,6 +83,7 @@ SIGNATURES = {
     "mmn_require_cuda": (_i, [_i]),
     "mmn_last_error": (ctypes.c_char_p, []),
     "mmn_abi_version": (_i, []),
+    "mmn_selftest_bounded_wait": (_i, [_i, _u64]),
     "mmn_adamw_config_default": (AdamWConfigC, []),
     "mmn_muon_config_default": (MuonConfigC, []),
     "mmn_adamw_create": (_i, [ctypes.POINTER(AdamWConfigC), _i, _vp, ctypes.POINTER(_vp)]),

@@ -167,6 +167,51 @@ const char* mmn_last_error(void) { return mmn::t_last_error.c_str(); }
 
 int mmn_abi_version(void) { return MMN_OPTIM_ABI_VERSION; }
 
+namespace {
+// Waits on an mbarrier phase that nothing completes, through the same bounded
+// wait the GEMM kernels use, and records the time-out in *status.
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mmn::mbar_init(&bar, 1);
+    abort_flag = 0;
+    mmn::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mmn::mbar_wait(&bar, 0, &abort_flag, limit_ns))
+    atomicExch(status, mmn::kDevWaitTimeout);
+}
+}  // namespace
+
+int mmn_selftest_bounded_wait(int device, uint64_t limit_ns) {
+  using namespace mmn;
+  if (limit_ns == 0 || limit_ns > 2000000000ull) return fail(MMN_E_INVALID, "limit must be in (0, 2 s]");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return fail(MMN_E_NO_DEVICE, "no such CUDA device");
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  int* d = nullptr;
+  int st = -1;
+  cudaError_t e = cudaMalloc(&d, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(d, 0, sizeof(int));
+  if (e == cudaSuccess) {
+    selftest_wait_kernel<<<1, 32>>>(limit_ns, d);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&st, d, sizeof(int), cudaMemcpyDeviceToHost);
+  if (d) cudaFree(d);
+  if (prev >= 0) cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "bounded-wait self-test");
+  if (st == kDevWaitTimeout) return fail(MMN_E_TIMEOUT, "the wait gave up after its limit");
+  return MMN_OK;
+}
+
 mmn_adamw_config mmn_adamw_config_default(void) {
   mmn_adamw_config c;
   c.lr = 3e-4f;

@@ -78,16 +78,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and
-// sets *abort) if the wait gave up after kWaitLimitNs or another role of the
-// CTA already gave up; the caller then stops issuing work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// sets *abort) if the wait gave up after limit_ns or another role of the CTA
+// already gave up; the caller then stops issuing work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t start = global_timer_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - start > kWaitLimitNs) {
+    if (global_timer_ns() - start > limit_ns) {
       *abort = 1;
       return false;
     }
