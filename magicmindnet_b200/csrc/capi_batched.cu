@@ -9,6 +9,8 @@
 #include <cstring>
 #include <unordered_set>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "capi_internal.cuh"
 #include "elementwise.cuh"
 #include "ns_engine.cuh"
@@ -30,6 +32,15 @@ struct DevGuard {
 };
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// NVTX range over one host-side phase (a no-op unless a profiler is attached),
+// so that a timeline shows which part of the step enqueued which kernels.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 struct ShardTensor {
   int64_t numel = 0;
@@ -842,6 +853,7 @@ static int param_out(mmn_optim_t* h, const HostIO* io, int i, int64_t lo, int64_
 // starts when its copy lands, and each finished group's params start back at
 // once, so the PCIe transfers in both directions overlap the compute.
 static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
+  NvtxRange range_step(io ? "mmn.step_host" : "mmn.step");
   cudaStream_t s = h->work;
   const bool tm = h->timing && !io;
   const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
@@ -896,60 +908,63 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
 
   // ---- AdamW on the side stream: one launch over this rank's range, or (host
   // steps) one per part, each after its grads landed
-  MMN_CUDA_TRY(cudaEventRecord(h->fork, s));
-  MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->fork, 0));
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[1], h->side));
-  AdamwArgs a{};
-  a.p = h->ap;
-  a.g = bf ? nullptr : static_cast<const float*>(h->ag);
-  a.g_bf16 = bf ? static_cast<const __nv_bfloat16*>(h->ag) : nullptr;
-  a.m = h->am;
-  a.v = h->av;
-  a.p_bf16 = h->ap16;
-  a.segs = h->d_segs;
-  a.chunk_seg = h->d_chunk_seg;
-  a.bc_table = h->bc.dev;
-  a.t_sat = h->bc.t_sat;
-  a.step_base = h->d_step;
-  a.skip = skip;
-  a.grad_scale = gscale;
-  a.lr = h->cfg.adamw.lr;
-  a.b1 = h->cfg.adamw.beta1;
-  a.b2 = h->cfg.adamw.beta2;
-  a.eps = h->cfg.adamw.eps;
-  a.wd = h->cfg.adamw.weight_decay;
-  a.grad_divisor = divisor;
-  a.fresh_state = h->cfg.fresh_state;
-  void* a_src = h->cfg.bf16_param_shadow ? (void*)h->ap16 : (void*)h->ap;
-  if (io) {
-    for (size_t j = 0; j < h->jobs.size(); ++j) {
-      if (h->jobs[j] >= 0) continue;
-      const int p = -1 - h->jobs[j];
-      MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->h2d_ev[j], 0));
-      a.begin4 = h->apart_begin4[p];
-      a.end4 = h->apart_end4[p];
+  {
+    NvtxRange range_adamw("mmn.adamw");
+    MMN_CUDA_TRY(cudaEventRecord(h->fork, s));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->fork, 0));
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[1], h->side));
+    AdamwArgs a{};
+    a.p = h->ap;
+    a.g = bf ? nullptr : static_cast<const float*>(h->ag);
+    a.g_bf16 = bf ? static_cast<const __nv_bfloat16*>(h->ag) : nullptr;
+    a.m = h->am;
+    a.v = h->av;
+    a.p_bf16 = h->ap16;
+    a.segs = h->d_segs;
+    a.chunk_seg = h->d_chunk_seg;
+    a.bc_table = h->bc.dev;
+    a.t_sat = h->bc.t_sat;
+    a.step_base = h->d_step;
+    a.skip = skip;
+    a.grad_scale = gscale;
+    a.lr = h->cfg.adamw.lr;
+    a.b1 = h->cfg.adamw.beta1;
+    a.b2 = h->cfg.adamw.beta2;
+    a.eps = h->cfg.adamw.eps;
+    a.wd = h->cfg.adamw.weight_decay;
+    a.grad_divisor = divisor;
+    a.fresh_state = h->cfg.fresh_state;
+    void* a_src = h->cfg.bf16_param_shadow ? (void*)h->ap16 : (void*)h->ap;
+    if (io) {
+      for (size_t j = 0; j < h->jobs.size(); ++j) {
+        if (h->jobs[j] >= 0) continue;
+        const int p = -1 - h->jobs[j];
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->h2d_ev[j], 0));
+        a.begin4 = h->apart_begin4[p];
+        a.end4 = h->apart_end4[p];
+        launch_adamw(a, h->ctx.num_sms, h->side);
+        MMN_CUDA_TRY(cudaGetLastError());
+        MMN_CUDA_TRY(cudaEventRecord(h->apart_ev[p], h->side));
+        if (h->n_peers) {
+          MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->apart_ev[p], 0));
+          MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
+        }
+      }
+    } else {
+      a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
+      a.end4 = std::min<long long>(h->a_region4 * (R + 1), h->a_used4);
       launch_adamw(a, h->ctx.num_sms, h->side);
       MMN_CUDA_TRY(cudaGetLastError());
-      MMN_CUDA_TRY(cudaEventRecord(h->apart_ev[p], h->side));
       if (h->n_peers) {
-        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->apart_ev[p], 0));
+        // this rank's AdamW range goes to every peer while the Muon work runs
+        MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
+        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
         MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
       }
     }
-  } else {
-    a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
-    a.end4 = std::min<long long>(h->a_region4 * (R + 1), h->a_used4);
-    launch_adamw(a, h->ctx.num_sms, h->side);
-    MMN_CUDA_TRY(cudaGetLastError());
-    if (h->n_peers) {
-      // this rank's AdamW range goes to every peer while the Muon work runs
-      MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
-      MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
-      MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
-    }
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
+    MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
   }
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
-  MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
 
   // ---- Muon on the work stream, chunk by chunk
   if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[3], s));
@@ -979,6 +994,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     };
     // momentum, bf16 cast and norms of chunk k
     auto prologue = [&](size_t k) -> int {
+      NvtxRange r("mmn.muon_momentum");
       select(k);
       m.cls = h->d_cls_in;
       launch_muon_momentum(m, h->ctx.num_sms, s);
@@ -990,6 +1006,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     // (lib.rs:169-174); with zero iterations the update kernel does it.
     const bool fuse = h->cfg.muon.ns_steps >= 1;
     auto newton_schulz = [&](size_t k) -> int {
+      NvtxRange r("mmn.newton_schulz");
       NsFused f;
       f.p = h->mp;
       f.p_bf16 = h->mp16;
@@ -1334,6 +1351,7 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
 }
 
 extern "C" int mmn_optim_reduce_grads(mmn_optim_t* h) {
+  NvtxRange range("mmn.reduce_grads");
   if (!h) return fail(MMN_E_INVALID, "null handle");
   if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
   if (!h->cfg.reduce_grads || h->cfg.world_size < 2)
