@@ -321,6 +321,9 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev)).split(",")[0])
                           if os.environ.get("CUDA_VISIBLE_DEVICES", "").isdigit() else dev)
+    # the timed steps record per-phase CUDA events (launched without the graph;
+    # the warm-up steps captured and replayed it, at the same speed)
+    step.enable_timing(True)
     clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -335,12 +338,8 @@ def run_ours(args, rank, world, local_rank):
     ev1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    # per-kernel device times from one more step, outside the timed region, with
-    # CUDA events the library records on the streams its kernels run on (the
-    # timed steps replay the captured CUDA graph, which holds no events)
-    step.enable_timing(True)
-    one_step()
-    torch.cuda.synchronize()
+    # per-phase device times averaged over the timed steps (CUDA events the
+    # library records on the streams its kernels run on)
     phase = {k2: [v] for k2, v in step.last_timing().items()}
     step.enable_timing(False)
     ms = ev0.elapsed_time(ev1) / args.steps
@@ -429,9 +428,10 @@ def run_ours(args, rank, world, local_rank):
                           "TFLOP/s": (ns_flops / (med["newton_schulz"] / 1e3) / 1e12)
                           if med["newton_schulz"] else None},
         "muon_momentum_ms": med["muon_momentum"], "muon_update_ms": med["muon_update"],
-        "note": "AdamW runs on a side stream concurrently with the Newton-Schulz GEMMs, so in "
-                "hybrid workloads its event time includes waiting for SMs; its kernel rate is "
-                "the adamw_arena workload's",
+        "step_ms_events": med["step"],
+        "note": "phase times are averaged over the timed steps. AdamW runs on a side stream "
+                "concurrently with the Newton-Schulz GEMMs, so in hybrid workloads its event "
+                "time includes waiting for SMs; its kernel rate is the adamw_arena workload's",
     }
     if n_muon and med["newton_schulz"] > 0:
         ach = ns_flops / (med["newton_schulz"] / 1e3) / 1e12

@@ -386,9 +386,10 @@ int mmn_optim_ns_flops(mmn_optim_t *h, double *flops);
  * mmn_optim_reduce_grads (0 unless reduce_grads). */
 int mmn_optim_kernel_launches(mmn_optim_t *h, int64_t *per_step, int64_t *per_reduce);
 
-/* Per-step device-time breakdown of the last synchronised step, in ms:
- * [0] AdamW kernel, [1] Muon momentum+norm, [2] Newton-Schulz GEMMs,
- * [3] Muon update, [4] whole step. Needs timing enabled. */
+/* Per-step device-time breakdown in ms, averaged over the steps enqueued since
+ * timing was (re-)enabled (each such step records CUDA events around its phases
+ * and is launched without the CUDA graph): [0] AdamW kernel, [1] Muon
+ * momentum+norm, [2] Newton-Schulz GEMMs, [3] Muon update, [4] whole step. */
 int mmn_optim_enable_timing(mmn_optim_t *h, int enable);
 int mmn_optim_last_timing(mmn_optim_t *h, float *ms5);
 

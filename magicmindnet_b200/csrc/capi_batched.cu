@@ -5,6 +5,7 @@
 // tensors keep the reference's call order, which fixes each AdamW tensor's
 // step count t (crates/mmn-optim/src/lib.rs:41-43).
 #include <algorithm>
+#include <array>
 #include <climits>
 #include <cstring>
 #include <unordered_set>
@@ -253,7 +254,11 @@ struct mmn_optim {
   cudaGraphExec_t graph = nullptr;
   float graph_divisor = 0.0f;
   bool timing = false;
-  cudaEvent_t ev[8] = {};
+  // per-step phase events while timing is on: one set of 8 per step (up to
+  // kTimedSteps, then the sets are reused), averaged by mmn_optim_last_timing
+  static constexpr size_t kTimedSteps = 4096;
+  std::vector<std::array<cudaEvent_t, 8>> ev_sets;
+  size_t ev_used = 0;
   std::vector<void*> allocs;
 
   int dalloc(void** p, size_t bytes) {
@@ -324,8 +329,9 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   for (auto& c : h->classes) ns_class_free(c);
   for (void* p : h->peer_maps) cudaIpcCloseMemHandle(p);
   for (void* p : h->allocs) cudaFree(p);
-  for (auto& e : h->ev)
-    if (e) cudaEventDestroy(e);
+  for (auto& set : h->ev_sets)
+    for (auto e : set)
+      if (e) cudaEventDestroy(e);
   if (h->fork) cudaEventDestroy(h->fork);
   if (h->join) cudaEventDestroy(h->join);
   if (h->side) cudaStreamDestroy(h->side);
@@ -619,7 +625,6 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->out_ev, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming));
-  for (auto& e : h->ev) MMN_CUDA_TRY(cudaEventCreate(&e));
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->xfer, cudaStreamNonBlocking));
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->h2d, cudaStreamNonBlocking));
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->d2h, cudaStreamNonBlocking));
@@ -856,9 +861,20 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   NvtxRange range_step(io ? "mmn.step_host" : "mmn.step");
   cudaStream_t s = h->work;
   const bool tm = h->timing && !io;
+  cudaEvent_t* ev = nullptr;
+  if (tm) {
+    const size_t k = h->ev_used % mmn_optim::kTimedSteps;
+    if (k == h->ev_sets.size()) {
+      std::array<cudaEvent_t, 8> set{};
+      for (auto& e : set) MMN_CUDA_TRY(cudaEventCreate(&e));
+      h->ev_sets.push_back(set);
+    }
+    ev = h->ev_sets[k].data();
+    ++h->ev_used;
+  }
   const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
   const int R = h->cfg.rank;
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[0], s));
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[0], s));
 
   // ---- grads in (host steps), job by job
   if (io) {
@@ -912,7 +928,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     NvtxRange range_adamw("mmn.adamw");
     MMN_CUDA_TRY(cudaEventRecord(h->fork, s));
     MMN_CUDA_TRY(cudaStreamWaitEvent(h->side, h->fork, 0));
-    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[1], h->side));
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[1], h->side));
     AdamwArgs a{};
     a.p = h->ap;
     a.g = bf ? nullptr : static_cast<const float*>(h->ag);
@@ -962,12 +978,12 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
         MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
       }
     }
-    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[2], h->side));
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[2], h->side));
     MMN_CUDA_TRY(cudaEventRecord(h->join, h->side));
   }
 
   // ---- Muon on the work stream, chunk by chunk
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[3], s));
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[3], s));
   if (!h->mats.empty()) {
     MuonArgs m{};
     m.p = h->mp;
@@ -1041,16 +1057,16 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     } else {
       for (int k : h->jobs)
         if (k >= 0) MMN_TRY_RC(prologue(k));
-      if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
+      if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[4], s));
       for (int k : h->jobs)
         if (k >= 0) MMN_TRY_RC(newton_schulz(k));
     }
-    if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
+    if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[5], s));
   } else if (tm) {
-    MMN_CUDA_TRY(cudaEventRecord(h->ev[4], s));
-    MMN_CUDA_TRY(cudaEventRecord(h->ev[5], s));
+    MMN_CUDA_TRY(cudaEventRecord(ev[4], s));
+    MMN_CUDA_TRY(cudaEventRecord(ev[5], s));
   }
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[6], s));
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[6], s));
 
   // ---- params out (host steps), job by job, queued after all compute so that
   // a copy into pageable memory, which blocks the host, cannot hold back a launch
@@ -1083,7 +1099,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   t.skipped_total = h->d_skipped;
   launch_step_tail(t, s);
   MMN_CUDA_TRY(cudaGetLastError());
-  if (tm) MMN_CUDA_TRY(cudaEventRecord(h->ev[7], s));
+  if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[7], s));
   return MMN_OK;
 }
 
@@ -1419,18 +1435,26 @@ extern "C" int mmn_optim_kernel_launches(mmn_optim_t* h, int64_t* per_step,
 extern "C" int mmn_optim_enable_timing(mmn_optim_t* h, int enable) {
   if (!h) return fail(MMN_E_INVALID, "null handle");
   h->timing = enable != 0;
+  if (h->timing) h->ev_used = 0;  // a new averaging window
   return MMN_OK;
 }
 
 extern "C" int mmn_optim_last_timing(mmn_optim_t* h, float* ms5) {
   if (!h || !ms5) return fail(MMN_E_INVALID, "null argument");
-  if (!h->timing) return fail(MMN_E_STATE, "enable timing before the step");
+  if (!h->timing || h->ev_used == 0) return fail(MMN_E_STATE, "enable timing before the steps");
   DevGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
-  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[0], h->ev[1], h->ev[2]));
-  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[1], h->ev[3], h->ev[4]));
-  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[2], h->ev[4], h->ev[5]));
-  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[3], h->ev[5], h->ev[6]));
-  MMN_CUDA_TRY(cudaEventElapsedTime(&ms5[4], h->ev[0], h->ev[7]));
+  const size_t n = std::min(h->ev_used, mmn_optim::kTimedSteps);
+  double acc[5] = {0, 0, 0, 0, 0};
+  for (size_t k = 0; k < n; ++k) {
+    const cudaEvent_t* ev = h->ev_sets[k].data();
+    const int from[5] = {1, 3, 4, 5, 0}, to[5] = {2, 4, 5, 6, 7};
+    for (int i = 0; i < 5; ++i) {
+      float ms = 0.0f;
+      MMN_CUDA_TRY(cudaEventElapsedTime(&ms, ev[from[i]], ev[to[i]]));
+      acc[i] += ms;
+    }
+  }
+  for (int i = 0; i < 5; ++i) ms5[i] = (float)(acc[i] / (double)n);
   return MMN_OK;
 }
