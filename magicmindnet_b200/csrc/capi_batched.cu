@@ -497,14 +497,27 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   h->chunk_mat0.push_back((int)h->mats.size());
   h->chunk_tile0.push_back(tiles);
 
-  // ---- AdamW parts of at most kChunkElems elements over this rank's range
+  // ---- AdamW parts over this rank's range: at most kChunkElems elements each,
+  // and, when the range is large, a small first and last part (2^24 elements)
+  // so that a host-memory step's copies start back early and end soon after
+  // the last grads land
   {
     const int64_t lo4 = std::min<int64_t>(h->a_region4 * R, h->a_used4);
     const int64_t hi4 = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4);
     const int64_t n4 = hi4 - lo4;
-    const int64_t parts = n4 > 0 ? (n4 * 4 + kChunkElems - 1) / kChunkElems : 0;
-    for (int64_t p = 0; p < parts; ++p) {
-      const int64_t b4 = lo4 + n4 * p / parts, e4 = lo4 + n4 * (p + 1) / parts;
+    constexpr int64_t kEdge4 = (int64_t(1) << 24) / 4;
+    std::vector<int64_t> cuts{lo4};
+    if (n4 > 4 * kEdge4) {
+      const int64_t mid = n4 - 2 * kEdge4;
+      const int64_t parts = (mid * 4 + kChunkElems - 1) / kChunkElems;
+      for (int64_t p = 0; p <= parts; ++p) cuts.push_back(lo4 + kEdge4 + mid * p / parts);
+      cuts.push_back(hi4);
+    } else if (n4 > 0) {
+      const int64_t parts = (n4 * 4 + kChunkElems - 1) / kChunkElems;
+      for (int64_t p = 1; p <= parts; ++p) cuts.push_back(lo4 + n4 * p / parts);
+    }
+    for (size_t p = 0; p + 1 < cuts.size(); ++p) {
+      const int64_t b4 = cuts[p], e4 = cuts[p + 1];
       h->apart_begin4.push_back(b4);
       h->apart_end4.push_back(e4);
       std::vector<mmn_optim::Piece> pcs;
