@@ -148,7 +148,13 @@ class RankMonitor:
         try:
             yield self
         except BaseException as e:
-            if not any(self.store.check([self._key(kind, self.rank)])
-                       for kind in ("failed", "lost")):
-                self.report_failure(f"{type(e).__name__}: {e}")
+            try:
+                if not any(self.store.check([self._key(kind, self.rank)])
+                           for kind in ("failed", "lost")):
+                    self.report_failure(f"{type(e).__name__}: {e}")
+            except Exception:
+                # The store is gone (its host process ended): the peers learn of
+                # this exit from their collective's timeout instead, and the
+                # original exception is what this rank reports.
+                pass
             raise

@@ -21,7 +21,9 @@ def _worker(rank, port, q, scenario):
 
     from magicmindnet_b200.failure import RankFailure, RankMonitor, RankTimeout
 
-    store = dist.TCPStore("127.0.0.1", port, WORLD, rank == 0,
+    # The store is served by the parent process, so it outlives every rank:
+    # a rank that exits first cannot take it down under the others.
+    store = dist.TCPStore("127.0.0.1", port, WORLD + 1, False,
                           timeout=datetime.timedelta(seconds=30))
     dist.init_process_group("gloo", store=store, rank=rank, world_size=WORLD,
                             timeout=datetime.timedelta(seconds=3))
@@ -53,11 +55,14 @@ def _worker(rank, port, q, scenario):
 
 
 def _run(scenario):
+    import torch.distributed as dist
     import torch.multiprocessing as mp
 
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
+    server = dist.TCPStore("127.0.0.1", port, WORLD + 1, True,
+                           timeout=datetime.timedelta(seconds=30), wait_for_workers=False)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_worker, args=(r, port, q, scenario)) for r in range(WORLD)]
@@ -69,6 +74,7 @@ def _run(scenario):
         got[r] = (outcome, dt)
     for p in procs:
         p.join(timeout=60)
+    del server
     return got
 
 
