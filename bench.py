@@ -58,6 +58,45 @@ def peaks():
         return PEAKS_FALLBACK, "fallback"
 
 
+def measure_tf32_peak(dev, sustained_s=3.0):
+    """Dense TF32 tensor-core peak of this GPU, measured the way the bf16 peak
+    is: cuBLAS fp32 GEMM with TF32 allowed, 8192^3 (2*N^3 flops), best of 10 on
+    CUDA events (burst) and back to back for sustained_s seconds (sustained).
+    Run before the timed region, only for the TF32 Newton-Schulz mode."""
+    import torch
+
+    n = 8192
+    a = torch.randn(n, n, device=f"cuda:{dev}")
+    b = torch.randn(n, n, device=f"cuda:{dev}")
+    c = torch.empty(n, n, device=f"cuda:{dev}")
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for _ in range(3):
+            torch.mm(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.mm(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(1, int(sustained_s * 1e3 / best))
+        e0.record()
+        for _ in range(reps):
+            torch.mm(a, b, out=c)
+        e1.record()
+        e1.synchronize()
+        sus = e0.elapsed_time(e1) / reps
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    flops = 2.0 * n ** 3
+    return flops / (best / 1e3) / 1e12, flops / (sus / 1e3) / 1e12
+
+
 # ------------------------------------------------------------------ workloads
 def hybrid_model(d, n_layer, ffn, vocab, kv_dim=None):
     """(name, shape, route) in optimizer call order (lm_head; blocks last..first:
@@ -310,6 +349,9 @@ def run_ours(args, rank, world, local_rank):
             for full, mine in gathers:
                 dist.all_gather_into_tensor(full, mine)
 
+    # TF32 roofline denominator, measured before the warm-up so that the timed
+    # region is untouched
+    tf32_peak = measure_tf32_peak(dev) if args.ns_mode == "tf32" else None
     inj = []
     for i in range(args.warmup):
         one_step()
@@ -435,10 +477,19 @@ def run_ours(args, rank, world, local_rank):
     }
     if n_muon and med["newton_schulz"] > 0:
         ach = ns_flops / (med["newton_schulz"] / 1e3) / 1e12
-        peak = pk["bf16_tflops_sustained"] if args.workload.startswith("hybrid") else pk["bf16_tflops"]
+        sustained = args.workload.startswith("hybrid")
+        if args.ns_mode == "tf32":
+            # the dense TF32 rate is half the bf16 one and not in the peaks file:
+            # measured in this run, before the timed region
+            peak = tf32_peak[1] if sustained else tf32_peak[0]
+            peak_src = ("measured in this run: cuBLAS tf32 8192^3, "
+                        + ("sustained" if sustained else "best of 10"))
+        else:
+            peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+            peak_src = pk_kind
         roof = {"bound": "tensor", "kernel": "ns_gemm (tcgen05, Gram + Square + Poly per iteration)",
                 "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                "peak_source": pk_kind,
+                "peak_source": peak_src,
                 "traffic": ns_flops * NS_DRAM_BYTES_PER_FLOP if args.ns_mode == "reference" else None,
                 "traffic_unit": "DRAM bytes per step of the NS kernels (ncu ratio of the "
                                 "8 x [2048,8192] capture, scaled by flops)",
@@ -456,7 +507,8 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32 (NS GEMMs bf16 x bf16 -> f32)" if not is_8b else "bf16 grads/params, f32 master",
+        "dtype": (f"f32 (NS GEMMs {'tf32 x tf32' if args.ns_mode == 'tf32' else 'bf16 x bf16'}"
+                  " -> f32)") if not is_8b else "bf16 grads/params, f32 master",
         "data": "synthetic (seeded normal params/grads)",
         "config": {"workload": args.workload, "desc": spec["desc"], "params": n_total,
                    "adamw_params": n_adamw, "muon_params": n_muon, "ns_mode": args.ns_mode,
@@ -514,7 +566,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="hybrid_1b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16"])
+    ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16", "tf32"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],

@@ -59,6 +59,11 @@ extern "C" {
 /* Newton-Schulz arithmetic */
 #define MMN_NS_REFERENCE 0 /* lib.rs:112-120 rounding points; B = b*A + c*A2 kept exact */
 #define MMN_NS_BF16 1      /* B rounded to bf16 before B*X (faster; looser tolerance) */
+#define MMN_NS_TF32 2      /* the same recipe with tf32 rounding points in place of bf16
+                              (X, A, A2 held as tf32 values in fp32 words, kind::tf32
+                              tensor-core products, fp32 accumulate): about 8x closer to
+                              exact Newton-Schulz, half the bf16 tensor rate. No
+                              counterpart in the reference. */
 
 /* AdamWConfig, lib.rs:6-11 (defaults lib.rs:13-21: 3e-4, (0.9, 0.95), 1e-8, 0.01) */
 typedef struct {
@@ -170,7 +175,7 @@ int mmn_newton_schulz5(const float *g, const int64_t *shape, int ndim, int steps
  * (rows*cols floats) on `device`. Its scratch is one fixed 8.25 MiB array in
  * the library, held by every GPU that loads the library until exit, so the
  * size is limited to min(rows, cols) <= 1024 and rows*cols <= 1048576; larger
- * inputs return MMN_E_UNSUPPORTED. The first call on a device resolves that
+ * inputs, and MMN_NS_TF32, return MMN_E_UNSUPPORTED. The first call on a device resolves that
  * array's device address and should come before any stream capture. All calls
  * on a device share the array, so calls that overlap on the GPU race. Work is
  * enqueued on `stream` (NULL = legacy default stream) and the call returns
@@ -179,9 +184,10 @@ int mmn_newton_schulz5_noalloc(const float *g, int64_t rows, int64_t cols, int s
                                int ns_mode, float *out, int device, void *stream);
 
 /* One loop body of newton_schulz5 (lib.rs:113-119) on an n x m (n <= m)
- * matrix x whose values are bf16-representable, divided by x_norm first
- * (x_norm = the Frobenius norm for the first iteration, 1 afterwards). Writes
- * A = bf16(x x^T), A2 = bf16(A A) (or, for MMN_NS_BF16, bf16(b*A + c*A2)),
+ * matrix x whose values are bf16-representable (tf32-representable for
+ * MMN_NS_TF32), divided by x_norm first (x_norm = the Frobenius norm for the
+ * first iteration, 1 afterwards). Writes A = bf16(x x^T), A2 = bf16(A A) (or,
+ * for MMN_NS_BF16, bf16(b*A + c*A2); tf32 in place of bf16 for MMN_NS_TF32),
  * and the next x; any output pointer may be NULL. Host memory, synchronous.
  * Exposes the three tensor-core products for per-iteration parity checks. */
 int mmn_newton_schulz_iteration(const float *x, int64_t n, int64_t m, float x_norm, int ns_mode,

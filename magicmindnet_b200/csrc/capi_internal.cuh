@@ -4,6 +4,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -56,5 +57,17 @@ struct BiasTable {
 };
 
 int64_t shape_numel(const int64_t* shape, int ndim, int* err);
+
+// fp32 -> tf32 value (10 leading mantissa bits), to nearest with ties to even
+// on the 13 discarded bits; Inf and NaN pass through. The host form of the
+// TF32 mode's rounding point.
+inline float host_tf32_round(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+  float r;
+  std::memcpy(&r, &u, 4);
+  return r;
+}
 
 }  // namespace mmn

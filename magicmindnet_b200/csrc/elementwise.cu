@@ -193,20 +193,33 @@ __device__ __forceinline__ float block_sum_256(float x, float* red) {
   return r;
 }
 
-// Momentum arithmetic of lib.rs:154-165 for one element; returns bf16(u).
+// Round to tf32 (10 leading mantissa bits), to nearest with ties to even on
+// the 13 discarded bits; Inf and NaN pass through.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+  return __uint_as_float(u);
+}
+
+// Momentum arithmetic of lib.rs:154-165 for one element; returns bf16(u), the
+// rounding of lib.rs:104, or tf32(u) in the TF32 mode.
+template <bool F32X>
 __device__ __forceinline__ float momentum_elem(float g, float& vel, float mu, float one_m,
                                                int nesterov) {
   const float v1 = __fadd_rn(__fmul_rn(mu, vel), __fmul_rn(one_m, g));
   vel = v1;
   const float u = nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
-  return __bfloat162float(__float2bfloat16_rn(u));
+  if constexpr (F32X)
+    return tf32_round(u);
+  else
+    return __bfloat162float(__float2bfloat16_rn(u));
 }
 
 // 128-bit variant of one 64 x 64 momentum tile: thread t covers 4 consecutive
 // columns; a transposed X is written through `tile` in groups of 4 rows.
-template <bool BF16G, bool FRESH>
+template <bool BF16G, bool FRESH, bool F32X>
 __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const MuonMat& mm, int r0,
-                                                   int c0, __nv_bfloat16* X, int ld,
+                                                   int c0, void* Xv, int ld,
                                                    float (*tile)[kTile + 1], float scale,
                                                    float mu, float one_m) {
   const int cq = (threadIdx.x & 15) * 4;
@@ -240,10 +253,14 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
       for (int e = 0; e < 4; ++e) {
         if (scale != 1.0f) g[e] = __fdiv_rn(g[e], scale);
         if (a.grad_divisor != 1.0f) g[e] = __fdiv_rn(g[e], a.grad_divisor);
-        y[e] = momentum_elem(g[e], vv[e], mu, one_m, a.nesterov);
+        y[e] = momentum_elem<F32X>(g[e], vv[e], mu, one_m, a.nesterov);
       }
       __stcs(reinterpret_cast<float4*>(a.vel + idx), make_float4(vv[0], vv[1], vv[2], vv[3]));
-      if (!mm.transposed) {
+      if (!mm.transposed && F32X) {
+        *reinterpret_cast<float4*>(static_cast<float*>(Xv) + (long long)r * ld + c) =
+            make_float4(y[0], y[1], y[2], y[3]);
+      } else if (!mm.transposed) {
+        __nv_bfloat16* X = static_cast<__nv_bfloat16*>(Xv);
         uint2 o;
         __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]);
         __nv_bfloat162 h1 = __floats2bfloat162_rn(y[2], y[3]);
@@ -265,8 +282,16 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
     const int rq = (threadIdx.x & 15) * 4;
     for (int cl = rs; cl < kTile; cl += 16) {
       const int c = c0 + cl, r = r0 + rq;
-      if (c < mm.cols && r < mm.rows) {
-        __nv_bfloat16* dst = X + (long long)c * ld + r;
+      if (c < mm.cols && r < mm.rows && F32X) {
+        float* dst = static_cast<float*>(Xv) + (long long)c * ld + r;
+        if (r + 3 < mm.rows) {
+          *reinterpret_cast<float4*>(dst) =
+              make_float4(tile[rq][cl], tile[rq + 1][cl], tile[rq + 2][cl], tile[rq + 3][cl]);
+        } else {
+          for (int e = 0; e < 4 && r + e < mm.rows; ++e) dst[e] = tile[rq + e][cl];
+        }
+      } else if (c < mm.cols && r < mm.rows) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(Xv) + (long long)c * ld + r;
         if (r + 3 < mm.rows) {
           uint2 o;
           __nv_bfloat162 h0 = __floats2bfloat162_rn(tile[rq][cl], tile[rq + 1][cl]);
@@ -285,8 +310,9 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
 
 // Muon momentum (lib.rs:154-165) + the bf16 cast and orientation of
 // newton_schulz5 (lib.rs:101-107) + per-tile sums of squares of the bf16
-// values (lib.rs:109), all in one pass over g and vel.
-template <bool BF16G, bool FRESH>
+// values (lib.rs:109), all in one pass over g and vel. F32X: the TF32 mode's
+// tf32 cast into an fp32 X.
+template <bool BF16G, bool FRESH, bool F32X>
 __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   __shared__ float red[8];
@@ -302,10 +328,11 @@ __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
     const int lt = t - mm.tile0;
     const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
     const MuonClassPtr cp = a.cls[mm.xcls];
-    __nv_bfloat16* X = cp.x + (long long)mm.xbatch * cp.bstride;
+    void* Xv = F32X ? (void*)(static_cast<float*>(cp.x) + (long long)mm.xbatch * cp.bstride)
+                    : (void*)(static_cast<__nv_bfloat16*>(cp.x) + (long long)mm.xbatch * cp.bstride);
     if (a.vec_ok && (mm.cols & 3) == 0 && (mm.off & 3) == 0) {
       const float ssv =
-          momentum_tile_vec<BF16G, FRESH>(a, mm, r0, c0, X, cp.ld, tile, scale, mu, one_m);
+          momentum_tile_vec<BF16G, FRESH, F32X>(a, mm, r0, c0, Xv, cp.ld, tile, scale, mu, one_m);
       const float totv = block_sum_256(ssv, red);
       if (threadIdx.x == 0) a.partials[t] = totv;
       continue;
@@ -323,9 +350,13 @@ __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
         const float v1 = __fadd_rn(__fmul_rn(mu, v0), __fmul_rn(one_m, g));
         a.vel[idx] = v1;
         const float u = a.nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
-        const __nv_bfloat16 h = __float2bfloat16_rn(u);
-        y = __bfloat162float(h);
-        if (!mm.transposed) X[(long long)r * cp.ld + c] = h;
+        y = F32X ? tf32_round(u) : __bfloat162float(__float2bfloat16_rn(u));
+        if (!mm.transposed) {
+          if (F32X)
+            static_cast<float*>(Xv)[(long long)r * cp.ld + c] = y;
+          else
+            static_cast<__nv_bfloat16*>(Xv)[(long long)r * cp.ld + c] = __float2bfloat16_rn(y);
+        }
       }
       if (mm.transposed) tile[rr][tx] = y;
       ss = __fadd_rn(ss, __fmul_rn(y, y));
@@ -335,8 +366,13 @@ __global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
       // X[c][r] = tile[r - r0][c - c0]; consecutive threads write consecutive r.
       for (int cc = ty; cc < kTile; cc += 4) {
         const int c = c0 + cc, r = r0 + tx;
-        if (c < mm.cols && r < mm.rows)
-          X[(long long)c * cp.ld + r] = __float2bfloat16_rn(tile[tx][cc]);
+        if (c < mm.cols && r < mm.rows) {
+          if (F32X)
+            static_cast<float*>(Xv)[(long long)c * cp.ld + r] = tile[tx][cc];
+          else
+            static_cast<__nv_bfloat16*>(Xv)[(long long)c * cp.ld + r] =
+                __float2bfloat16_rn(tile[tx][cc]);
+        }
       }
     }
     const float tot = block_sum_256(ss, red);
@@ -360,7 +396,7 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(const MuonArgs a) {
 
 // Muon::step_matrix tail (lib.rs:169-174): p -= (lr*scale) * O, O read back in
 // the parameter's orientation from the final Newton-Schulz X.
-template <bool SHADOW>
+template <bool SHADOW, bool F32X>
 __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   if (a.skip && *a.skip) return;
@@ -372,14 +408,16 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
     const int lt = t - mm.tile0;
     const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
     const MuonClassPtr cp = a.cls[mm.xcls];
-    const __nv_bfloat16* X = cp.x + (long long)mm.xbatch * cp.bstride;
+    const long long xb = (long long)mm.xbatch * cp.bstride;
+    auto xat = [&](long long i) -> float {
+      if (F32X) return static_cast<const float*>(cp.x)[xb + i];
+      return __bfloat162float(static_cast<const __nv_bfloat16*>(cp.x)[xb + i]);
+    };
     if (mm.transposed) {
       __syncthreads();
       for (int cc = ty; cc < kTile; cc += 4) {
         const int c = c0 + cc, r = r0 + tx;
-        tile[cc][tx] = (c < mm.cols && r < mm.rows)
-                           ? __bfloat162float(X[(long long)c * cp.ld + r])
-                           : 0.0f;
+        tile[cc][tx] = (c < mm.cols && r < mm.rows) ? xat((long long)c * cp.ld + r) : 0.0f;
       }
       __syncthreads();
     }
@@ -387,7 +425,7 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
       const int r = r0 + rr, c = c0 + tx;
       if (r < mm.rows && c < mm.cols) {
         const long long idx = mm.off + (long long)r * mm.cols + c;
-        float o = mm.transposed ? tile[tx][rr] : __bfloat162float(X[(long long)r * cp.ld + c]);
+        float o = mm.transposed ? tile[tx][rr] : xat((long long)r * cp.ld + c);
         if (a.apply_divides_norm) o = __fdiv_rn(o, a.norms[mm.norm_idx]);
         const float pn = __fsub_rn(a.p[idx], __fmul_rn(mm.lr_scale, o));
         a.p[idx] = pn;
@@ -571,10 +609,17 @@ void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
   if (a.total_tiles <= 0) return;
   const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
   const bool bf = a.g_bf16 != nullptr, fresh = a.fresh_state != 0;
-  if (bf && fresh) muon_momentum_kernel<true, true><<<grid, 256, 0, stream>>>(a);
-  if (bf && !fresh) muon_momentum_kernel<true, false><<<grid, 256, 0, stream>>>(a);
-  if (!bf && fresh) muon_momentum_kernel<false, true><<<grid, 256, 0, stream>>>(a);
-  if (!bf && !fresh) muon_momentum_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+#define MMN_MOM(F32X)                                                                  \
+  if (bf && fresh) muon_momentum_kernel<true, true, F32X><<<grid, 256, 0, stream>>>(a);   \
+  if (bf && !fresh) muon_momentum_kernel<true, false, F32X><<<grid, 256, 0, stream>>>(a); \
+  if (!bf && fresh) muon_momentum_kernel<false, true, F32X><<<grid, 256, 0, stream>>>(a); \
+  if (!bf && !fresh) muon_momentum_kernel<false, false, F32X><<<grid, 256, 0, stream>>>(a);
+  if (a.x_f32) {
+    MMN_MOM(true)
+  } else {
+    MMN_MOM(false)
+  }
+#undef MMN_MOM
 }
 
 void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
@@ -585,10 +630,14 @@ void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
 void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream) {
   if (a.total_tiles <= 0) return;
   const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
-  if (a.p_bf16)
-    muon_apply_kernel<true><<<grid, 256, 0, stream>>>(a);
+  if (a.p_bf16 && a.x_f32)
+    muon_apply_kernel<true, true><<<grid, 256, 0, stream>>>(a);
+  else if (a.p_bf16)
+    muon_apply_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+  else if (a.x_f32)
+    muon_apply_kernel<false, true><<<grid, 256, 0, stream>>>(a);
   else
-    muon_apply_kernel<false><<<grid, 256, 0, stream>>>(a);
+    muon_apply_kernel<false, false><<<grid, 256, 0, stream>>>(a);
 }
 
 void launch_grad_reduce(const GradReduceArgs& a, int num_sms, cudaStream_t stream) {

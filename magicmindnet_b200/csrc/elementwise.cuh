@@ -55,7 +55,7 @@ struct MuonMat {
 };
 
 struct MuonClassPtr {
-  __nv_bfloat16* x;   // class X buffer (batch x n x ld)
+  void* x;            // class X buffer (batch x n x ld): bf16, or fp32 when x_f32
   long long bstride;  // elements between batch items
   int ld;
   int pad;
@@ -83,6 +83,7 @@ struct MuonArgs {
   int apply_divides_norm;  // zero Newton-Schulz steps: O = bf16(u) / norm (lib.rs:110)
   int vec_ok;              // p / g / vel bases are 16-byte aligned: matrices with
                            // cols % 4 == 0 and off % 4 == 0 take the 128-bit path
+  int x_f32;               // TF32 mode: X is fp32 holding tf32(u) instead of bf16(u)
 };
 
 void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream);

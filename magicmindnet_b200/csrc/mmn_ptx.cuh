@@ -239,6 +239,26 @@ __device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, ui
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[smem] * B[smem]; tf32 inputs (fp32 words in shared memory),
+// fp32 accumulate (kind::tf32), on one CTA or on a CTA pair.
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void tc_mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrive on an mbarrier once every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
@@ -272,9 +292,10 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // ------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor (tcgen05 format, version 1) for a tile
 // stored with the 128-byte swizzle that TMA SWIZZLE_128B produces.
-//   K-major : rows of 64 bf16 (128 B); 8-row groups 1024 B apart (SBO).
-//   MN-major: 64 MN-elements per 128 B row, one row per K index; 8-K groups
-//             1024 B apart (SBO), 64-wide MN groups lbo_bytes apart (LBO).
+//   K-major : rows of 128 B (64 bf16 or 32 tf32); 8-row groups 1024 B apart (SBO).
+//   MN-major (bf16): 64 MN-elements per 128 B row, one row per K index; 8-K
+//             groups 1024 B apart (SBO), 64-wide MN groups lbo_bytes apart (LBO).
+//             MN-major tf32 uses umma_desc_sw128_32b instead.
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
                                                     uint32_t sbo_bytes) {
   uint64_t d = 0;
@@ -296,6 +317,35 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn_m
          | ((b_mn_major ? 1u : 0u) << 16)  // B major-ness
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Descriptor of an MN-major tf32 operand. tcgen05 reads MN-major 32-bit
+// operands only in the "128-byte swizzle with 32-byte atoms" layout (layout
+// type 1), which TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: 128-byte
+// rows of 32 MN-elements, one row per K index, 32-byte chunks XOR-swizzled by
+// the row index mod 4, so the pattern repeats every 4 K rows (512 B, SBO);
+// 128-byte-wide MN groups sit lbo_bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128_32b(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                        uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)1u << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
+// Instruction descriptor, kind::tf32: tf32 x tf32 -> fp32, M x N tile.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N, bool a_mn_major,
+                                                       bool b_mn_major) {
+  return (1u << 4)                       // D format: f32
+         | (2u << 7)                     // A format: tf32
+         | (2u << 10)                    // B format: tf32
+         | ((a_mn_major ? 1u : 0u) << 15)
+         | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace mmn

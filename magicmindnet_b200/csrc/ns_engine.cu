@@ -26,29 +26,37 @@ std::string get_encode() {
   return err;
 }
 
-// 3-D bf16 map (inner, rows, batch) with 128-byte swizzle; box (64, box_rows, 1).
+CUtensorMapDataType map_type(int esize) {
+  return esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// 3-D map (inner, rows, batch) of bf16 (esize 2) or fp32 (esize 4) elements
+// with 128-byte swizzle; box (128 bytes of inner elements, box_rows, 1).
+// atom32: swizzle 32-byte chunks instead of 16-byte ones, the layout tcgen05
+// needs for MN-major tf32 operands.
 std::string encode_3d(CUtensorMap* map, const void* base, int inner, int rows, int batch,
-                      int ld, int box_rows) {
+                      int ld, int box_rows, int esize, bool atom32 = false) {
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * (cuuint64_t)rows};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * esize, (cuuint64_t)ld * esize * (cuuint64_t)rows};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / esize), (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+  CUresult r = g_encode(map, map_type(esize), 3, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
   return "";
 }
 
-// 3-D bf16 map for TMA stores of 32 x 32 blocks (unswizzled, row-major stage).
+// 3-D map for TMA stores of 32 x 32 blocks (unswizzled, row-major stage).
 std::string encode_3d_store(CUtensorMap* map, const void* base, int inner, int rows, int batch,
-                            int ld) {
+                            int ld, int esize) {
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * esize, (cuuint64_t)ld * esize * (cuuint64_t)rows};
   cuuint32_t box[3] = {32, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+  CUresult r = g_encode(map, map_type(esize), 3, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -75,22 +83,23 @@ size_t sym_tiles_total(int n) {
 
 // Lays out the buffers of a class over `p` and encodes its tensor maps.
 std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
-                   std::vector<int2>* tiles) {
+                   std::vector<int2>* tiles, int esize) {
   c.n = n;
   c.m = m;
   c.batch = batch;
+  c.esize = esize;
   c.ld_x = round_up(m, 8);
   c.ld_a = round_up(n, 8);
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
   size_t off = 0;
-  c.x[0] = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.x_elems() * 2);
-  c.x[1] = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.x_elems() * 2);
-  c.a = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.a_elems() * 2);
-  c.a2 = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += al(c.a_elems() * 2);
+  c.x[0] = p + off;
+  off += al(c.x_elems() * esize);
+  c.x[1] = p + off;
+  off += al(c.x_elems() * esize);
+  c.a = p + off;
+  off += al(c.a_elems() * esize);
+  c.a2 = p + off;
+  off += al(c.a_elems() * esize);
   c.norms = reinterpret_cast<float*>(p + off);
   off += al((size_t)batch * 4);
   tiles->clear();
@@ -101,32 +110,38 @@ std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
   c.sym_tiles = reinterpret_cast<int2*>(p + off);
   c.sym_tiles2 = c.sym_tiles + c.n_sym_tiles;
   std::string err;
+  // MN-major X boxes: 128 bytes of columns by one stage of K rows (64 bf16 or
+  // 32 tf32 rows); K-major boxes: one stage of K columns by the operand's rows.
+  const int kb = 128 / esize;
+  const int e = esize;
   for (int i = 0; i < 2; ++i) {
-    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM)).empty()) return err;
-    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256)).empty()) return err;
-    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, batch, c.ld_x, 64)).empty()) return err;
+    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM, e)).empty()) return err;
+    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256, e)).empty()) return err;
+    // (in the TF32 mode X is read MN-major only through this map)
+    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, batch, c.ld_x, kb, e, e == 4)).empty())
+      return err;
   }
-  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, batch, c.ld_a, 64)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, batch, c.ld_a, 64)).empty()) return err;
-  if (!(err = encode_3d_store(&c.tm_a_out, c.a, n, n, batch, c.ld_a)).empty()) return err;
-  if (!(err = encode_3d_store(&c.tm_a2_out, c.a2, n, n, batch, c.ld_a)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, batch, c.ld_a, 64, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, batch, c.ld_a, 64, e)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a_out, c.a, n, n, batch, c.ld_a, e)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a2_out, c.a2, n, n, batch, c.ld_a, e)).empty()) return err;
   return "";
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
 cudaError_t set_smem() {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
-  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
+  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
 cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
                    const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
   if (args.num_tiles <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -149,8 +164,8 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
     if (max_pairs == 0) {
       cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
       int n = 0;
-      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>,
-                                                     &cfg);
+      cudaError_t e = cudaOccupancyMaxActiveClusters(
+          &n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>, &cfg);
       if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
       max_pairs = n < num_sms / 2 ? n : num_sms / 2;
     }
@@ -163,7 +178,8 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR>, a1, a2, b, args);
+  return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>, a1, a2, b,
+                            args);
 }
 
 // CTA pairs pay off once a matrix fills 256-row tiles.
@@ -183,22 +199,30 @@ std::string ns_gemm_setup() {
   MMN_SET(256, false, true, kEpiPolySingle)
 #undef MMN_SET
   if (e == cudaSuccess) e = set_smem<128, true, false, kEpiPolyDualT, true>();
+  // TF32 mode
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiGram, false, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiGram, true, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare, false, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare, true, true>();
+  if (e == cudaSuccess) e = set_smem<128, true, true, kEpiPolyDual, false, true>();
+  if (e == cudaSuccess) e = set_smem<128, true, false, kEpiPolyDualT, true, true>();
   if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
   return get_encode();
 }
 
-size_t ns_class_bytes(int n, int m, int batch) {
+size_t ns_class_bytes(int n, int m, int batch, int esize) {
   const size_t ld_x = (size_t)round_up(m, 8), ld_a = (size_t)round_up(n, 8);
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-  return 2 * al((size_t)batch * n * ld_x * 2) + 2 * al((size_t)batch * n * ld_a * 2) +
+  return 2 * al((size_t)batch * n * ld_x * esize) + 2 * al((size_t)batch * n * ld_a * esize) +
          al((size_t)batch * 4) + al(sym_tiles_total(n) * sizeof(int2));
 }
 
-std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
+std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base, int esize) {
   if (n <= 0 || m <= 0 || n > m || batch <= 0) return "invalid Newton-Schulz class shape";
+  if (esize != 2 && esize != 4) return "invalid Newton-Schulz element size";
   std::string err = get_encode();
   if (!err.empty()) return err;
-  const size_t bytes = ns_class_bytes(n, m, batch);
+  const size_t bytes = ns_class_bytes(n, m, batch, esize);
   uint8_t* p = static_cast<uint8_t*>(base);
   bool own = false;
   if (!p) {
@@ -206,7 +230,7 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
     own = true;
   }
   std::vector<int2> tiles;
-  err = layout(c, n, m, batch, p, &tiles);
+  err = layout(c, n, m, batch, p, &tiles, esize);
   c.owns_memory = own;
   if (!err.empty()) return err;
   // Padding columns of X and A are never read (the tensor maps stop at n / m);
@@ -219,13 +243,14 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base) {
 }
 
 std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
-                          std::vector<int2>* tiles_out) {
-  if (n <= 0 || m <= 0 || n > m || batch <= 0 || !base || !tiles_out)
+                          std::vector<int2>* tiles_out, int esize) {
+  if (n <= 0 || m <= 0 || n > m || batch <= 0 || !base || !tiles_out ||
+      (esize != 2 && esize != 4))
     return "invalid Newton-Schulz class shape or base";
   std::string err = get_encode();
   if (!err.empty()) return err;
   c = NsClass();
-  return layout(c, n, m, batch, static_cast<uint8_t*>(base), tiles_out);
+  return layout(c, n, m, batch, static_cast<uint8_t*>(base), tiles_out, esize);
 }
 
 void ns_class_free(NsClass& c) {
@@ -238,14 +263,14 @@ static constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;
 
 namespace {
 
-template <bool PAIR>
+template <bool PAIR, bool F32>
 cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int mode,
                           const NsGemmArgs& base, const NsFused* fused, int num_sms,
                           cudaStream_t stream) {
   const int tile_m = PAIR ? 2 * kBM : kBM;
   NsGemmArgs g = base;
 
-  // A = bf16((X X^T) / s / s)
+  // A = round((X X^T) / s / s), round = bf16, or tf32 in the TF32 mode
   g.out = c.a;
   g.out_bstride = (long long)c.n * c.ld_a;
   g.out_ld = c.ld_a;
@@ -260,27 +285,33 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
   g.num_tiles = g.tiles_per_matrix * c.batch;
   // B is the same X rows: 128 rows per CTA of a pair, 256 for a single CTA.
   const CUtensorMap& xb = PAIR ? c.tm_x_a[cur] : c.tm_x_b[cur];
-  cudaError_t e =
-      launch<256, false, false, kEpiGram, PAIR>(c.tm_x_a[cur], c.tm_a_out, xb, g, num_sms, stream);
+  cudaError_t e = launch<256, false, false, kEpiGram, PAIR, F32>(c.tm_x_a[cur], c.tm_a_out, xb, g,
+                                                                 num_sms, stream);
   if (e != cudaSuccess) return e;
 
-  // A2 = bf16(A A)   or   Bm = bf16(b*A + c*bf16(A A))
+  // A2 = round(A A)   or   Bm = bf16(b*A + c*bf16(A A))
   g.out = c.a2;
   g.norms = nullptr;
   g.K = c.n;
   const CUtensorMap& ab = PAIR ? c.tm_a_a : c.tm_a_b;
-  if (mode == kNsBf16) {
-    g.aux = c.a;
-    g.aux_bstride = (long long)c.n * c.ld_a;
-    g.aux_ld = c.ld_a;
-    e = launch<256, false, false, kEpiSquareBf16, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
-                                                       stream);
+  if constexpr (!F32) {
+    if (mode == kNsBf16) {
+      g.aux = c.a;
+      g.aux_bstride = (long long)c.n * c.ld_a;
+      g.aux_ld = c.ld_a;
+      e = launch<256, false, false, kEpiSquareBf16, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
+                                                         stream);
+    } else {
+      e = launch<256, false, false, kEpiSquare, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
+                                                      stream);
+    }
   } else {
-    e = launch<256, false, false, kEpiSquare, PAIR>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms, stream);
+    e = launch<256, false, false, kEpiSquare, PAIR, true>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
+                                                          stream);
   }
   if (e != cudaSuccess) return e;
 
-  // X' = bf16((X/s)*a + (b*(A X) + c*(A2 X))/s)   or   bf16((X/s)*a + (Bm X)/s)
+  // X' = round((X/s)*a + (b*(A X) + c*(A2 X))/s)   or   bf16((X/s)*a + (Bm X)/s)
   g.out = c.x[nxt];
   g.out_bstride = (long long)c.n * c.ld_x;
   g.out_ld = c.ld_x;
@@ -297,12 +328,14 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
     g.p_bf16 = fused->p_bf16;
     g.apply = fused->apply;
   }
-  if (mode == kNsBf16) {
-    g.tiles_n = (c.m + 255) / 256;
-    g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
-    g.num_tiles = g.tiles_per_matrix * c.batch;
-    return launch<256, false, true, kEpiPolySingle, PAIR>(c.tm_a2_a, c.tm_a2_a, c.tm_x_mn[cur], g,
-                                                          num_sms, stream);
+  if constexpr (!F32) {
+    if (mode == kNsBf16) {
+      g.tiles_n = (c.m + 255) / 256;
+      g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
+      g.num_tiles = g.tiles_per_matrix * c.batch;
+      return launch<256, false, true, kEpiPolySingle, PAIR>(c.tm_a2_a, c.tm_a2_a, c.tm_x_mn[cur],
+                                                            g, num_sms, stream);
+    }
   }
   // Two accumulators of 128 columns, double-buffered in TMEM. Measured against
   // 256-column dual tiles (single-buffered TMEM) and a stacked A|A2 pair that
@@ -312,14 +345,14 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
     g.tiles_n = (c.n + 127) / 128;
     g.tiles_per_matrix = ((c.m + 255) / 256) * g.tiles_n;
     g.num_tiles = g.tiles_per_matrix * c.batch;
-    return launch<128, true, false, kEpiPolyDualT, true>(c.tm_x_mn[cur], c.tm_a2_n, c.tm_a_n, g,
-                                                         num_sms, stream);
+    return launch<128, true, false, kEpiPolyDualT, true, F32>(c.tm_x_mn[cur], c.tm_a2_n, c.tm_a_n,
+                                                              g, num_sms, stream);
   }
   g.tiles_n = (c.m + 127) / 128;
   g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
   g.num_tiles = g.tiles_per_matrix * c.batch;
-  return launch<128, true, true, kEpiPolyDual, PAIR>(c.tm_a_a, c.tm_a2_a, c.tm_x_mn[cur], g,
-                                                     num_sms, stream);
+  return launch<128, true, true, kEpiPolyDual, PAIR, F32>(c.tm_a_a, c.tm_a2_a, c.tm_x_mn[cur], g,
+                                                          num_sms, stream);
 }
 
 }  // namespace
@@ -334,12 +367,22 @@ int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
   base.coef_b = kNsB;
   base.coef_c = kNsC;
   const bool pair = use_pairs(c);
+  const bool f32 = mode == kNsTf32;
+  if (c.esize != ns_elem_bytes(mode)) {
+    if (err) *err = "Newton-Schulz class buffers do not match the arithmetic mode";
+    return -1;
+  }
   for (int it = 0; it < steps; ++it) {
     const int nxt = cur ^ 1;
     const float* norms = it == 0 ? c.norms : nullptr;
     const NsFused* f = (fused && it == steps - 1) ? fused : nullptr;
-    cudaError_t e = pair ? run_iteration<true>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
-                         : run_iteration<false>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
+    cudaError_t e;
+    if (f32)
+      e = pair ? run_iteration<true, true>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
+               : run_iteration<false, true>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
+    else
+      e = pair ? run_iteration<true, false>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
+               : run_iteration<false, false>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
     if (e != cudaSuccess) {
       if (err) *err = std::string("Newton-Schulz GEMM launch: ") + cudaGetErrorString(e);
       return -1;

@@ -22,6 +22,13 @@
 // s is the per-matrix Frobenius norm in the first iteration (lib.rs:109-110)
 // and 1 afterwards. All operand values are exactly bf16, so the tensor-core
 // products are exact and only the fp32 summation order differs from the CPU.
+//
+// F32 = true instantiates the TF32 mode: the same three products and the same
+// rounding points, with every stored matrix (X, A, A2) held in fp32 words
+// rounded to tf32 (10-bit mantissa, round-to-nearest-even) instead of bf16,
+// and the MMAs issued as kind::tf32. A 128-byte swizzle row then holds 32
+// elements, so a stage covers K = 32 and one MMA K = 8; stage byte sizes and
+// the TMEM layout are the same as in bf16.
 // In the last iteration the Poly epilogue can apply the Muon update
 // p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
@@ -49,7 +56,6 @@ enum NsEpilogue : int {
 };
 
 constexpr int kBM = 128;  // rows per CTA (TMEM lanes)
-constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of bf16
 
 // Where the last iteration writes when it is fused with the Muon update.
 struct NsApply {
@@ -59,10 +65,10 @@ struct NsApply {
 };
 
 struct NsGemmArgs {
-  __nv_bfloat16* out;        // output matrices (bf16)
+  void* out;                 // output matrices (bf16, or tf32-valued fp32 for F32)
   long long out_bstride;     // elements between batch items
   int out_ld;                // elements between rows
-  const __nv_bfloat16* aux;  // epilogue input: X (Poly) or A (SquareBf16)
+  const void* aux;           // epilogue input: X (Poly) or A (SquareBf16), as out
   long long aux_bstride;
   int aux_ld;
   const float* norms;        // per-matrix divisor s (nullptr means 1)
@@ -79,8 +85,12 @@ struct NsGemmArgs {
   const int* skip;           // device non-finite flag: when set the launch does nothing
 };
 
-template <int BN, bool DUAL, bool B_MN, bool PAIR, int EPI>
+template <int BN, bool DUAL, bool B_MN, bool PAIR, int EPI, bool F32 = false>
 struct NsGemmShape {
+  static constexpr int kEsz = F32 ? 4 : 2;  // bytes per stored operand element
+  static constexpr int kBKe = 128 / kEsz;   // K per stage: one 128-byte swizzle row
+  static constexpr int kKi = 32 / kEsz;     // K per MMA instruction (32 bytes)
+  static constexpr int kMNe = 128 / kEsz;   // MN elements per 128-byte row of an MN-major box
   // transposed Poly: one A operand (X^T, MN-major) and a B operand of stacked
   // A and A2 rows
   static constexpr bool SWAP = EPI == kEpiPolyDualT;
@@ -88,11 +98,20 @@ struct NsGemmShape {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kTileM = kBM * kCtas;        // output rows per tile
   static constexpr int kBNc = BN / kCtas;           // B columns loaded by one CTA
-  static constexpr int kABytes = kBM * kBK * 2;     // 16 KB per A operand
-  static constexpr int kBBytes = kBNc * kBK * 2;
+  static constexpr int kABytes = kBM * 128;         // 16 KB per A operand
+  static constexpr int kBBytes = kBNc * 128;
   static constexpr int kStageBytes =
       SWAP ? kABytes + 2 * kBBytes : kABytes * (DUAL ? 2 : 1) + kBBytes;
-  static constexpr int kStages = (204800 / kStageBytes) < 8 ? (204800 / kStageBytes) : 8;
+  // per epilogue warp: two 32 x 32 blocks of the symmetric output (direct and
+  // mirrored, staged for TMA stores), or (SWAP) a 32 x 33 fp32 tile that turns
+  // lane-per-column values into lane-per-row ones
+  static constexpr int kEpiWarpBytes = SWAP ? 32 * 33 * 4 : (SYM ? 2 * 32 * 32 * kEsz : 0);
+  // bf16: at most 200 KB of stages; tf32: whatever the larger fp32 epilogue
+  // stage leaves of the 227 KB
+  static constexpr int kStageBudget =
+      F32 ? 232448 - 2048 - 8 * kEpiWarpBytes : 204800;
+  static constexpr int kStages =
+      (kStageBudget / kStageBytes) < 8 ? (kStageBudget / kStageBytes) : 8;
   static constexpr int kAccCols = BN * (DUAL ? 2 : 1);  // per accumulator buffer
   // two accumulator buffers when they fit in TMEM's 512 columns, else one
   // (the MMA of the next tile then waits for the epilogue)
@@ -103,15 +122,14 @@ struct NsGemmShape {
   // tile's column chunks, so that the epilogue keeps pace with short K loops.
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  // per epilogue warp: two 32 x 32 bf16 blocks (symmetric outputs: the direct
-  // and the mirrored block for TMA stores), or (SWAP) a 32 x 33 fp32 tile that
-  // turns lane-per-column values into lane-per-row ones
-  static constexpr int kEpiBytes =
-      kEpiWarps * (SWAP ? 32 * 33 * 4 : (SYM ? 2 * 32 * 32 * 2 : 0));
+  static constexpr int kEpiBytes = kEpiWarps * kEpiWarpBytes;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiBytes + 1024;
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kStages >= 2, "pipeline needs two stages");
-  static_assert(!B_MN || kBNc % 64 == 0, "MN-major B is loaded in 64-column boxes");
+  static_assert(!B_MN || kBNc % kMNe == 0, "MN-major B is loaded in 128-byte-wide boxes");
+  static_assert(kEpiWarps == 8, "the stage budget counts eight epilogue warps");
+  static_assert(!F32 || (EPI != kEpiSquareBf16 && EPI != kEpiPolySingle),
+                "the bf16 mode has no tf32 form");
   static_assert(!SWAP || (DUAL && !B_MN && PAIR && kBNc == 64), "transposed Poly: pairs, dual");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
@@ -123,6 +141,42 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ float bf16r(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Round an fp32 value to tf32 (the 10 leading mantissa bits), to nearest with
+// ties to even on the 13 discarded bits, written from the IEEE-754 definition.
+// Inf and NaN pass through unchanged.
+__device__ __forceinline__ float tf32r(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+  return __uint_as_float(u);
+}
+
+// The rounding point of the stored matrices: bf16, or tf32 in the TF32 mode.
+template <bool F32>
+__device__ __forceinline__ float op_round(float x) {
+  if constexpr (F32)
+    return tf32r(x);
+  else
+    return bf16r(x);
+}
+
+// 32 consecutive fp32 <-> float[32] (16-byte aligned).
+__device__ __forceinline__ void load_f32x32(const float* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 u = *reinterpret_cast<const float4*>(src + q * 4);
+    v[q * 4 + 0] = u.x;
+    v[q * 4 + 1] = u.y;
+    v[q * 4 + 2] = u.z;
+    v[q * 4 + 3] = u.w;
+  }
+}
+__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(dst + q * 4) =
+        make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
 }
 
 // 32 consecutive bf16 -> float (16-byte aligned source).
@@ -154,37 +208,60 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
 }
 
 // Last step of every Poly epilogue for one row r and 32 columns c0..c0+31,
-// given bx = (b*A X + c*A2 X) or Bm X: o = bf16((X/s)*a + bx/s), stored as X'
-// or, in the last iteration, applied as p -= lr*scale*o in the parameter's
-// orientation (lib.rs:169-174). bx is overwritten with o.
+// given bx = (b*A X + c*A2 X) or Bm X: o = round((X/s)*a + bx/s) (bf16, or tf32
+// for F32), stored as X' or, in the last iteration, applied as
+// p -= lr*scale*o in the parameter's orientation (lib.rs:169-174). bx is
+// overwritten with o.
+template <bool F32>
 __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r, int c0,
                                             bool row_ok, bool cols_full, float s,
                                             float (&v)[32]) {
-  const __nv_bfloat16* xrow = args.aux + (long long)b * args.aux_bstride +
-                              (long long)r * args.aux_ld + c0;
+  const long long xoff = (long long)b * args.aux_bstride + (long long)r * args.aux_ld + c0;
   float xv[32];
-  if (row_ok && cols_full) {
-    load_bf16x32(xrow, xv);
-  } else {
+  if constexpr (F32) {
+    const float* xrow = static_cast<const float*>(args.aux) + xoff;
+    if (row_ok && cols_full) {
+      load_f32x32(xrow, xv);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      xv[j] = (row_ok && c0 + j < args.N) ? __bfloat162float(xrow[j]) : 0.0f;
+      for (int j = 0; j < 32; ++j) xv[j] = (row_ok && c0 + j < args.N) ? xrow[j] : 0.0f;
+    }
+  } else {
+    const __nv_bfloat16* xrow = static_cast<const __nv_bfloat16*>(args.aux) + xoff;
+    if (row_ok && cols_full) {
+      load_bf16x32(xrow, xv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        xv[j] = (row_ok && c0 + j < args.N) ? __bfloat162float(xrow[j]) : 0.0f;
+    }
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float x0 = s != 1.0f ? __fdiv_rn(xv[j], s) : xv[j];
     const float bs = s != 1.0f ? __fdiv_rn(v[j], s) : v[j];
-    v[j] = bf16r(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
+    v[j] = op_round<F32>(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
   }
   if (!args.p) {
-    __nv_bfloat16* orow =
-        args.out + (long long)b * args.out_bstride + (long long)r * args.out_ld + c0;
-    if (row_ok && cols_full) {
-      store_bf16x32(orow, v);
-    } else if (row_ok) {
+    const long long ooff = (long long)b * args.out_bstride + (long long)r * args.out_ld + c0;
+    if constexpr (F32) {
+      float* orow = static_cast<float*>(args.out) + ooff;
+      if (row_ok && cols_full) {
+        store_f32x32(orow, v);
+      } else if (row_ok) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < args.N) orow[j] = v[j];
+      }
+    } else {
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(args.out) + ooff;
+      if (row_ok && cols_full) {
+        store_bf16x32(orow, v);
+      } else if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < args.N) orow[j] = __float2bfloat16_rn(v[j]);
+      }
     }
     return;
   }
@@ -231,13 +308,31 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
   }
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR>
+// One MMA of the tile's element type, on one CTA or on the pair.
+template <bool F32, bool PAIR>
+__device__ __forceinline__ void ns_mma(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc,
+                                       uint32_t accum) {
+  if constexpr (F32) {
+    if constexpr (PAIR)
+      tc_mma_tf32_pair(d, da, db, idesc, accum);
+    else
+      tc_mma_tf32(d, da, db, idesc, accum);
+  } else {
+    if constexpr (PAIR)
+      tc_mma_bf16_pair(d, da, db, idesc, accum);
+    else
+      tc_mma_bf16(d, da, db, idesc, accum);
+  }
+}
+
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
 __global__ void __launch_bounds__(320, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
   constexpr bool kSwap = EPI == kEpiPolyDualT;
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
+  constexpr int kBK = S::kBKe;  // K per stage
   constexpr int STAGES = S::kStages;
   constexpr bool kSym = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -252,8 +347,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* drain = bars + 2 * STAGES + 4;   // abort path: MMA completion
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 6);
-  __nv_bfloat16* epi_stage =
-      reinterpret_cast<__nv_bfloat16*>(smem + STAGES * S::kStageBytes + S::kBarBytes);
+  uint8_t* epi_stage = smem + STAGES * S::kStageBytes + S::kBarBytes;
 
   // Launched as a programmatic dependent: nothing of the previous kernel's output
   // (X, A, A2, the skip flag) is read before it has completed. The next kernel
@@ -342,8 +436,9 @@ __global__ void __launch_bounds__(320, 1)
             // A side: X^T rows row0.. = X columns, two 64-column MN-major boxes;
             // B side: rows col0.. of A (tm_b) and of A2 (tm_a2), K-major.
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_3d_pair(st, &tm_a1, fb, row0, k0, b);
-            tma_load_3d_pair(st + kBK * 128, &tm_a1, fb, row0 + 64, k0, b);
+#pragma unroll
+            for (int g = 0; g < kBM / S::kMNe; ++g)  // 2 (bf16) or 4 (tf32) boxes
+              tma_load_3d_pair(st + g * (kBK * 128), &tm_a1, fb, row0 + g * S::kMNe, k0, b);
             tma_load_3d_pair(st + S::kABytes, &tm_b, fb, k0, col0, b);
             tma_load_3d_pair(st + S::kABytes + S::kBBytes, &tm_a2, fb, k0, col0, b);
           } else if (PAIR) {
@@ -352,8 +447,8 @@ __global__ void __launch_bounds__(320, 1)
             if (DUAL) tma_load_3d_pair(st + S::kABytes, &tm_a2, fb, k0, row0, b);
             if (B_MN) {
 #pragma unroll
-              for (int g = 0; g < S::kBNc / 64; ++g)
-                tma_load_3d_pair(sb + g * (kBK * 128), &tm_b, fb, col0 + g * 64, k0, b);
+              for (int g = 0; g < S::kBNc / S::kMNe; ++g)
+                tma_load_3d_pair(sb + g * (kBK * 128), &tm_b, fb, col0 + g * S::kMNe, k0, b);
             } else {
               tma_load_3d_pair(sb, &tm_b, fb, k0, col0, b);
             }
@@ -362,8 +457,9 @@ __global__ void __launch_bounds__(320, 1)
             if (DUAL) tma_load_3d(st + S::kABytes, &tm_a2, &full[stage], k0, row0, b);
             if (B_MN) {
 #pragma unroll
-              for (int g = 0; g < S::kBNc / 64; ++g)
-                tma_load_3d(sb + g * (kBK * 128), &tm_b, &full[stage], col0 + g * 64, k0, b);
+              for (int g = 0; g < S::kBNc / S::kMNe; ++g)
+                tma_load_3d(sb + g * (kBK * 128), &tm_b, &full[stage], col0 + g * S::kMNe, k0,
+                            b);
             } else {
               tma_load_3d(sb, &tm_b, &full[stage], k0, col0, b);
             }
@@ -396,7 +492,19 @@ __global__ void __launch_bounds__(320, 1)
     // ----------------------------------------------------------- MMA issue
     if (lane == 0 && leader) {
       // (transposed Poly: one N = 2*BN MMA over the stacked [A rows | A2 rows])
-      constexpr uint32_t idesc = umma_idesc_bf16(S::kTileM, kSwap ? 2 * BN : BN, kSwap, B_MN);
+      constexpr uint32_t idesc =
+          F32 ? umma_idesc_tf32(S::kTileM, kSwap ? 2 * BN : BN, kSwap, B_MN)
+              : umma_idesc_bf16(S::kTileM, kSwap ? 2 * BN : BN, kSwap, B_MN);
+      constexpr int kKSteps = kBK / S::kKi;  // MMAs per stage (4)
+      constexpr uint32_t kMnStep = S::kKi * 128;  // MN-major operand: bytes per MMA K
+      // MN-major operand descriptor: bf16 in the 128-byte swizzle (8-row
+      // pattern), tf32 in the 32-byte-atom 128-byte swizzle (4-row pattern)
+      auto mn_desc = [](uint32_t addr) -> uint64_t {
+        if constexpr (F32)
+          return umma_desc_sw128_32b(addr, kBK * 128, 512);
+        else
+          return umma_desc_sw128(addr, kBK * 128, 1024);
+      };
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -424,28 +532,22 @@ __global__ void __launch_bounds__(320, 1)
             // peer's 64 rows.
             const uint32_t b1 = a1 + S::kABytes;
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t da = umma_desc_sw128(a1 + kk * 2048, kBK * 128, 1024);
+            for (int kk = 0; kk < kKSteps; ++kk) {
+              const uint64_t da = mn_desc(a1 + kk * kMnStep);
               const uint64_t db = umma_desc_sw128(b1 + kk * 32, 16, 1024);
-              tc_mma_bf16_pair(d1, da, db, idesc, (kb | kk) != 0);
+              ns_mma<F32, true>(d1, da, db, idesc, (kb | kk) != 0);
             }
           }
 #pragma unroll
-          for (int kk = 0; kk < (kSwap ? 0 : kBK / 16); ++kk) {
+          for (int kk = 0; kk < (kSwap ? 0 : kKSteps); ++kk) {
             const uint64_t da1 = umma_desc_sw128(a1 + kk * 32, 16, 1024);
-            const uint64_t db = B_MN ? umma_desc_sw128(bb + kk * 2048, kBK * 128, 1024)
+            const uint64_t db = B_MN ? mn_desc(bb + kk * kMnStep)
                                      : umma_desc_sw128(bb + kk * 32, 16, 1024);
             const uint32_t accum = (kb | kk) != 0;
-            if (PAIR)
-              tc_mma_bf16_pair(d1, da1, db, idesc, accum);
-            else
-              tc_mma_bf16(d1, da1, db, idesc, accum);
+            ns_mma<F32, PAIR>(d1, da1, db, idesc, accum);
             if (DUAL) {
               const uint64_t da2 = umma_desc_sw128(a2 + kk * 32, 16, 1024);
-              if (PAIR)
-                tc_mma_bf16_pair(d2, da2, db, idesc, accum);
-              else
-                tc_mma_bf16(d2, da2, db, idesc, accum);
+              ns_mma<F32, PAIR>(d2, da2, db, idesc, accum);
             }
           }
           issued_any = true;
@@ -486,8 +588,8 @@ __global__ void __launch_bounds__(320, 1)
     // column chunks of a tile this warp finishes: [ch_lo, ch_hi)
     constexpr int kChunksPerWarp = (BN / 32) / (S::kEpiWarps / 4);
     const int ch_lo = ((warp - 2) >> 2) * kChunksPerWarp, ch_hi = ch_lo + kChunksPerWarp;
-    // symmetric outputs: two 32 x 32 bf16 blocks per warp (direct, mirror)
-    __nv_bfloat16* stg = epi_stage + (warp - 2) * 2 * 32 * 32;
+    // symmetric outputs: two 32 x 32 blocks per warp (direct, mirror)
+    uint8_t* stg = epi_stage + (warp - 2) * S::kEpiWarpBytes;
     const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -523,8 +625,11 @@ __global__ void __launch_bounds__(320, 1)
       const int r = rw + lane;
       const uint32_t tbase = tmem_base + acc * S::kAccCols + ((uint32_t)(sub * 32) << 16);
       const float s = args.norms ? args.norms[b] : 1.0f;
-      __nv_bfloat16* out = args.out + (long long)b * args.out_bstride;
-      const __nv_bfloat16* aux = args.aux ? args.aux + (long long)b * args.aux_bstride : nullptr;
+      // SquareBf16 epilogue input (bf16 A of this batch item)
+      const __nv_bfloat16* aux =
+          (!F32 && args.aux)
+              ? static_cast<const __nv_bfloat16*>(args.aux) + (long long)b * args.aux_bstride
+              : nullptr;
       // (transposed Poly: the TMEM lanes run along X' columns, the
       // accumulator columns along X' rows)
       const int lane_dim = kSwap ? args.N : args.M, col_dim = kSwap ? args.M : args.N;
@@ -552,9 +657,10 @@ __global__ void __launch_bounds__(320, 1)
           // This tile owns the symmetric entries with col >= row and writes each
           // at (r, c) and, through a transposing smem stage, at (c, r).
           if (c0 + 31 < rw) continue;  // block entirely below the diagonal
-          if (EPI == kEpiSquareBf16) {
+          if constexpr (EPI == kEpiSquareBf16) {
             float a_in[32];
-            const __nv_bfloat16* arow = aux + (long long)r * args.aux_ld + c0;
+            const __nv_bfloat16* arow =
+                static_cast<const __nv_bfloat16*>(aux) + (long long)r * args.aux_ld + c0;
             if (row_ok && cols_full) {
               load_bf16x32(arow, a_in);
             } else {
@@ -580,26 +686,39 @@ __global__ void __launch_bounds__(320, 1)
           const bool diag = c0 == rw;
           if (lane == 0) bulk_wait_read_all();  // this warp's previous stores read their stage
           __syncwarp();
-          uint4* drow = reinterpret_cast<uint4*>(stg + lane * 32);
+          uint8_t* mir_base = stg + 32 * 32 * S::kEsz;
+          if constexpr (F32) {
+            float* drow = reinterpret_cast<float*>(stg) + lane * 32;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u;
-            u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-            u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-            u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-            u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-            drow[q] = u;
+            for (int j = 0; j < 32; ++j) v[j] = tf32r(v[j]);
+            store_f32x32(drow, v);
+            float* mir = reinterpret_cast<float*>(diag ? stg : mir_base);
+            if (diag) __syncwarp();  // the lower triangle overwrites direct values
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (!diag || j > lane) mir[j * 32 + lane] = v[j];
+          } else {
+            uint4* drow = reinterpret_cast<uint4*>(stg) + lane * 4;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+              u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+              u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+              u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+              drow[q] = u;
+            }
+            __nv_bfloat16* mir = reinterpret_cast<__nv_bfloat16*>(diag ? stg : mir_base);
+            if (diag) __syncwarp();  // the lower triangle overwrites direct values
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (!diag || j > lane) mir[j * 32 + lane] = __float2bfloat16_rn(v[j]);
           }
-          __nv_bfloat16* mir = diag ? stg : stg + 32 * 32;
-          if (diag) __syncwarp();  // the lower triangle overwrites direct values
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (!diag || j > lane) mir[j * 32 + lane] = __float2bfloat16_rn(v[j]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
             tma_store_3d(&tm_a2, stg, c0, rw, b);
-            if (!diag) tma_store_3d(&tm_a2, stg + 32 * 32, rw, c0, b);
+            if (!diag) tma_store_3d(&tm_a2, mir_base, rw, c0, b);
             bulk_commit();
           }
         } else {
@@ -619,9 +738,9 @@ __global__ void __launch_bounds__(320, 1)
             for (int j = 0; j < 32; ++j) v[j] = tst[lane * 33 + j];
             __syncwarp();
             const int xr = c0 + lane;
-            poly_finish(args, b, xr, rw, xr < args.M, rw + 32 <= args.N, s, v);
+            poly_finish<F32>(args, b, xr, rw, xr < args.M, rw + 32 <= args.N, s, v);
           } else {
-            poly_finish(args, b, r, c0, row_ok, cols_full, s, v);
+            poly_finish<F32>(args, b, r, c0, row_ok, cols_full, s, v);
           }
         }
       }

@@ -224,6 +224,27 @@ void ref_gemm(const float *A, const float *B, float *C, int64_t M, int64_t N, in
     }
 }
 
+/*
+ * tf32 round-to-nearest-even on the f32 bit pattern: keep the sign, the
+ * exponent and the 10 leading mantissa bits, round on the 13 discarded bits,
+ * ties to the even kept value. Inf and NaN pass through. The rounding point of
+ * the TF32 Newton-Schulz mode (REF_NS_TF32), which has no reference
+ * counterpart.
+ */
+float ref_tf32_round(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+/* The rounding point of a Newton-Schulz variant: bf16, or tf32 for REF_NS_TF32. */
+static float ns_round(float x, int variant) {
+    return variant == REF_NS_TF32 ? ref_tf32_round(x) : ref_bf16_round(x);
+}
+
 /* --------------------------------------------------------- Newton-Schulz -- */
 static const float NS_A = 3.4445f, NS_B = -4.7750f, NS_C = 2.0315f; /* lib.rs:84-86 */
 static const float NS_EPS = 1e-7f;                                  /* lib.rs:87 */
@@ -236,6 +257,7 @@ static const float NS_EPS = 1e-7f;                                  /* lib.rs:87
  *   B    = A_bf*b + A2*c                 (:117, kept fp32)
  *   x'   = bf16(x*a + B*x)               (:118-119)
  * REF_NS_BF16 additionally rounds B to bf16 (no reference counterpart).
+ * REF_NS_TF32 rounds to tf32 wherever the reference rounds to bf16.
  */
 void ref_ns_iteration(const float *x, int64_t n, int64_t m, float *x_next, int gemm_order,
                       int variant, int n_threads) {
@@ -246,15 +268,15 @@ void ref_ns_iteration(const float *x, int64_t n, int64_t m, float *x_next, int g
     for (int64_t i = 0; i < n; ++i)
         for (int64_t j = 0; j < m; ++j) xt[j * n + i] = x[i * m + j];
     ref_gemm(x, xt, a, n, n, m, gemm_order, n_threads);
-    for (int64_t i = 0; i < n * n; ++i) a[i] = ref_bf16_round(a[i]);
+    for (int64_t i = 0; i < n * n; ++i) a[i] = ns_round(a[i], variant);
     ref_gemm(a, a, a2, n, n, n, gemm_order, n_threads);
     for (int64_t i = 0; i < n * n; ++i) {
-        float sq = ref_bf16_round(a2[i]);
+        float sq = ns_round(a2[i], variant);
         float b = a[i] * NS_B + sq * NS_C;
         a2[i] = variant == REF_NS_BF16 ? ref_bf16_round(b) : b;
     }
     ref_gemm(a2, x, bx, n, m, n, gemm_order, n_threads);
-    for (int64_t i = 0; i < n * m; ++i) x_next[i] = ref_bf16_round(x[i] * NS_A + bx[i]);
+    for (int64_t i = 0; i < n * m; ++i) x_next[i] = ns_round(x[i] * NS_A + bx[i], variant);
     free(xt);
     free(a);
     free(a2);
@@ -276,7 +298,7 @@ int ref_newton_schulz5(const float *g, int64_t rows, int64_t cols, int steps, fl
     float *y = (float *)malloc(sizeof(float) * (size_t)(n * m));
     for (int64_t i = 0; i < n; ++i)
         for (int64_t j = 0; j < m; ++j)
-            x[i * m + j] = ref_bf16_round(transposed ? g[j * cols + i] : g[i * cols + j]);
+            x[i * m + j] = ns_round(transposed ? g[j * cols + i] : g[i * cols + j], variant);
     float s = 0.0f;
     for (int64_t i = 0; i < n * m; ++i) s = s + x[i] * x[i];
     float norm = fmaxf(sqrtf(s), NS_EPS);

@@ -38,10 +38,14 @@ enum {
 /* Newton-Schulz recipe variants. */
 enum {
     REF_NS_REFERENCE = 0, /* lib.rs:112-120 exactly: B = b*A_bf + c*A2_bf kept fp32 */
-    REF_NS_BF16 = 1       /* fast variant (no reference counterpart): B rounded to bf16 */
+    REF_NS_BF16 = 1,      /* fast variant (no reference counterpart): B rounded to bf16 */
+    REF_NS_TF32 = 2       /* TF32 mode (no reference counterpart): the REF_NS_REFERENCE
+                             recipe with every bf16 rounding point of lib.rs:104,115,116,119
+                             replaced by a tf32 rounding (10-bit mantissa, nearest-even) */
 };
 
 float ref_bf16_round(float x);
+float ref_tf32_round(float x);
 
 /* AdamW::step_param (lib.rs:41-60) for one tensor whose step counter is already t. */
 void ref_adamw_step(float *p, float *m, float *v, const float *g, int64_t n,

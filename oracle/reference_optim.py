@@ -28,7 +28,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libmmn_optim_ref.so")
 
 GEMM_F32_SEQ, GEMM_F32_FMA, GEMM_F64 = 0, 1, 2
-NS_REFERENCE, NS_BF16 = 0, 1
+NS_REFERENCE, NS_BF16, NS_TF32 = 0, 1, 2
 
 _f = ctypes.c_float
 _i64 = ctypes.c_int64
@@ -52,6 +52,8 @@ def lib():
         L = ctypes.CDLL(_LIB_PATH)
         L.ref_bf16_round.restype = _f
         L.ref_bf16_round.argtypes = [_f]
+        L.ref_tf32_round.restype = _f
+        L.ref_tf32_round.argtypes = [_f]
         L.ref_adamw_step.argtypes = [_fp, _fp, _fp, _fp, _i64, _f, _f, _f, _f, _f, _i64, _f]
         L.ref_adamw_step_timed.restype = ctypes.c_double
         L.ref_adamw_step_timed.argtypes = [_fp, _fp, _fp, _fp, _i64, _f, _f, _f, _f, _f,
@@ -88,6 +90,17 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     up = (lo > 0x8000) | ((lo == 0x8000) & ((hi & 1) == 1))
     r = ((hi + up.astype(np.uint64)) << 16)
     r = np.where(nan, (u | 0x00400000) & 0xFFFF0000, r)
+    return r.astype(np.uint32).view(np.float32).reshape(x.shape)
+
+
+def tf32_round(x: np.ndarray) -> np.ndarray:
+    """Vectorised tf32 round-to-nearest-even of finite values (same rule as
+    ref_tf32_round): 10 mantissa bits kept, rounding on the 13 dropped."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = (u + 0xFFF + ((u >> 13) & 1)) & 0xFFFFE000
+    keep = (u & 0x7F800000) == 0x7F800000
+    r = np.where(keep, u, r)
     return r.astype(np.uint32).view(np.float32).reshape(x.shape)
 
 

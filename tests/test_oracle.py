@@ -113,6 +113,58 @@ def test_ns_scaled_identity_follows_scalar_recurrence(oracle):
     np.testing.assert_allclose(np.diag(out), np.full(n, x), rtol=0, atol=0)
 
 
+def test_tf32_round_known_answers(oracle):
+    """Nearest-even on the 13 dropped mantissa bits; exact values unchanged."""
+    f = np.float32
+    cases = {
+        0x3F800000: 0x3F800000,  # 1.0 exact
+        0x3F801000: 0x3F800000,  # tie, kept value even -> down
+        0x3F803000: 0x3F804000,  # tie, kept value odd -> up
+        0x3F800FFF: 0x3F800000,  # below half -> down
+        0x3F801001: 0x3F802000,  # above half -> up
+        0xBF803000: 0xBF804000,  # sign kept
+        0x7F800000: 0x7F800000,  # inf
+    }
+    for src, want in cases.items():
+        x = np.array([src], np.uint32).view(f)
+        assert oracle.tf32_round(x).view(np.uint32)[0] == want, hex(src)
+        assert np.array([oracle.lib().ref_tf32_round(float(x[0]))], f).view(np.uint32)[0] == want
+
+
+def test_ns_tf32_scaled_identity_follows_scalar_recurrence(oracle):
+    """The TF32 recipe on s*I_n: every diagonal entry follows
+    x <- tf32(a*x + (b*tf32(x^2) + c*tf32(tf32(x^2)^2)) * x) from x0 = 1/sqrt(n)."""
+    n = 8
+    out = oracle.newton_schulz5(np.eye(n, dtype=np.float32) * 0.37, variant=oracle.NS_TF32)
+    assert np.count_nonzero(out - np.diag(np.diag(out))) == 0
+    t = lambda v: oracle.tf32_round(np.array([v], np.float32))[0]
+    y = t(np.float32(0.37))
+    s = np.float32(0)
+    for _ in range(n):
+        s = np.float32(s + np.float32(y * y))
+    x = np.float32(y / np.float32(np.sqrt(s)))
+    a, b, c = np.float32(3.4445), np.float32(-4.7750), np.float32(2.0315)
+    for _ in range(5):
+        x2 = t(np.float32(x * x))
+        x4 = t(np.float32(x2 * x2))
+        x = t(np.float32(x * a + np.float32(np.float32(x2 * b) + np.float32(x4 * c)) * x))
+    np.testing.assert_allclose(np.diag(out), np.full(n, x), rtol=0, atol=0)
+
+
+def test_ns_tf32_recipe_is_closer_to_exact_than_bf16(oracle):
+    """The TF32 mode's reason to exist: on a 128 x 384 input it ends several
+    times closer to Newton-Schulz without rounding than the bf16 recipe."""
+    g = np.random.default_rng(8).normal(0, 1e-2, (128, 384)).astype(np.float32)
+    x = g.astype(np.float64) / np.linalg.norm(g.astype(np.float64))
+    for _ in range(5):
+        a = x @ x.T
+        x = 3.4445 * x + (-4.7750 * a + 2.0315 * (a @ a)) @ x
+    t = oracle.newton_schulz5(g, order=oracle.GEMM_F64, variant=oracle.NS_TF32)
+    b = oracle.newton_schulz5(g, order=oracle.GEMM_F64)
+    err = lambda o: np.linalg.norm(o - x) / np.linalg.norm(x)
+    assert err(t) < 4e-3 and err(t) * 4 < err(b)
+
+
 def test_ns_transpose_rule_exact(oracle):
     rng = np.random.default_rng(2)
     g = rng.normal(0, 1e-2, (24, 40)).astype(np.float32)
