@@ -224,38 +224,58 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
                                                    float mu, float one_m) {
   const int cq = (threadIdx.x & 15) * 4;
   const int rs = threadIdx.x >> 4;
-  float ss = 0.0f;
-  for (int rr = rs; rr < kTile; rr += 16) {
-    const int r = r0 + rr, c = c0 + cq;
-    float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (r < mm.rows && c < mm.cols) {
-      const long long idx = mm.off + (long long)r * mm.cols + c;
-      float g[4];
+  constexpr int kRounds = kTile / 16;  // rows rs, rs + 16, rs + 32, rs + 48
+  // All of the thread's loads are issued before any store, so that 8 x 16 B
+  // (fp32 grads) per thread are in flight at once.
+  float g[kRounds][4];
+  float vv[kRounds][4];
+  bool ok[kRounds];
+#pragma unroll
+  for (int q = 0; q < kRounds; ++q) {
+    const int r = r0 + rs + 16 * q, c = c0 + cq;
+    ok[q] = r < mm.rows && c < mm.cols;
+    const long long idx = mm.off + (long long)r * mm.cols + c;
+    if (ok[q]) {
       if (BF16G) {
         const uint2 raw = *reinterpret_cast<const uint2*>(a.g_bf16 + idx);
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
         const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-        g[0] = f0.x;
-        g[1] = f0.y;
-        g[2] = f1.x;
-        g[3] = f1.y;
+        g[q][0] = f0.x;
+        g[q][1] = f0.y;
+        g[q][2] = f1.x;
+        g[q][3] = f1.y;
       } else {
         const float4 g4 = __ldcs(reinterpret_cast<const float4*>(a.g + idx));
-        g[0] = g4.x;
-        g[1] = g4.y;
-        g[2] = g4.z;
-        g[3] = g4.w;
+        g[q][0] = g4.x;
+        g[q][1] = g4.y;
+        g[q][2] = g4.z;
+        g[q][3] = g4.w;
       }
-      float4 v4 = FRESH ? make_float4(0.f, 0.f, 0.f, 0.f)
-                        : __ldcs(reinterpret_cast<const float4*>(a.vel + idx));
-      float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+      const float4 v4 = FRESH ? make_float4(0.f, 0.f, 0.f, 0.f)
+                              : __ldcs(reinterpret_cast<const float4*>(a.vel + idx));
+      vv[q][0] = v4.x;
+      vv[q][1] = v4.y;
+      vv[q][2] = v4.z;
+      vv[q][3] = v4.w;
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kRounds; ++q) {
+    const int rr = rs + 16 * q;
+    const int r = r0 + rr, c = c0 + cq;
+    float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (ok[q]) {
+      const long long idx = mm.off + (long long)r * mm.cols + c;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        if (scale != 1.0f) g[e] = __fdiv_rn(g[e], scale);
-        if (a.grad_divisor != 1.0f) g[e] = __fdiv_rn(g[e], a.grad_divisor);
-        y[e] = momentum_elem<F32X>(g[e], vv[e], mu, one_m, a.nesterov);
+        float ge = g[q][e];
+        if (scale != 1.0f) ge = __fdiv_rn(ge, scale);
+        if (a.grad_divisor != 1.0f) ge = __fdiv_rn(ge, a.grad_divisor);
+        y[e] = momentum_elem<F32X>(ge, vv[q][e], mu, one_m, a.nesterov);
       }
-      __stcs(reinterpret_cast<float4*>(a.vel + idx), make_float4(vv[0], vv[1], vv[2], vv[3]));
+      __stcs(reinterpret_cast<float4*>(a.vel + idx),
+             make_float4(vv[q][0], vv[q][1], vv[q][2], vv[q][3]));
       if (!mm.transposed && F32X) {
         *reinterpret_cast<float4*>(static_cast<float*>(Xv) + (long long)r * ld + c) =
             make_float4(y[0], y[1], y[2], y[3]);
@@ -312,8 +332,11 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
 // newton_schulz5 (lib.rs:101-107) + per-tile sums of squares of the bf16
 // values (lib.rs:109), all in one pass over g and vel. F32X: the TF32 mode's
 // tf32 cast into an fp32 X.
+// Four 256-thread blocks per SM (at most 64 registers a thread, 16.6 KB of
+// shared memory a block), launched as one wave that strides over the tiles.
+constexpr int kMomentumBlocksPerSm = 4;
 template <bool BF16G, bool FRESH, bool F32X>
-__global__ void __launch_bounds__(256) muon_momentum_kernel(const MuonArgs a) {
+__global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   __shared__ float red[8];
   if (a.skip && *a.skip) return;
@@ -607,7 +630,7 @@ void launch_adamw(const AdamwArgs& a, int num_sms, cudaStream_t stream) {
 
 void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
   if (a.total_tiles <= 0) return;
-  const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
+  const int grid = grid_for(a.total_tiles, 1, num_sms, kMomentumBlocksPerSm);
   const bool bf = a.g_bf16 != nullptr, fresh = a.fresh_state != 0;
 #define MMN_MOM(F32X)                                                                  \
   if (bf && fresh) muon_momentum_kernel<true, true, F32X><<<grid, 256, 0, stream>>>(a);   \
