@@ -351,7 +351,7 @@ def run_ours(args, rank, world, local_rank):
 
     # TF32 roofline denominator, measured before the warm-up so that the timed
     # region is untouched
-    tf32_peak = measure_tf32_peak(dev) if args.ns_mode == "tf32" else None
+    tf32_peak = measure_tf32_peak(dev) if args.ns_mode in ("tf32", "fp32") else None
     inj = []
     for i in range(args.warmup):
         one_step()
@@ -478,12 +478,15 @@ def run_ours(args, rank, world, local_rank):
     if n_muon and med["newton_schulz"] > 0:
         ach = ns_flops / (med["newton_schulz"] / 1e3) / 1e12
         sustained = args.workload.startswith("hybrid")
-        if args.ns_mode == "tf32":
+        if args.ns_mode in ("tf32", "fp32"):
             # the dense TF32 rate is half the bf16 one and not in the peaks file:
-            # measured in this run, before the timed region
-            peak = tf32_peak[1] if sustained else tf32_peak[0]
+            # measured in this run, before the timed region. The fp32 mode forms
+            # every product from three tf32 MMAs, so its ceiling is a third.
+            split = 3.0 if args.ns_mode == "fp32" else 1.0
+            peak = (tf32_peak[1] if sustained else tf32_peak[0]) / split
             peak_src = ("measured in this run: cuBLAS tf32 8192^3, "
-                        + ("sustained" if sustained else "best of 10"))
+                        + ("sustained" if sustained else "best of 10")
+                        + (", / 3 (three tf32 MMAs per fp32 product)" if split > 1 else ""))
         else:
             peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
             peak_src = pk_kind
@@ -507,8 +510,9 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": (f"f32 (NS GEMMs {'tf32 x tf32' if args.ns_mode == 'tf32' else 'bf16 x bf16'}"
-                  " -> f32)") if not is_8b else "bf16 grads/params, f32 master",
+        "dtype": ("f32 (NS GEMMs " + {"tf32": "tf32 x tf32", "fp32": "3 x tf32 split fp32"}.get(
+                      args.ns_mode, "bf16 x bf16") + " -> f32)")
+                 if not is_8b else "bf16 grads/params, f32 master",
         "data": "synthetic (seeded normal params/grads)",
         "config": {"workload": args.workload, "desc": spec["desc"], "params": n_total,
                    "adamw_params": n_adamw, "muon_params": n_muon, "ns_mode": args.ns_mode,
@@ -566,7 +570,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="hybrid_1b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16", "tf32"])
+    ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16", "tf32", "fp32"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],

@@ -64,6 +64,11 @@ extern "C" {
                               tensor-core products, fp32 accumulate): about 8x closer to
                               exact Newton-Schulz, half the bf16 tensor rate. No
                               counterpart in the reference. */
+#define MMN_NS_FP32 3      /* no rounding points: X, A, A2 kept as fp32 values (each as
+                              hi + lo tf32 planes) and every product formed from three
+                              tf32 MMAs (hi*hi + hi*lo + lo*hi), fp32 accumulate: fp32-
+                              accurate Newton-Schulz at about a sixth of the bf16 rate.
+                              No counterpart in the reference. */
 
 /* AdamWConfig, lib.rs:6-11 (defaults lib.rs:13-21: 3e-4, (0.9, 0.95), 1e-8, 0.01) */
 typedef struct {
@@ -175,20 +180,21 @@ int mmn_newton_schulz5(const float *g, const int64_t *shape, int ndim, int steps
  * (rows*cols floats) on `device`. Its scratch is one fixed 8.25 MiB array in
  * the library, held by every GPU that loads the library until exit, so the
  * size is limited to min(rows, cols) <= 1024 and rows*cols <= 1048576; larger
- * inputs, and MMN_NS_TF32, return MMN_E_UNSUPPORTED. The first call on a device resolves that
- * array's device address and should come before any stream capture. All calls
- * on a device share the array, so calls that overlap on the GPU race. Work is
- * enqueued on `stream` (NULL = legacy default stream) and the call returns
- * after it has finished. */
+ * inputs, and MMN_NS_TF32 / MMN_NS_FP32, return MMN_E_UNSUPPORTED. The first
+ * call on a device resolves that array's device address and should come
+ * before any stream capture. All calls on a device share the array, so calls
+ * that overlap on the GPU race. Work is enqueued on `stream` (NULL = legacy
+ * default stream) and the call returns after it has finished. */
 int mmn_newton_schulz5_noalloc(const float *g, int64_t rows, int64_t cols, int steps,
                                int ns_mode, float *out, int device, void *stream);
 
 /* One loop body of newton_schulz5 (lib.rs:113-119) on an n x m (n <= m)
  * matrix x whose values are bf16-representable (tf32-representable for
- * MMN_NS_TF32), divided by x_norm first (x_norm = the Frobenius norm for the
- * first iteration, 1 afterwards). Writes A = bf16(x x^T), A2 = bf16(A A) (or,
- * for MMN_NS_BF16, bf16(b*A + c*A2); tf32 in place of bf16 for MMN_NS_TF32),
- * and the next x; any output pointer may be NULL. Host memory, synchronous.
+ * MMN_NS_TF32, any fp32 value for MMN_NS_FP32), divided by x_norm first
+ * (x_norm = the Frobenius norm for the first iteration, 1 afterwards). Writes
+ * A = bf16(x x^T), A2 = bf16(A A) (or, for MMN_NS_BF16, bf16(b*A + c*A2); tf32
+ * in place of bf16 for MMN_NS_TF32, no rounding for MMN_NS_FP32), and the next
+ * x; any output pointer may be NULL. Host memory, synchronous.
  * Exposes the three tensor-core products for per-iteration parity checks. */
 int mmn_newton_schulz_iteration(const float *x, int64_t n, int64_t m, float x_norm, int ns_mode,
                                 float *a_out, float *a2_out, float *x_next, int device);

@@ -17,7 +17,7 @@ MMN_E_STATE, MMN_E_OOM, MMN_E_TIMEOUT, MMN_E_UNSUPPORTED = -5, -6, -7, -8
 MEM_HOST, MEM_DEVICE = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTE_AUTO, ROUTE_MUON, ROUTE_ADAMW = 0, 1, 2
-NS_REFERENCE, NS_BF16, NS_TF32 = 0, 1, 2
+NS_REFERENCE, NS_BF16, NS_TF32, NS_FP32 = 0, 1, 2, 3
 
 
 class MmnError(RuntimeError):

@@ -299,7 +299,7 @@ extern "C" int mmn_optim_create(const mmn_optim_config* cfg, int device, void* s
   mmn_optim_config c = cfg ? *cfg : mmn_optim_config_default();
   if (c.world_size < 1 || c.rank < 0 || c.rank >= c.world_size)
     return fail(MMN_E_INVALID, "rank / world_size out of range");
-  if (c.ns_mode != MMN_NS_REFERENCE && c.ns_mode != MMN_NS_BF16 && c.ns_mode != MMN_NS_TF32)
+  if (c.ns_mode < MMN_NS_REFERENCE || c.ns_mode > MMN_NS_FP32)
     return fail(MMN_E_INVALID, "unknown ns_mode");
   if (c.grad_dtype != MMN_DTYPE_F32 && c.grad_dtype != MMN_DTYPE_BF16)
     return fail(MMN_E_INVALID, "grad_dtype must be f32 or bf16");
@@ -566,7 +566,8 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   std::vector<int> cls_norm0(cls_shapes.size());
   for (size_t k = 0; k < cls_shapes.size(); ++k) {
     std::string e = ns_class_init(h->classes[k], cls_shapes[k].first, cls_shapes[k].second,
-                                  cls_count[k], nullptr, ns_elem_bytes(h->cfg.ns_mode));
+                                  cls_count[k], nullptr, ns_elem_bytes(h->cfg.ns_mode),
+                                  ns_planes(h->cfg.ns_mode));
     if (!e.empty()) return fail(MMN_E_OOM, e);
     cls_norm0[k] = norm_base;
     norm_base += cls_count[k];
@@ -1015,7 +1016,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     m.fresh_state = h->cfg.fresh_state;
     m.apply_divides_norm = h->cfg.muon.ns_steps == 0;
     m.vec_ok = 1;  // arena bases come from cudaMalloc; offsets are 64-element aligned
-    m.x_f32 = h->cfg.ns_mode == MMN_NS_TF32;
+    m.x_mode = h->cfg.ns_mode == MMN_NS_FP32 ? 2 : (h->cfg.ns_mode == MMN_NS_TF32 ? 1 : 0);
     auto select = [&](size_t k) {
       m.mats = h->d_mats + h->chunk_mat0[k];
       m.nmat = h->chunk_mat0[k + 1] - h->chunk_mat0[k];

@@ -245,7 +245,8 @@ static int muon_class(mmn_muon* h, int n, int m, NsClass** out) {
   auto it = h->classes.find(key);
   if (it == h->classes.end()) {
     NsClass c;
-    std::string e = ns_class_init(c, n, m, 1, nullptr, ns_elem_bytes(h->ns_mode));
+    std::string e =
+        ns_class_init(c, n, m, 1, nullptr, ns_elem_bytes(h->ns_mode), ns_planes(h->ns_mode));
     if (!e.empty()) return fail(MMN_E_CUDA, e);
     it = h->classes.emplace(key, c).first;
   }
@@ -301,7 +302,7 @@ static int muon_run(mmn_muon* h, float* p, const float* g, float* vel, int rows,
   a.grad_divisor = grad_divisor;
   a.fresh_state = fresh;
   a.apply_divides_norm = steps == 0;
-  a.x_f32 = h->ns_mode == kNsTf32;
+  a.x_mode = h->ns_mode == kNsFp32 ? 2 : (h->ns_mode == kNsTf32 ? 1 : 0);
   launch_muon_momentum(a, h->ctx.num_sms, s);
   launch_muon_norms(a, s);
   MMN_CUDA_TRY(cudaGetLastError());
@@ -318,7 +319,7 @@ extern "C" int mmn_muon_create(const mmn_muon_config* cfg, int ns_mode, int devi
                                mmn_muon_t** out) {
   if (!out) return fail(MMN_E_INVALID, "out is null");
   *out = nullptr;
-  if (ns_mode != MMN_NS_REFERENCE && ns_mode != MMN_NS_BF16 && ns_mode != MMN_NS_TF32)
+  if (ns_mode < MMN_NS_REFERENCE || ns_mode > MMN_NS_FP32)
     return fail(MMN_E_INVALID, "unknown ns_mode");
   mmn_muon_config c = cfg ? *cfg : mmn_muon_config_default();
   if (c.ns_steps < 0) return fail(MMN_E_INVALID, "ns_steps must be >= 0");
@@ -486,7 +487,7 @@ extern "C" int mmn_newton_schulz_iteration(const float* x, int64_t n, int64_t m,
                                            float* x_next, int device) {
   if (!x) return fail(MMN_E_INVALID, "null input");
   if (n < 1 || m < n || m > (1 << 30)) return fail(MMN_E_SHAPE, "need 1 <= n <= m");
-  if (ns_mode != MMN_NS_REFERENCE && ns_mode != MMN_NS_BF16 && ns_mode != MMN_NS_TF32)
+  if (ns_mode < MMN_NS_REFERENCE || ns_mode > MMN_NS_FP32)
     return fail(MMN_E_INVALID, "unknown ns_mode");
   Ctx ctx;
   int rc = ctx.init(device, nullptr);
@@ -498,14 +499,26 @@ extern "C" int mmn_newton_schulz_iteration(const float* x, int64_t n, int64_t m,
     return fail(MMN_E_CUDA, e);
   }
   NsClass c;
-  const bool f32 = ns_mode == MMN_NS_TF32;
-  e = ns_class_init(c, (int)n, (int)m, 1, nullptr, ns_elem_bytes(ns_mode));
+  const bool f32 = ns_mode == MMN_NS_TF32 || ns_mode == MMN_NS_FP32;
+  const bool split = ns_mode == MMN_NS_FP32;
+  e = ns_class_init(c, (int)n, (int)m, 1, nullptr, ns_elem_bytes(ns_mode), ns_planes(ns_mode));
   if (!e.empty()) {
     ctx.release();
     return fail(MMN_E_OOM, e);
   }
   auto run = [&]() -> int {
-    if (f32) {
+    if (split) {
+      // fp32 mode: the hi and lo tf32 planes of x, one matrix item each
+      const size_t plane = (size_t)n * c.ld_x;
+      std::vector<float> hx(2 * plane, 0.0f);
+      for (int64_t i = 0; i < n; ++i)
+        for (int64_t j = 0; j < m; ++j) {
+          const float v = x[i * m + j], hi = host_tf32_round(v);
+          hx[(size_t)i * c.ld_x + j] = hi;
+          hx[plane + (size_t)i * c.ld_x + j] = host_tf32_round(v - hi);
+        }
+      MMN_CUDA_TRY(cudaMemcpy(c.x[0], hx.data(), hx.size() * 4, cudaMemcpyHostToDevice));
+    } else if (f32) {
       std::vector<float> hx((size_t)n * c.ld_x, 0.0f);
       for (int64_t i = 0; i < n; ++i)
         for (int64_t j = 0; j < m; ++j) hx[(size_t)i * c.ld_x + j] = host_tf32_round(x[i * m + j]);
@@ -526,10 +539,15 @@ extern "C" int mmn_newton_schulz_iteration(const float* x, int64_t n, int64_t m,
     auto fetch = [&](const void* src, int64_t rows, int64_t cols, int ld, float* dst) -> int {
       if (!dst) return MMN_OK;
       if (f32) {
-        std::vector<float> h((size_t)rows * ld);
+        // (fp32 mode: hi plane then lo plane; the value is their sum)
+        const size_t plane = (size_t)rows * ld;
+        std::vector<float> h(plane * (split ? 2 : 1));
         MMN_CUDA_TRY(cudaMemcpy(h.data(), src, h.size() * 4, cudaMemcpyDeviceToHost));
         for (int64_t i = 0; i < rows; ++i)
-          for (int64_t j = 0; j < cols; ++j) dst[i * cols + j] = h[(size_t)i * ld + j];
+          for (int64_t j = 0; j < cols; ++j) {
+            const size_t k = (size_t)i * ld + j;
+            dst[i * cols + j] = split ? h[k] + h[plane + k] : h[k];
+          }
         return MMN_OK;
       }
       std::vector<__nv_bfloat16> h((size_t)rows * ld);

@@ -201,25 +201,94 @@ __device__ __forceinline__ float tf32_round(float x) {
   return __uint_as_float(u);
 }
 
-// Momentum arithmetic of lib.rs:154-165 for one element; returns bf16(u), the
-// rounding of lib.rs:104, or tf32(u) in the TF32 mode.
-template <bool F32X>
+// How the Newton-Schulz input X is stored (MuonArgs::x_mode): 0 bf16(u), the
+// rounding of lib.rs:104; 1 tf32(u) in fp32 words (TF32 mode); 2 u itself as
+// two tf32 planes, hi = tf32(u) at item 2b and lo = tf32(u - hi) at item
+// 2b + 1 (fp32 mode). x_value() is the value the norm and the iteration see.
+template <int XM>
+__device__ __forceinline__ float x_value(float u) {
+  if constexpr (XM == 0)
+    return __bfloat162float(__float2bfloat16_rn(u));
+  else if constexpr (XM == 1)
+    return tf32_round(u);
+  else
+    return u;
+}
+
+// Stores 4 consecutive X values y (already x_value) at element i of the
+// matrix item(s) starting at X; plane_stride separates the split planes.
+template <int XM>
+__device__ __forceinline__ void x_store4(void* X, long long i, long long plane_stride,
+                                         const float (&y)[4]) {
+  if constexpr (XM == 0) {
+    uint2 o;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]);
+    __nv_bfloat162 h1 = __floats2bfloat162_rn(y[2], y[3]);
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(X) + i) = o;
+  } else if constexpr (XM == 1) {
+    *reinterpret_cast<float4*>(static_cast<float*>(X) + i) = make_float4(y[0], y[1], y[2], y[3]);
+  } else {
+    float hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      hi[e] = tf32_round(y[e]);
+      lo[e] = tf32_round(__fsub_rn(y[e], hi[e]));
+    }
+    float* xf = static_cast<float*>(X) + i;
+    *reinterpret_cast<float4*>(xf) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<float4*>(xf + plane_stride) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+template <int XM>
+__device__ __forceinline__ void x_store1(void* X, long long i, long long plane_stride, float y) {
+  if constexpr (XM == 0) {
+    static_cast<__nv_bfloat16*>(X)[i] = __float2bfloat16_rn(y);
+  } else if constexpr (XM == 1) {
+    static_cast<float*>(X)[i] = y;
+  } else {
+    const float hi = tf32_round(y);
+    static_cast<float*>(X)[i] = hi;
+    static_cast<float*>(X)[i + plane_stride] = tf32_round(__fsub_rn(y, hi));
+  }
+}
+
+template <int XM>
+__device__ __forceinline__ float x_load1(const void* X, long long i, long long plane_stride) {
+  if constexpr (XM == 0)
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(X)[i]);
+  else if constexpr (XM == 1)
+    return static_cast<const float*>(X)[i];
+  else
+    return __fadd_rn(static_cast<const float*>(X)[i], static_cast<const float*>(X)[i + plane_stride]);
+}
+
+// The first X element of a matrix: item xbatch (2 * xbatch with split planes).
+template <int XM>
+__device__ __forceinline__ void* x_matrix(const MuonClassPtr& cp, int xbatch) {
+  if constexpr (XM == 0)
+    return static_cast<__nv_bfloat16*>(cp.x) + (long long)xbatch * cp.bstride;
+  else
+    return static_cast<float*>(cp.x) + (long long)xbatch * (XM == 2 ? 2 : 1) * cp.bstride;
+}
+
+// Momentum arithmetic of lib.rs:154-165 for one element; returns x_value(u).
+template <int XM>
 __device__ __forceinline__ float momentum_elem(float g, float& vel, float mu, float one_m,
                                                int nesterov) {
   const float v1 = __fadd_rn(__fmul_rn(mu, vel), __fmul_rn(one_m, g));
   vel = v1;
   const float u = nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
-  if constexpr (F32X)
-    return tf32_round(u);
-  else
-    return __bfloat162float(__float2bfloat16_rn(u));
+  return x_value<XM>(u);
 }
 
 // 128-bit variant of one 64 x 64 momentum tile: thread t covers 4 consecutive
 // columns; a transposed X is written through `tile` in groups of 4 rows.
-template <bool BF16G, bool FRESH, bool F32X>
+template <bool BF16G, bool FRESH, int XM>
 __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const MuonMat& mm, int r0,
-                                                   int c0, void* Xv, int ld,
+                                                   int c0, void* Xv, int ld, long long pstride,
                                                    float (*tile)[kTile + 1], float scale,
                                                    float mu, float one_m) {
   const int cq = (threadIdx.x & 15) * 4;
@@ -272,22 +341,11 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
         float ge = g[q][e];
         if (scale != 1.0f) ge = __fdiv_rn(ge, scale);
         if (a.grad_divisor != 1.0f) ge = __fdiv_rn(ge, a.grad_divisor);
-        y[e] = momentum_elem<F32X>(ge, vv[q][e], mu, one_m, a.nesterov);
+        y[e] = momentum_elem<XM>(ge, vv[q][e], mu, one_m, a.nesterov);
       }
       __stcs(reinterpret_cast<float4*>(a.vel + idx),
              make_float4(vv[q][0], vv[q][1], vv[q][2], vv[q][3]));
-      if (!mm.transposed && F32X) {
-        *reinterpret_cast<float4*>(static_cast<float*>(Xv) + (long long)r * ld + c) =
-            make_float4(y[0], y[1], y[2], y[3]);
-      } else if (!mm.transposed) {
-        __nv_bfloat16* X = static_cast<__nv_bfloat16*>(Xv);
-        uint2 o;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]);
-        __nv_bfloat162 h1 = __floats2bfloat162_rn(y[2], y[3]);
-        o.x = *reinterpret_cast<uint32_t*>(&h0);
-        o.y = *reinterpret_cast<uint32_t*>(&h1);
-        *reinterpret_cast<uint2*>(X + (long long)r * ld + c) = o;
-      }
+      if (!mm.transposed) x_store4<XM>(Xv, (long long)r * ld + c, pstride, y);
     }
     if (mm.transposed) {
 #pragma unroll
@@ -302,25 +360,14 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
     const int rq = (threadIdx.x & 15) * 4;
     for (int cl = rs; cl < kTile; cl += 16) {
       const int c = c0 + cl, r = r0 + rq;
-      if (c < mm.cols && r < mm.rows && F32X) {
-        float* dst = static_cast<float*>(Xv) + (long long)c * ld + r;
+      if (c < mm.cols && r < mm.rows) {
+        const long long i = (long long)c * ld + r;
         if (r + 3 < mm.rows) {
-          *reinterpret_cast<float4*>(dst) =
-              make_float4(tile[rq][cl], tile[rq + 1][cl], tile[rq + 2][cl], tile[rq + 3][cl]);
+          const float y4[4] = {tile[rq][cl], tile[rq + 1][cl], tile[rq + 2][cl], tile[rq + 3][cl]};
+          x_store4<XM>(Xv, i, pstride, y4);
         } else {
-          for (int e = 0; e < 4 && r + e < mm.rows; ++e) dst[e] = tile[rq + e][cl];
-        }
-      } else if (c < mm.cols && r < mm.rows) {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(Xv) + (long long)c * ld + r;
-        if (r + 3 < mm.rows) {
-          uint2 o;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(tile[rq][cl], tile[rq + 1][cl]);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(tile[rq + 2][cl], tile[rq + 3][cl]);
-          o.x = *reinterpret_cast<uint32_t*>(&h0);
-          o.y = *reinterpret_cast<uint32_t*>(&h1);
-          *reinterpret_cast<uint2*>(dst) = o;
-        } else {
-          for (int e = 0; e < 4 && r + e < mm.rows; ++e) dst[e] = __float2bfloat16_rn(tile[rq + e][cl]);
+          for (int e = 0; e < 4 && r + e < mm.rows; ++e)
+            x_store1<XM>(Xv, i + e, pstride, tile[rq + e][cl]);
         }
       }
     }
@@ -330,12 +377,12 @@ __device__ __forceinline__ float momentum_tile_vec(const MuonArgs& a, const Muon
 
 // Muon momentum (lib.rs:154-165) + the bf16 cast and orientation of
 // newton_schulz5 (lib.rs:101-107) + per-tile sums of squares of the bf16
-// values (lib.rs:109), all in one pass over g and vel. F32X: the TF32 mode's
-// tf32 cast into an fp32 X.
+// values (lib.rs:109), all in one pass over g and vel. XM selects the X
+// storage of the TF32 and fp32 modes instead of bf16 (x_value).
 // Four 256-thread blocks per SM (at most 64 registers a thread, 16.6 KB of
 // shared memory a block), launched as one wave that strides over the tiles.
 constexpr int kMomentumBlocksPerSm = 4;
-template <bool BF16G, bool FRESH, bool F32X>
+template <bool BF16G, bool FRESH, int XM>
 __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   __shared__ float red[8];
@@ -351,11 +398,10 @@ __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kerne
     const int lt = t - mm.tile0;
     const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
     const MuonClassPtr cp = a.cls[mm.xcls];
-    void* Xv = F32X ? (void*)(static_cast<float*>(cp.x) + (long long)mm.xbatch * cp.bstride)
-                    : (void*)(static_cast<__nv_bfloat16*>(cp.x) + (long long)mm.xbatch * cp.bstride);
+    void* Xv = x_matrix<XM>(cp, mm.xbatch);
     if (a.vec_ok && (mm.cols & 3) == 0 && (mm.off & 3) == 0) {
-      const float ssv =
-          momentum_tile_vec<BF16G, FRESH, F32X>(a, mm, r0, c0, Xv, cp.ld, tile, scale, mu, one_m);
+      const float ssv = momentum_tile_vec<BF16G, FRESH, XM>(a, mm, r0, c0, Xv, cp.ld, cp.bstride,
+                                                            tile, scale, mu, one_m);
       const float totv = block_sum_256(ssv, red);
       if (threadIdx.x == 0) a.partials[t] = totv;
       continue;
@@ -373,13 +419,8 @@ __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kerne
         const float v1 = __fadd_rn(__fmul_rn(mu, v0), __fmul_rn(one_m, g));
         a.vel[idx] = v1;
         const float u = a.nesterov ? __fadd_rn(__fmul_rn(g, one_m), __fmul_rn(v1, mu)) : v1;
-        y = F32X ? tf32_round(u) : __bfloat162float(__float2bfloat16_rn(u));
-        if (!mm.transposed) {
-          if (F32X)
-            static_cast<float*>(Xv)[(long long)r * cp.ld + c] = y;
-          else
-            static_cast<__nv_bfloat16*>(Xv)[(long long)r * cp.ld + c] = __float2bfloat16_rn(y);
-        }
+        y = x_value<XM>(u);
+        if (!mm.transposed) x_store1<XM>(Xv, (long long)r * cp.ld + c, cp.bstride, y);
       }
       if (mm.transposed) tile[rr][tx] = y;
       ss = __fadd_rn(ss, __fmul_rn(y, y));
@@ -389,13 +430,8 @@ __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kerne
       // X[c][r] = tile[r - r0][c - c0]; consecutive threads write consecutive r.
       for (int cc = ty; cc < kTile; cc += 4) {
         const int c = c0 + cc, r = r0 + tx;
-        if (c < mm.cols && r < mm.rows) {
-          if (F32X)
-            static_cast<float*>(Xv)[(long long)c * cp.ld + r] = tile[tx][cc];
-          else
-            static_cast<__nv_bfloat16*>(Xv)[(long long)c * cp.ld + r] =
-                __float2bfloat16_rn(tile[tx][cc]);
-        }
+        if (c < mm.cols && r < mm.rows)
+          x_store1<XM>(Xv, (long long)c * cp.ld + r, cp.bstride, tile[tx][cc]);
       }
     }
     const float tot = block_sum_256(ss, red);
@@ -419,7 +455,7 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(const MuonArgs a) {
 
 // Muon::step_matrix tail (lib.rs:169-174): p -= (lr*scale) * O, O read back in
 // the parameter's orientation from the final Newton-Schulz X.
-template <bool SHADOW, bool F32X>
+template <bool SHADOW, int XM>
 __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
   __shared__ float tile[kTile][kTile + 1];
   if (a.skip && *a.skip) return;
@@ -431,16 +467,14 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
     const int lt = t - mm.tile0;
     const int r0 = (lt / tiles_c) * kTile, c0 = (lt % tiles_c) * kTile;
     const MuonClassPtr cp = a.cls[mm.xcls];
-    const long long xb = (long long)mm.xbatch * cp.bstride;
-    auto xat = [&](long long i) -> float {
-      if (F32X) return static_cast<const float*>(cp.x)[xb + i];
-      return __bfloat162float(static_cast<const __nv_bfloat16*>(cp.x)[xb + i]);
-    };
+    const void* X = x_matrix<XM>(cp, mm.xbatch);
     if (mm.transposed) {
       __syncthreads();
       for (int cc = ty; cc < kTile; cc += 4) {
         const int c = c0 + cc, r = r0 + tx;
-        tile[cc][tx] = (c < mm.cols && r < mm.rows) ? xat((long long)c * cp.ld + r) : 0.0f;
+        tile[cc][tx] = (c < mm.cols && r < mm.rows)
+                           ? x_load1<XM>(X, (long long)c * cp.ld + r, cp.bstride)
+                           : 0.0f;
       }
       __syncthreads();
     }
@@ -448,7 +482,7 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const MuonArgs a) {
       const int r = r0 + rr, c = c0 + tx;
       if (r < mm.rows && c < mm.cols) {
         const long long idx = mm.off + (long long)r * mm.cols + c;
-        float o = mm.transposed ? tile[tx][rr] : xat((long long)r * cp.ld + c);
+        float o = mm.transposed ? tile[tx][rr] : x_load1<XM>(X, (long long)r * cp.ld + c, cp.bstride);
         if (a.apply_divides_norm) o = __fdiv_rn(o, a.norms[mm.norm_idx]);
         const float pn = __fsub_rn(a.p[idx], __fmul_rn(mm.lr_scale, o));
         a.p[idx] = pn;
@@ -632,15 +666,17 @@ void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
   if (a.total_tiles <= 0) return;
   const int grid = grid_for(a.total_tiles, 1, num_sms, kMomentumBlocksPerSm);
   const bool bf = a.g_bf16 != nullptr, fresh = a.fresh_state != 0;
-#define MMN_MOM(F32X)                                                                  \
-  if (bf && fresh) muon_momentum_kernel<true, true, F32X><<<grid, 256, 0, stream>>>(a);   \
-  if (bf && !fresh) muon_momentum_kernel<true, false, F32X><<<grid, 256, 0, stream>>>(a); \
-  if (!bf && fresh) muon_momentum_kernel<false, true, F32X><<<grid, 256, 0, stream>>>(a); \
-  if (!bf && !fresh) muon_momentum_kernel<false, false, F32X><<<grid, 256, 0, stream>>>(a);
-  if (a.x_f32) {
-    MMN_MOM(true)
+#define MMN_MOM(XM)                                                                  \
+  if (bf && fresh) muon_momentum_kernel<true, true, XM><<<grid, 256, 0, stream>>>(a);   \
+  if (bf && !fresh) muon_momentum_kernel<true, false, XM><<<grid, 256, 0, stream>>>(a); \
+  if (!bf && fresh) muon_momentum_kernel<false, true, XM><<<grid, 256, 0, stream>>>(a); \
+  if (!bf && !fresh) muon_momentum_kernel<false, false, XM><<<grid, 256, 0, stream>>>(a);
+  if (a.x_mode == 2) {
+    MMN_MOM(2)
+  } else if (a.x_mode == 1) {
+    MMN_MOM(1)
   } else {
-    MMN_MOM(false)
+    MMN_MOM(0)
   }
 #undef MMN_MOM
 }
@@ -653,14 +689,19 @@ void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
 void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream) {
   if (a.total_tiles <= 0) return;
   const int grid = grid_for(a.total_tiles, 1, num_sms, 8);
-  if (a.p_bf16 && a.x_f32)
-    muon_apply_kernel<true, true><<<grid, 256, 0, stream>>>(a);
-  else if (a.p_bf16)
-    muon_apply_kernel<true, false><<<grid, 256, 0, stream>>>(a);
-  else if (a.x_f32)
-    muon_apply_kernel<false, true><<<grid, 256, 0, stream>>>(a);
-  else
-    muon_apply_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+#define MMN_APPLY(XM)                                                   \
+  if (a.p_bf16)                                                         \
+    muon_apply_kernel<true, XM><<<grid, 256, 0, stream>>>(a);           \
+  else                                                                  \
+    muon_apply_kernel<false, XM><<<grid, 256, 0, stream>>>(a);
+  if (a.x_mode == 2) {
+    MMN_APPLY(2)
+  } else if (a.x_mode == 1) {
+    MMN_APPLY(1)
+  } else {
+    MMN_APPLY(0)
+  }
+#undef MMN_APPLY
 }
 
 void launch_grad_reduce(const GradReduceArgs& a, int num_sms, cudaStream_t stream) {

@@ -55,8 +55,8 @@ struct MuonMat {
 };
 
 struct MuonClassPtr {
-  void* x;            // class X buffer (batch x n x ld): bf16, or fp32 when x_f32
-  long long bstride;  // elements between batch items
+  void* x;            // class X buffer (items x n x ld): bf16, or fp32 when x_mode > 0
+  long long bstride;  // elements between items (x_mode 2: two items, hi and lo, per matrix)
   int ld;
   int pad;
 };
@@ -83,7 +83,8 @@ struct MuonArgs {
   int apply_divides_norm;  // zero Newton-Schulz steps: O = bf16(u) / norm (lib.rs:110)
   int vec_ok;              // p / g / vel bases are 16-byte aligned: matrices with
                            // cols % 4 == 0 and off % 4 == 0 take the 128-bit path
-  int x_f32;               // TF32 mode: X is fp32 holding tf32(u) instead of bf16(u)
+  int x_mode;              // X storage: 0 bf16(u); 1 tf32(u) in fp32 words (TF32
+                           // mode); 2 u as hi + lo tf32 planes (fp32 mode)
 };
 
 void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream);

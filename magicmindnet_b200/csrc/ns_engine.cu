@@ -83,11 +83,12 @@ size_t sym_tiles_total(int n) {
 
 // Lays out the buffers of a class over `p` and encodes its tensor maps.
 std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
-                   std::vector<int2>* tiles, int esize) {
+                   std::vector<int2>* tiles, int esize, int planes) {
   c.n = n;
   c.m = m;
   c.batch = batch;
   c.esize = esize;
+  c.planes = planes;
   c.ld_x = round_up(m, 8);
   c.ld_a = round_up(n, 8);
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
@@ -114,34 +115,35 @@ std::string layout(NsClass& c, int n, int m, int batch, uint8_t* p,
   // 32 tf32 rows); K-major boxes: one stage of K columns by the operand's rows.
   const int kb = 128 / esize;
   const int e = esize;
+  const int nb = batch * planes;  // the maps index planes as batch items
   for (int i = 0; i < 2; ++i) {
-    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, batch, c.ld_x, kBM, e)).empty()) return err;
-    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, batch, c.ld_x, 256, e)).empty()) return err;
-    // (in the TF32 mode X is read MN-major only through this map)
-    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, batch, c.ld_x, kb, e, e == 4)).empty())
+    if (!(err = encode_3d(&c.tm_x_a[i], c.x[i], m, n, nb, c.ld_x, kBM, e)).empty()) return err;
+    if (!(err = encode_3d(&c.tm_x_b[i], c.x[i], m, n, nb, c.ld_x, 256, e)).empty()) return err;
+    // (in the TF32 and fp32 modes X is read MN-major only through this map)
+    if (!(err = encode_3d(&c.tm_x_mn[i], c.x[i], m, n, nb, c.ld_x, kb, e, e == 4)).empty())
       return err;
   }
-  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, batch, c.ld_a, kBM, e)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, batch, c.ld_a, 256, e)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, batch, c.ld_a, kBM, e)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, batch, c.ld_a, 64, e)).empty()) return err;
-  if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, batch, c.ld_a, 64, e)).empty()) return err;
-  if (!(err = encode_3d_store(&c.tm_a_out, c.a, n, n, batch, c.ld_a, e)).empty()) return err;
-  if (!(err = encode_3d_store(&c.tm_a2_out, c.a2, n, n, batch, c.ld_a, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_a, c.a, n, n, nb, c.ld_a, kBM, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_b, c.a, n, n, nb, c.ld_a, 256, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_a, c.a2, n, n, nb, c.ld_a, kBM, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a_n, c.a, n, n, nb, c.ld_a, 64, e)).empty()) return err;
+  if (!(err = encode_3d(&c.tm_a2_n, c.a2, n, n, nb, c.ld_a, 64, e)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a_out, c.a, n, n, nb, c.ld_a, e)).empty()) return err;
+  if (!(err = encode_3d_store(&c.tm_a2_out, c.a2, n, n, nb, c.ld_a, e)).empty()) return err;
   return "";
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false, bool SPLIT = false>
 cudaError_t set_smem() {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
-  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>,
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32, SPLIT>;
+  return cudaFuncSetAttribute(ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32, SPLIT>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false, bool SPLIT = false>
 cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b,
                    const NsGemmArgs& args, int num_sms, cudaStream_t stream) {
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32, SPLIT>;
   if (args.num_tiles <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -165,7 +167,7 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
       cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
       int n = 0;
       cudaError_t e = cudaOccupancyMaxActiveClusters(
-          &n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>, &cfg);
+          &n, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32, SPLIT>, &cfg);
       if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
       max_pairs = n < num_sms / 2 ? n : num_sms / 2;
     }
@@ -178,8 +180,8 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32>, a1, a2, b,
-                            args);
+  return cudaLaunchKernelEx(&cfg, ns_gemm_kernel<BN, DUAL, B_MN, EPI, PAIR, F32, SPLIT>, a1, a2,
+                            b, args);
 }
 
 // CTA pairs pay off once a matrix fills 256-row tiles.
@@ -206,23 +208,33 @@ std::string ns_gemm_setup() {
   if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare, true, true>();
   if (e == cudaSuccess) e = set_smem<128, true, true, kEpiPolyDual, false, true>();
   if (e == cudaSuccess) e = set_smem<128, true, false, kEpiPolyDualT, true, true>();
+  // fp32 mode (split tf32 planes)
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiGram, false, true, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiGram, true, true, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare, false, true, true>();
+  if (e == cudaSuccess) e = set_smem<256, false, false, kEpiSquare, true, true, true>();
+  if (e == cudaSuccess) e = set_smem<128, true, true, kEpiPolyDual, false, true, true>();
+  if (e == cudaSuccess) e = set_smem<128, true, false, kEpiPolyDualT, true, true, true>();
   if (e != cudaSuccess) return std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
   return get_encode();
 }
 
-size_t ns_class_bytes(int n, int m, int batch, int esize) {
+size_t ns_class_bytes(int n, int m, int batch, int esize, int planes) {
   const size_t ld_x = (size_t)round_up(m, 8), ld_a = (size_t)round_up(n, 8);
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-  return 2 * al((size_t)batch * n * ld_x * esize) + 2 * al((size_t)batch * n * ld_a * esize) +
+  const size_t items = (size_t)batch * planes;
+  return 2 * al(items * n * ld_x * esize) + 2 * al(items * n * ld_a * esize) +
          al((size_t)batch * 4) + al(sym_tiles_total(n) * sizeof(int2));
 }
 
-std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base, int esize) {
+std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base, int esize,
+                          int planes) {
   if (n <= 0 || m <= 0 || n > m || batch <= 0) return "invalid Newton-Schulz class shape";
-  if (esize != 2 && esize != 4) return "invalid Newton-Schulz element size";
+  if ((esize != 2 && esize != 4) || (planes != 1 && planes != 2) || (planes == 2 && esize != 4))
+    return "invalid Newton-Schulz element size";
   std::string err = get_encode();
   if (!err.empty()) return err;
-  const size_t bytes = ns_class_bytes(n, m, batch, esize);
+  const size_t bytes = ns_class_bytes(n, m, batch, esize, planes);
   uint8_t* p = static_cast<uint8_t*>(base);
   bool own = false;
   if (!p) {
@@ -230,7 +242,7 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base, int e
     own = true;
   }
   std::vector<int2> tiles;
-  err = layout(c, n, m, batch, p, &tiles, esize);
+  err = layout(c, n, m, batch, p, &tiles, esize, planes);
   c.owns_memory = own;
   if (!err.empty()) return err;
   // Padding columns of X and A are never read (the tensor maps stop at n / m);
@@ -243,14 +255,14 @@ std::string ns_class_init(NsClass& c, int n, int m, int batch, void* base, int e
 }
 
 std::string ns_class_bind(NsClass& c, int n, int m, int batch, void* base,
-                          std::vector<int2>* tiles_out, int esize) {
+                          std::vector<int2>* tiles_out, int esize, int planes) {
   if (n <= 0 || m <= 0 || n > m || batch <= 0 || !base || !tiles_out ||
-      (esize != 2 && esize != 4))
+      (esize != 2 && esize != 4) || (planes != 1 && planes != 2) || (planes == 2 && esize != 4))
     return "invalid Newton-Schulz class shape or base";
   std::string err = get_encode();
   if (!err.empty()) return err;
   c = NsClass();
-  return layout(c, n, m, batch, static_cast<uint8_t*>(base), tiles_out, esize);
+  return layout(c, n, m, batch, static_cast<uint8_t*>(base), tiles_out, esize, planes);
 }
 
 void ns_class_free(NsClass& c) {
@@ -263,14 +275,15 @@ static constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;
 
 namespace {
 
-template <bool PAIR, bool F32>
+template <bool PAIR, bool F32, bool SPLIT>
 cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int mode,
                           const NsGemmArgs& base, const NsFused* fused, int num_sms,
                           cudaStream_t stream) {
   const int tile_m = PAIR ? 2 * kBM : kBM;
   NsGemmArgs g = base;
 
-  // A = round((X X^T) / s / s), round = bf16, or tf32 in the TF32 mode
+  // A = round((X X^T) / s / s), round = bf16, tf32 in the TF32 mode, none
+  // (hi + lo planes) in the fp32 mode
   g.out = c.a;
   g.out_bstride = (long long)c.n * c.ld_a;
   g.out_ld = c.ld_a;
@@ -285,7 +298,7 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
   g.num_tiles = g.tiles_per_matrix * c.batch;
   // B is the same X rows: 128 rows per CTA of a pair, 256 for a single CTA.
   const CUtensorMap& xb = PAIR ? c.tm_x_a[cur] : c.tm_x_b[cur];
-  cudaError_t e = launch<256, false, false, kEpiGram, PAIR, F32>(c.tm_x_a[cur], c.tm_a_out, xb, g,
+  cudaError_t e = launch<256, false, false, kEpiGram, PAIR, F32, SPLIT>(c.tm_x_a[cur], c.tm_a_out, xb, g,
                                                                  num_sms, stream);
   if (e != cudaSuccess) return e;
 
@@ -306,8 +319,8 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
                                                       stream);
     }
   } else {
-    e = launch<256, false, false, kEpiSquare, PAIR, true>(c.tm_a_a, c.tm_a2_out, ab, g, num_sms,
-                                                          stream);
+    e = launch<256, false, false, kEpiSquare, PAIR, true, SPLIT>(c.tm_a_a, c.tm_a2_out, ab, g,
+                                                                 num_sms, stream);
   }
   if (e != cudaSuccess) return e;
 
@@ -345,14 +358,14 @@ cudaError_t run_iteration(NsClass& c, int cur, int nxt, const float* norms, int 
     g.tiles_n = (c.n + 127) / 128;
     g.tiles_per_matrix = ((c.m + 255) / 256) * g.tiles_n;
     g.num_tiles = g.tiles_per_matrix * c.batch;
-    return launch<128, true, false, kEpiPolyDualT, true, F32>(c.tm_x_mn[cur], c.tm_a2_n, c.tm_a_n,
-                                                              g, num_sms, stream);
+    return launch<128, true, false, kEpiPolyDualT, true, F32, SPLIT>(
+        c.tm_x_mn[cur], c.tm_a2_n, c.tm_a_n, g, num_sms, stream);
   }
   g.tiles_n = (c.m + 127) / 128;
   g.tiles_per_matrix = ((c.n + tile_m - 1) / tile_m) * g.tiles_n;
   g.num_tiles = g.tiles_per_matrix * c.batch;
-  return launch<128, true, true, kEpiPolyDual, PAIR, F32>(c.tm_a_a, c.tm_a2_a, c.tm_x_mn[cur], g,
-                                                          num_sms, stream);
+  return launch<128, true, true, kEpiPolyDual, PAIR, F32, SPLIT>(c.tm_a_a, c.tm_a2_a,
+                                                                 c.tm_x_mn[cur], g, num_sms, stream);
 }
 
 }  // namespace
@@ -367,8 +380,8 @@ int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
   base.coef_b = kNsB;
   base.coef_c = kNsC;
   const bool pair = use_pairs(c);
-  const bool f32 = mode == kNsTf32;
-  if (c.esize != ns_elem_bytes(mode)) {
+  const bool f32 = mode == kNsTf32 || mode == kNsFp32, split = mode == kNsFp32;
+  if (c.esize != ns_elem_bytes(mode) || c.planes != ns_planes(mode)) {
     if (err) *err = "Newton-Schulz class buffers do not match the arithmetic mode";
     return -1;
   }
@@ -377,12 +390,20 @@ int ns_class_run(NsClass& c, int steps, int mode, int* status, int num_sms,
     const float* norms = it == 0 ? c.norms : nullptr;
     const NsFused* f = (fused && it == steps - 1) ? fused : nullptr;
     cudaError_t e;
-    if (f32)
-      e = pair ? run_iteration<true, true>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
-               : run_iteration<false, true>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
+    if (split)
+      e = pair ? run_iteration<true, true, true>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
+               : run_iteration<false, true, true>(c, cur, nxt, norms, mode, base, f, num_sms,
+                                                  stream);
+    else if (f32)
+      e = pair ? run_iteration<true, true, false>(c, cur, nxt, norms, mode, base, f, num_sms,
+                                                  stream)
+               : run_iteration<false, true, false>(c, cur, nxt, norms, mode, base, f, num_sms,
+                                                   stream);
     else
-      e = pair ? run_iteration<true, false>(c, cur, nxt, norms, mode, base, f, num_sms, stream)
-               : run_iteration<false, false>(c, cur, nxt, norms, mode, base, f, num_sms, stream);
+      e = pair ? run_iteration<true, false, false>(c, cur, nxt, norms, mode, base, f, num_sms,
+                                                   stream)
+               : run_iteration<false, false, false>(c, cur, nxt, norms, mode, base, f, num_sms,
+                                                    stream);
     if (e != cudaSuccess) {
       if (err) *err = std::string("Newton-Schulz GEMM launch: ") + cudaGetErrorString(e);
       return -1;

@@ -29,6 +29,13 @@
 // and the MMAs issued as kind::tf32. A 128-byte swizzle row then holds 32
 // elements, so a stage covers K = 32 and one MMA K = 8; stage byte sizes and
 // the TMEM layout are the same as in bf16.
+//
+// SPLIT = true (with F32) instantiates the fp32 mode: no rounding points at
+// all. Every stored matrix is kept as two tf32 planes, hi = tf32(v) and
+// lo = tf32(v - hi) (batch items 2b and 2b + 1 of the same buffer), and every
+// product is the three-pass hi*hi + hi*lo + lo*hi into one fp32 accumulator,
+// which carries about 21 mantissa bits instead of tf32's 11. Stages hold both
+// planes of each operand; the symmetric outputs are stored from registers.
 // In the last iteration the Poly epilogue can apply the Muon update
 // p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
@@ -85,8 +92,10 @@ struct NsGemmArgs {
   const int* skip;           // device non-finite flag: when set the launch does nothing
 };
 
-template <int BN, bool DUAL, bool B_MN, bool PAIR, int EPI, bool F32 = false>
+template <int BN, bool DUAL, bool B_MN, bool PAIR, int EPI, bool F32 = false,
+          bool SPLIT = false>
 struct NsGemmShape {
+  static constexpr int kPlanes = SPLIT ? 2 : 1;  // hi and lo tf32 planes per operand
   static constexpr int kEsz = F32 ? 4 : 2;  // bytes per stored operand element
   static constexpr int kBKe = 128 / kEsz;   // K per stage: one 128-byte swizzle row
   static constexpr int kKi = 32 / kEsz;     // K per MMA instruction (32 bytes)
@@ -101,18 +110,27 @@ struct NsGemmShape {
   static constexpr int kABytes = kBM * 128;         // 16 KB per A operand
   static constexpr int kBBytes = kBNc * 128;
   static constexpr int kStageBytes =
-      SWAP ? kABytes + 2 * kBBytes : kABytes * (DUAL ? 2 : 1) + kBBytes;
+      kPlanes * (SWAP ? kABytes + 2 * kBBytes : kABytes * (DUAL ? 2 : 1) + kBBytes);
   // per epilogue warp: two 32 x 32 blocks of the symmetric output (direct and
   // mirrored, staged for TMA stores), or (SWAP) a 32 x 33 fp32 tile that turns
   // lane-per-column values into lane-per-row ones
-  static constexpr int kEpiWarpBytes = SWAP ? 32 * 33 * 4 : (SYM ? 2 * 32 * 32 * kEsz : 0);
+  // (SPLIT symmetric outputs are stored directly from registers: their MMA phase
+  // is three tf32 products per step, so the epilogue has time to spare)
+  static constexpr int kEpiWarpBytes =
+      SWAP ? 32 * 33 * 4 : ((SYM && !SPLIT) ? 2 * 32 * 32 * kEsz : 0);
   // bf16: at most 200 KB of stages; tf32: whatever the larger fp32 epilogue
   // stage leaves of the 227 KB
   static constexpr int kStageBudget =
       F32 ? 232448 - 2048 - 8 * kEpiWarpBytes : 204800;
   static constexpr int kStages =
       (kStageBudget / kStageBytes) < 8 ? (kStageBudget / kStageBytes) : 8;
-  static constexpr int kAccCols = BN * (DUAL ? 2 : 1);  // per accumulator buffer
+  // SPLIT: the hi*hi products and the small hi*lo + lo*hi corrections go to two
+  // accumulators (the corrections kSmallOff columns further), summed in the
+  // epilogue. The tensor cores round each accumulator update toward zero, so
+  // keeping the corrections apart leaves the main accumulator one update per K
+  // step, as in the TF32 mode, and makes the corrections' own bias 2^-11 smaller.
+  static constexpr int kSmallOff = SPLIT ? BN * (DUAL ? 2 : 1) : 0;
+  static constexpr int kAccCols = BN * (DUAL ? 2 : 1) * (SPLIT ? 2 : 1);  // per buffer
   // two accumulator buffers when they fit in TMEM's 512 columns, else one
   // (the MMA of the next tile then waits for the epilogue)
   static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
@@ -130,6 +148,7 @@ struct NsGemmShape {
   static_assert(kEpiWarps == 8, "the stage budget counts eight epilogue warps");
   static_assert(!F32 || (EPI != kEpiSquareBf16 && EPI != kEpiPolySingle),
                 "the bf16 mode has no tf32 form");
+  static_assert(!SPLIT || F32, "split planes are tf32");
   static_assert(!SWAP || (DUAL && !B_MN && PAIR && kBNc == 64), "transposed Poly: pairs, dual");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
@@ -212,13 +231,30 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
 // for F32), stored as X' or, in the last iteration, applied as
 // p -= lr*scale*o in the parameter's orientation (lib.rs:169-174). bx is
 // overwritten with o.
-template <bool F32>
+template <bool F32, bool SPLIT = false>
 __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r, int c0,
                                             bool row_ok, bool cols_full, float s,
                                             float (&v)[32]) {
-  const long long xoff = (long long)b * args.aux_bstride + (long long)r * args.aux_ld + c0;
+  const long long xoff = (long long)b * args.aux_bstride * (SPLIT ? 2 : 1) +
+                         (long long)r * args.aux_ld + c0;
   float xv[32];
-  if constexpr (F32) {
+  if constexpr (SPLIT) {
+    // X = hi + lo (planes 2b and 2b + 1); no rounding point: the sum is X's
+    // fp32 value up to the bits below the lo plane's tf32 precision
+    const float* xh = static_cast<const float*>(args.aux) + xoff;
+    const float* xl = xh + args.aux_bstride;
+    if (row_ok && cols_full) {
+      float lo[32];
+      load_f32x32(xh, xv);
+      load_f32x32(xl, lo);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) xv[j] = __fadd_rn(xv[j], lo[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        xv[j] = (row_ok && c0 + j < args.N) ? __fadd_rn(xh[j], xl[j]) : 0.0f;
+    }
+  } else if constexpr (F32) {
     const float* xrow = static_cast<const float*>(args.aux) + xoff;
     if (row_ok && cols_full) {
       load_f32x32(xrow, xv);
@@ -240,11 +276,34 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
   for (int j = 0; j < 32; ++j) {
     const float x0 = s != 1.0f ? __fdiv_rn(xv[j], s) : xv[j];
     const float bs = s != 1.0f ? __fdiv_rn(v[j], s) : v[j];
-    v[j] = op_round<F32>(__fadd_rn(__fmul_rn(x0, args.coef_a), bs));
+    const float o = __fadd_rn(__fmul_rn(x0, args.coef_a), bs);
+    v[j] = SPLIT ? o : op_round<F32>(o);
   }
   if (!args.p) {
-    const long long ooff = (long long)b * args.out_bstride + (long long)r * args.out_ld + c0;
-    if constexpr (F32) {
+    const long long ooff = (long long)b * args.out_bstride * (SPLIT ? 2 : 1) +
+                           (long long)r * args.out_ld + c0;
+    if constexpr (SPLIT) {
+      // X' as its hi and lo tf32 planes
+      float hi[32], lo[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        hi[j] = tf32r(v[j]);
+        lo[j] = tf32r(__fsub_rn(v[j], hi[j]));
+      }
+      float* oh = static_cast<float*>(args.out) + ooff;
+      float* ol = oh + args.out_bstride;
+      if (row_ok && cols_full) {
+        store_f32x32(oh, hi);
+        store_f32x32(ol, lo);
+      } else if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < args.N) {
+            oh[j] = hi[j];
+            ol[j] = lo[j];
+          }
+      }
+    } else if constexpr (F32) {
       float* orow = static_cast<float*>(args.out) + ooff;
       if (row_ok && cols_full) {
         store_f32x32(orow, v);
@@ -325,13 +384,13 @@ __device__ __forceinline__ void ns_mma(uint32_t d, uint64_t da, uint64_t db, uin
   }
 }
 
-template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false>
+template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false, bool SPLIT = false>
 __global__ void __launch_bounds__(320, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_a2,
                    const __grid_constant__ CUtensorMap tm_b, const NsGemmArgs args) {
   constexpr bool kSwap = EPI == kEpiPolyDualT;
-  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32>;
+  using S = NsGemmShape<BN, DUAL, B_MN, PAIR, EPI, F32, SPLIT>;
   constexpr int kBK = S::kBKe;  // K per stage
   constexpr int STAGES = S::kStages;
   constexpr bool kSym = EPI == kEpiGram || EPI == kEpiSquare || EPI == kEpiSquareBf16;
@@ -431,37 +490,40 @@ __global__ void __launch_bounds__(320, 1)
           uint8_t* st = tiles + stage * S::kStageBytes;
           if (leader) mbar_arrive_expect_tx(&full[stage], S::kStageBytes * S::kCtas);
           const int k0 = kb * kBK;
-          uint8_t* sb = st + S::kABytes * (DUAL ? 2 : 1);
-          if (kSwap) {
-            // A side: X^T rows row0.. = X columns, two 64-column MN-major boxes;
-            // B side: rows col0.. of A (tm_b) and of A2 (tm_a2), K-major.
-            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          // One load of a box into st_dst, on the pair's leader barrier or this CTA's.
+          const uint32_t fb = PAIR ? mapa_shared(smem_u32(&full[stage]), 0) : 0u;
+          auto load = [&](uint8_t* dst, const CUtensorMap* map, int x, int y, int z) {
+            if constexpr (PAIR)
+              tma_load_3d_pair(dst, map, fb, x, y, z);
+            else
+              tma_load_3d(dst, map, &full[stage], x, y, z);
+          };
+          // SPLIT: every operand comes as two planes (hi at batch index 2b, lo
+          // at 2b + 1), stored one after the other in the stage.
 #pragma unroll
-            for (int g = 0; g < kBM / S::kMNe; ++g)  // 2 (bf16) or 4 (tf32) boxes
-              tma_load_3d_pair(st + g * (kBK * 128), &tm_a1, fb, row0 + g * S::kMNe, k0, b);
-            tma_load_3d_pair(st + S::kABytes, &tm_b, fb, k0, col0, b);
-            tma_load_3d_pair(st + S::kABytes + S::kBBytes, &tm_a2, fb, k0, col0, b);
-          } else if (PAIR) {
-            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_3d_pair(st, &tm_a1, fb, k0, row0, b);
-            if (DUAL) tma_load_3d_pair(st + S::kABytes, &tm_a2, fb, k0, row0, b);
-            if (B_MN) {
+          for (int pl = 0; pl < S::kPlanes; ++pl) {
+            const int z = b * S::kPlanes + pl;
+            if (kSwap) {
+              // A side: X^T rows row0.. = X columns, 128-byte-wide MN-major
+              // boxes; B side: rows col0.. of A (tm_b) and of A2 (tm_a2), K-major.
+              uint8_t* sa = st + pl * S::kABytes;
+              uint8_t* sbp = st + S::kPlanes * S::kABytes + pl * 2 * S::kBBytes;
 #pragma unroll
-              for (int g = 0; g < S::kBNc / S::kMNe; ++g)
-                tma_load_3d_pair(sb + g * (kBK * 128), &tm_b, fb, col0 + g * S::kMNe, k0, b);
+              for (int g = 0; g < kBM / S::kMNe; ++g)  // 2 (bf16) or 4 (tf32) boxes
+                load(sa + g * (kBK * 128), &tm_a1, row0 + g * S::kMNe, k0, z);
+              load(sbp, &tm_b, k0, col0, z);
+              load(sbp + S::kBBytes, &tm_a2, k0, col0, z);
             } else {
-              tma_load_3d_pair(sb, &tm_b, fb, k0, col0, b);
-            }
-          } else {
-            tma_load_3d(st, &tm_a1, &full[stage], k0, row0, b);
-            if (DUAL) tma_load_3d(st + S::kABytes, &tm_a2, &full[stage], k0, row0, b);
-            if (B_MN) {
+              load(st + pl * S::kABytes, &tm_a1, k0, row0, z);
+              if (DUAL) load(st + (S::kPlanes + pl) * S::kABytes, &tm_a2, k0, row0, z);
+              uint8_t* sbp = st + S::kPlanes * S::kABytes * (DUAL ? 2 : 1) + pl * S::kBBytes;
+              if (B_MN) {
 #pragma unroll
-              for (int g = 0; g < S::kBNc / S::kMNe; ++g)
-                tma_load_3d(sb + g * (kBK * 128), &tm_b, &full[stage], col0 + g * S::kMNe, k0,
-                            b);
-            } else {
-              tma_load_3d(sb, &tm_b, &full[stage], k0, col0, b);
+                for (int g = 0; g < S::kBNc / S::kMNe; ++g)
+                  load(sbp + g * (kBK * 128), &tm_b, col0 + g * S::kMNe, k0, z);
+              } else {
+                load(sbp, &tm_b, k0, col0, z);
+              }
             }
           }
           issued_mask |= 1u << stage;
@@ -523,31 +585,47 @@ __global__ void __launch_bounds__(320, 1)
           }
           tc_fence_after();
           const uint32_t a1 = smem_u32(tiles + stage * S::kStageBytes);
-          const uint32_t a2 = a1 + S::kABytes;
-          const uint32_t bb = a1 + S::kABytes * (DUAL ? 2 : 1);
+          // SPLIT: products hi*hi + hi*lo + lo*hi of the two planes (plane pa of
+          // the A operand, pb of the B operand), the three-pass tf32 product that
+          // carries about 21 mantissa bits; hi*hi into the main accumulator, the
+          // two corrections into the one kSmallOff columns further.
+          constexpr int kCombos = SPLIT ? 3 : 1;
           if (kSwap) {
             // The CTA's A box and A2 box lie back to back: one 128-row K-major B
             // operand per CTA, 256 rows for the pair. Accumulator columns:
             // [A X | A2 X] for the leader's 64 rows of A, then the same for the
             // peer's 64 rows.
-            const uint32_t b1 = a1 + S::kABytes;
+            const uint32_t b1 = a1 + S::kPlanes * S::kABytes;
 #pragma unroll
             for (int kk = 0; kk < kKSteps; ++kk) {
-              const uint64_t da = mn_desc(a1 + kk * kMnStep);
-              const uint64_t db = umma_desc_sw128(b1 + kk * 32, 16, 1024);
-              ns_mma<F32, true>(d1, da, db, idesc, (kb | kk) != 0);
+#pragma unroll
+              for (int cmb = 0; cmb < kCombos; ++cmb) {
+                const uint32_t pa = cmb == 2, pb = cmb == 1;
+                const uint64_t da = mn_desc(a1 + pa * S::kABytes + kk * kMnStep);
+                const uint64_t db = umma_desc_sw128(b1 + pb * 2 * S::kBBytes + kk * 32, 16, 1024);
+                ns_mma<F32, true>(d1 + (cmb ? S::kSmallOff : 0), da, db, idesc,
+                                  cmb == 2 || (kb | kk) != 0);
+              }
             }
           }
+          const uint32_t a2 = a1 + S::kPlanes * S::kABytes;
+          const uint32_t bb = a1 + S::kPlanes * S::kABytes * (DUAL ? 2 : 1);
 #pragma unroll
           for (int kk = 0; kk < (kSwap ? 0 : kKSteps); ++kk) {
-            const uint64_t da1 = umma_desc_sw128(a1 + kk * 32, 16, 1024);
-            const uint64_t db = B_MN ? mn_desc(bb + kk * kMnStep)
-                                     : umma_desc_sw128(bb + kk * 32, 16, 1024);
-            const uint32_t accum = (kb | kk) != 0;
-            ns_mma<F32, PAIR>(d1, da1, db, idesc, accum);
-            if (DUAL) {
-              const uint64_t da2 = umma_desc_sw128(a2 + kk * 32, 16, 1024);
-              ns_mma<F32, PAIR>(d2, da2, db, idesc, accum);
+#pragma unroll
+            for (int cmb = 0; cmb < kCombos; ++cmb) {
+              const uint32_t pa = cmb == 2, pb = cmb == 1;
+              const uint64_t da1 = umma_desc_sw128(a1 + pa * S::kABytes + kk * 32, 16, 1024);
+              const uint32_t bp = bb + pb * S::kBBytes;
+              const uint64_t db = B_MN ? mn_desc(bp + kk * kMnStep)
+                                       : umma_desc_sw128(bp + kk * 32, 16, 1024);
+              const uint32_t accum = cmb == 2 || (kb | kk) != 0;
+              const uint32_t off = cmb ? S::kSmallOff : 0;
+              ns_mma<F32, PAIR>(d1 + off, da1, db, idesc, accum);
+              if (DUAL) {
+                const uint64_t da2 = umma_desc_sw128(a2 + pa * S::kABytes + kk * 32, 16, 1024);
+                ns_mma<F32, PAIR>(d2 + off, da2, db, idesc, accum);
+              }
             }
           }
           issued_any = true;
@@ -642,17 +720,30 @@ __global__ void __launch_bounds__(320, 1)
         const bool cols_full = c0 + 32 <= col_dim;
         float v[32];
         float w[32];
-        if (kSwap) {
-          // rows tn*BN + ch*32 .. +31 of A X at column (ch/2)*128 + (ch%2)*32,
-          // of A2 X 64 columns further
-          const uint32_t col = (uint32_t)((ch >> 1) * 128 + (ch & 1) * 32);
-          tmem_ld_32x32b_x32(tbase + col, v);
-          tmem_ld_32x32b_x32(tbase + col + 64, w);
+        // rows tn*BN + ch*32 .. +31 of A X at column (ch/2)*128 + (ch%2)*32 and
+        // of A2 X 64 columns further (transposed Poly), or columns ch*32.. of
+        // the first accumulator and BN further of the second
+        const uint32_t col_v = kSwap ? (uint32_t)((ch >> 1) * 128 + (ch & 1) * 32) : ch * 32;
+        const uint32_t col_w = kSwap ? col_v + 64 : BN + ch * 32;
+        tmem_ld_32x32b_x32(tbase + col_v, v);
+        if constexpr (SPLIT) {
+          // main + corrections, rounded once
+          float t[32];
+          tmem_ld_32x32b_x32(tbase + S::kSmallOff + col_v, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], t[j]);
+          if (DUAL) {
+            tmem_ld_32x32b_x32(tbase + col_w, w);
+            tmem_ld_32x32b_x32(tbase + S::kSmallOff + col_w, t);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __fadd_rn(w[j], t[j]);
+          }
         } else {
-          tmem_ld_32x32b_x32(tbase + ch * 32, v);
-          if (DUAL) tmem_ld_32x32b_x32(tbase + BN + ch * 32, w);
+          if (DUAL) tmem_ld_32x32b_x32(tbase + col_w, w);
+          tmem_ld_wait();
         }
-        tmem_ld_wait();
         if (kSym) {
           // This tile owns the symmetric entries with col >= row and writes each
           // at (r, c) and, through a transposing smem stage, at (c, r).
@@ -684,6 +775,37 @@ __global__ void __launch_bounds__(320, 1)
           // takes its lower triangle from the mirrored values so that the
           // output is exactly symmetric. The stores clip at the matrix edge.
           const bool diag = c0 == rw;
+          if constexpr (SPLIT) {
+            // The fp32 result as its hi and lo tf32 planes (batch items 2b and
+            // 2b + 1), stored from registers: the direct entries (r, c0 + j) and
+            // the mirrored ones (c0 + j, r); on a diagonal block the lower
+            // triangle comes from the mirrored values only.
+#pragma unroll
+            for (int pl = 0; pl < 2; ++pl) {
+              float* o = static_cast<float*>(args.out) + (long long)(b * 2 + pl) * args.out_bstride;
+              float pv[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float hi = tf32r(v[j]);
+                pv[j] = pl == 0 ? hi : tf32r(__fsub_rn(v[j], hi));
+              }
+              if (row_ok) {
+                float* orow = o + (long long)r * args.out_ld + c0;
+                if (!diag && cols_full) {
+                  store_f32x32(orow, pv);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if ((!diag || j >= lane) && c0 + j < args.N) orow[j] = pv[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if ((!diag || j > lane) && c0 + j < args.N)
+                    o[(long long)(c0 + j) * args.out_ld + r] = pv[j];
+              }
+            }
+            continue;
+          }
           if (lane == 0) bulk_wait_read_all();  // this warp's previous stores read their stage
           __syncwarp();
           uint8_t* mir_base = stg + 32 * 32 * S::kEsz;
@@ -738,9 +860,9 @@ __global__ void __launch_bounds__(320, 1)
             for (int j = 0; j < 32; ++j) v[j] = tst[lane * 33 + j];
             __syncwarp();
             const int xr = c0 + lane;
-            poly_finish<F32>(args, b, xr, rw, xr < args.M, rw + 32 <= args.N, s, v);
+            poly_finish<F32, SPLIT>(args, b, xr, rw, xr < args.M, rw + 32 <= args.N, s, v);
           } else {
-            poly_finish<F32>(args, b, r, c0, row_ok, cols_full, s, v);
+            poly_finish<F32, SPLIT>(args, b, r, c0, row_ok, cols_full, s, v);
           }
         }
       }

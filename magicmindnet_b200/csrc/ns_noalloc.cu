@@ -81,10 +81,10 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
   using namespace mmn;
   if (!g || !out) return fail(MMN_E_INVALID, "null input or output");
   if (steps < 0) return fail(MMN_E_INVALID, "steps must be >= 0");
-  if (ns_mode == MMN_NS_TF32)
+  if (ns_mode == MMN_NS_TF32 || ns_mode == MMN_NS_FP32)
     return fail(MMN_E_UNSUPPORTED,
-                "MMN_NS_TF32 needs twice the fixed scratch of mmn_newton_schulz5_noalloc "
-                "(use mmn_newton_schulz5)");
+                "the TF32 and fp32 modes need more than the fixed scratch of "
+                "mmn_newton_schulz5_noalloc (use mmn_newton_schulz5)");
   if (ns_mode != MMN_NS_REFERENCE && ns_mode != MMN_NS_BF16)
     return fail(MMN_E_INVALID, "unknown ns_mode");
   if (rows < 1 || cols < 1) return fail(MMN_E_SHAPE, "empty matrix");

@@ -102,7 +102,8 @@ class MuonConfig:
         return N.MuonConfigC(self.lr, self.momentum, int(self.nesterov), int(self.ns_steps))
 
 
-NS_MODES = {"reference": N.NS_REFERENCE, "bf16": N.NS_BF16, "tf32": N.NS_TF32}
+NS_MODES = {"reference": N.NS_REFERENCE, "bf16": N.NS_BF16, "tf32": N.NS_TF32,
+            "fp32": N.NS_FP32}
 
 
 class AdamW:

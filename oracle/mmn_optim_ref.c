@@ -240,8 +240,10 @@ float ref_tf32_round(float x) {
     return r;
 }
 
-/* The rounding point of a Newton-Schulz variant: bf16, or tf32 for REF_NS_TF32. */
+/* The rounding point of a Newton-Schulz variant: bf16, tf32 for REF_NS_TF32,
+ * none for REF_NS_FP32. */
 static float ns_round(float x, int variant) {
+    if (variant == REF_NS_FP32) return x;
     return variant == REF_NS_TF32 ? ref_tf32_round(x) : ref_bf16_round(x);
 }
 
@@ -257,7 +259,8 @@ static const float NS_EPS = 1e-7f;                                  /* lib.rs:87
  *   B    = A_bf*b + A2*c                 (:117, kept fp32)
  *   x'   = bf16(x*a + B*x)               (:118-119)
  * REF_NS_BF16 additionally rounds B to bf16 (no reference counterpart).
- * REF_NS_TF32 rounds to tf32 wherever the reference rounds to bf16.
+ * REF_NS_TF32 rounds to tf32 wherever the reference rounds to bf16;
+ * REF_NS_FP32 does not round at all.
  */
 void ref_ns_iteration(const float *x, int64_t n, int64_t m, float *x_next, int gemm_order,
                       int variant, int n_threads) {
@@ -288,7 +291,8 @@ void ref_ns_iteration(const float *x, int64_t n, int64_t m, float *x_next, int g
  * zero-padding branch at :93-99 is applied by the caller before this point).
  * Transposes when rows > cols (:101-107, :122-124); the Frobenius norm is a
  * sequential fp32 sum over the transposed matrix in row-major order, clamped
- * with max(1e-7) (:109), and the input is divided by it (:110).
+ * with max(1e-7) (:109), and the input is divided by it (:110). REF_NS_FP32
+ * sums in fp64 and rounds the sum to fp32 once.
  */
 int ref_newton_schulz5(const float *g, int64_t rows, int64_t cols, int steps, float *out,
                        int gemm_order, int variant, float *norm_out, int n_threads) {
@@ -300,7 +304,15 @@ int ref_newton_schulz5(const float *g, int64_t rows, int64_t cols, int steps, fl
         for (int64_t j = 0; j < m; ++j)
             x[i * m + j] = ns_round(transposed ? g[j * cols + i] : g[i * cols + j], variant);
     float s = 0.0f;
-    for (int64_t i = 0; i < n * m; ++i) s = s + x[i] * x[i];
+    if (variant == REF_NS_FP32) {
+        /* fp32 mode (no reference counterpart): the correctly rounded fp32 sum
+         * of squares, so that the norm carries no summation-order error */
+        double d = 0.0;
+        for (int64_t i = 0; i < n * m; ++i) d += (double)x[i] * (double)x[i];
+        s = (float)d;
+    } else {
+        for (int64_t i = 0; i < n * m; ++i) s = s + x[i] * x[i];
+    }
     float norm = fmaxf(sqrtf(s), NS_EPS);
     if (norm_out) *norm_out = norm;
     for (int64_t i = 0; i < n * m; ++i) x[i] = x[i] / norm;

@@ -39,9 +39,12 @@ enum {
 enum {
     REF_NS_REFERENCE = 0, /* lib.rs:112-120 exactly: B = b*A_bf + c*A2_bf kept fp32 */
     REF_NS_BF16 = 1,      /* fast variant (no reference counterpart): B rounded to bf16 */
-    REF_NS_TF32 = 2       /* TF32 mode (no reference counterpart): the REF_NS_REFERENCE
+    REF_NS_TF32 = 2,      /* TF32 mode (no reference counterpart): the REF_NS_REFERENCE
                              recipe with every bf16 rounding point of lib.rs:104,115,116,119
                              replaced by a tf32 rounding (10-bit mantissa, nearest-even) */
+    REF_NS_FP32 = 3       /* fp32 mode (no reference counterpart): the same recipe with no
+                             rounding points at all, every value kept in fp32, and the
+                             norm's sum of squares rounded to fp32 once */
 };
 
 float ref_bf16_round(float x);

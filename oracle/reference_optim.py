@@ -28,7 +28,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libmmn_optim_ref.so")
 
 GEMM_F32_SEQ, GEMM_F32_FMA, GEMM_F64 = 0, 1, 2
-NS_REFERENCE, NS_BF16, NS_TF32 = 0, 1, 2
+NS_REFERENCE, NS_BF16, NS_TF32, NS_FP32 = 0, 1, 2, 3
 
 _f = ctypes.c_float
 _i64 = ctypes.c_int64

@@ -165,6 +165,18 @@ def test_ns_tf32_recipe_is_closer_to_exact_than_bf16(oracle):
     assert err(t) < 4e-3 and err(t) * 4 < err(b)
 
 
+def test_ns_fp32_recipe_matches_exact_newton_schulz(oracle):
+    """The fp32 mode's recipe (no rounding points, norm summed once in fp64)
+    is Newton-Schulz in fp32 arithmetic: within 1e-5 of the fp64 iteration."""
+    g = np.random.default_rng(9).normal(0, 1e-2, (96, 256)).astype(np.float32)
+    x = g.astype(np.float64) / np.linalg.norm(g.astype(np.float64))
+    for _ in range(5):
+        a = x @ x.T
+        x = 3.4445 * x + (-4.7750 * a + 2.0315 * (a @ a)) @ x
+    o = oracle.newton_schulz5(g, order=oracle.GEMM_F32_SEQ, variant=oracle.NS_FP32)
+    assert np.linalg.norm(o - x) / np.linalg.norm(x) < 1e-5
+
+
 def test_ns_transpose_rule_exact(oracle):
     rng = np.random.default_rng(2)
     g = rng.normal(0, 1e-2, (24, 40)).astype(np.float32)
