@@ -46,18 +46,39 @@ class RankTimeout(RuntimeError):
         self.step = step
 
 
+def _is_comm_error(e: BaseException) -> bool:
+    """A collective or store operation that ended with an error (a peer that
+    closed its connection, or the process group's timeout), as opposed to an
+    exception of this rank's own step."""
+    try:
+        import torch.distributed as dist
+
+        if isinstance(e, dist.DistError):
+            return True
+    except ImportError:  # torch is optional for the monitor itself
+        pass
+    if not isinstance(e, RuntimeError):
+        return False
+    msg = str(e)
+    return any(k in msg for k in ("gloo", "NCCL", "Connection closed", "Connection reset",
+                                  "timed out", "Timeout", "timeout"))
+
+
 class RankMonitor:
     """Heartbeats and failure reports of the ranks of one job, in a shared store
     (anything with ``set(key, value)``, ``get(key)`` and ``check([keys])``, such
     as ``torch.distributed.TCPStore``)."""
 
     def __init__(self, store, rank: int, world_size: int, deadline_s: float = 30.0,
-                 prefix: str = "mmn"):
+                 prefix: str = "mmn", grace_s: float = 2.0):
         self.store = store
         self.rank = rank
         self.world = world_size
         self.deadline = deadline_s
         self.prefix = prefix
+        # how long a rank whose collective failed waits for the peer at fault
+        # to publish its failure before it names the cause itself
+        self.grace = min(grace_s, deadline_s)
         self.step = 0
 
     def _key(self, kind: str, rank: int) -> str:
@@ -129,14 +150,23 @@ class RankMonitor:
             if isinstance(e, (RankFailure, RankTimeout)):
                 self.report_failure(str(e), "lost")
                 raise
+            comm = _is_comm_error(e)
             failed = self._failed_peer()
+            t0 = time.monotonic()
+            while comm and failed is None and time.monotonic() - t0 < self.grace:
+                # the collective failed because a peer left: it publishes why
+                # before its connections close, so give the report a moment
+                time.sleep(0.05)
+                failed = self._failed_peer()
             if failed is not None:
                 self.report_failure(f"peer rank {failed[0]} failed", "lost")
                 raise RankFailure(*failed) from e
-            late = self._not_started(k)
-            if late:
-                self.report_failure(f"peer ranks {late} stalled", "lost")
-                raise RankTimeout(late, k, self.deadline) from e
+            if comm:
+                late = self._not_started(k)
+                if late:
+                    self.report_failure(f"peer ranks {late} stalled", "lost")
+                    raise RankTimeout(late, k, self.deadline) from e
+            # this rank's own step raised: it is the cause
             self.report_failure(f"{type(e).__name__}: {e}")
             raise
         self.step_done()
