@@ -1,6 +1,13 @@
 """Benchmark of the hybrid AdamW + Newton-Schulz Muon optimizer step on B200.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+               [--ns-mode reference|bf16|tf32|fp32]
+
+Newton-Schulz modes: reference (the reference's bf16 rounding points, bf16 tensor
+cores; default), bf16 (B rounded to bf16 too), tf32 (tf32 rounding points,
+kind::tf32 tensor cores), fp32 (no rounding points, three-pass tf32 products).
+The tf32 and fp32 modes report against the dense TF32 peak measured in the run
+(divided by 3 for fp32).
 
 Workloads (synthetic, seeded; shapes from the reference model family):
   hybrid_1b   (default) d_model 2048, 24 layers, FFN 8192, vocab 32000, untied lm_head;
