@@ -153,3 +153,30 @@ def test_fp32_muon_and_batched_step_within_1e4(mmn, oracle):
             else:
                 np.testing.assert_array_equal(out.view(np.uint32), p_ref[n].view(np.uint32))
     step.close()
+
+
+def _exact_ns_fp64_on_gpu(g, steps=5):
+    """Exact Newton-Schulz in fp64 computed on the GPU with torch (the fp64
+    form of exact_ns, for sizes the CPU would take minutes on)."""
+    import torch
+
+    x = torch.from_numpy(g).cuda().double()
+    tr = x.shape[0] > x.shape[1]
+    if tr:
+        x = x.T
+    x = x / max(torch.linalg.norm(x).item(), 1e-7)
+    for _ in range(steps):
+        a = x @ x.T
+        x = NS_A * x + (NS_B * a + NS_C * (a @ a)) @ x
+    return (x.T if tr else x).cpu().numpy()
+
+
+@pytest.mark.parametrize("shape", [(4096, 14336), (14336, 4096), (4096, 4096)])
+def test_fp32_and_tf32_full_size_against_fp64(mmn, shape):
+    """The largest Newton-Schulz shapes of the benchmark configurations (the
+    4096 x 14336 FFN matrices and 4096 x 4096 projections), one matrix each,
+    against fp64 Newton-Schulz: fp32 mode within 1e-4, TF32 mode within 4e-3."""
+    g = np.random.default_rng(5).normal(0, 1e-2, shape).astype(np.float32)
+    exact = _exact_ns_fp64_on_gpu(g)
+    assert rel_fro(mmn.newton_schulz5(g, 5, ns_mode="fp32"), exact) <= 1e-4
+    assert rel_fro(mmn.newton_schulz5(g, 5, ns_mode="tf32"), exact) <= 4e-3
