@@ -88,7 +88,10 @@ def _worker(rank, world, port, q, exchange):
                             device_id=torch.device(f"cuda:{rank}"))
     try:
         model = _model()
-        cfg = mmn.StepConfig(rank=rank, world_size=world, use_graph=False)
+        # "<exchange>-<ns mode>" runs the sharded step in that Newton-Schulz mode
+        exchange, _, mode = exchange.partition("-")
+        cfg = mmn.StepConfig(rank=rank, world_size=world, use_graph=False,
+                             ns_mode=mode or "reference")
         step = mmn.OptimizerStep(model, cfg, device=rank,
                                  stream=torch.cuda.current_stream(rank).cuda_stream)
         _fill(step, model, 0)
@@ -121,7 +124,7 @@ def _worker(rank, world, port, q, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "fused", "host"])
+@pytest.mark.parametrize("exchange", ["nccl", "fused", "host", "fused-tf32", "fused-fp32"])
 def test_sharded_step_equals_single_gpu(mmn, exchange):
     import torch
     import torch.multiprocessing as mp
@@ -133,7 +136,8 @@ def test_sharded_step_equals_single_gpu(mmn, exchange):
     if exchange == "host":
         _run_host(model, world)
         return
-    single = mmn.OptimizerStep(model, mmn.StepConfig(use_graph=False), device=0)
+    mode = exchange.partition("-")[2] or "reference"
+    single = mmn.OptimizerStep(model, mmn.StepConfig(use_graph=False, ns_mode=mode), device=0)
     _fill(single, model, 0)
     single.step()
     single.step()
