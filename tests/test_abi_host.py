@@ -140,3 +140,20 @@ def test_errors_report_through_last_error():
     rc = N.lib().mmn_optim_create(None, -5, None, ctypes.byref(h))
     assert rc in (N.MMN_E_INVALID, N.MMN_E_NO_DEVICE)
     assert N.lib().mmn_last_error()
+
+
+def test_ns_mode_constants_agree():
+    """The Newton-Schulz modes have one numbering: the header's MMN_NS_*, the
+    Python mode names and the oracle's REF_NS_* variants."""
+    import magicmindnet_b200 as mmn  # noqa: F401
+    from magicmindnet_b200.optim import NS_MODES
+    from oracle import reference_optim as R
+
+    text = open(os.path.join(ROOT, "include", "mmn_optim.h")).read()
+    header = {k.lower(): int(v) for k, v in re.findall(r"#define MMN_NS_(\w+) (\d+)", text)}
+    assert header == {"reference": 0, "bf16": 1, "tf32": 2, "fp32": 3}
+    assert NS_MODES == header
+    assert (R.NS_REFERENCE, R.NS_BF16, R.NS_TF32, R.NS_FP32) == (0, 1, 2, 3)
+    ref_h = open(os.path.join(ROOT, "oracle", "mmn_optim_ref.h")).read()
+    assert dict(re.findall(r"REF_NS_(\w+) = (\d)", ref_h)) == {
+        "REFERENCE": "0", "BF16": "1", "TF32": "2", "FP32": "3"}
