@@ -280,10 +280,14 @@ def run_ours(args, rank, world, local_rank):
     else:
         adamw = mmn.AdamWConfig()
     dp = world > 1 and args.grad_reduce != "none"
+    # loss-scaled sharded steps: each rank scans only what it steps and tells
+    # the others (mmn_optim_scan_grads), unless --scan full
+    shard_scan = (is_8b and world > 1 and not dp and args.scan == "shard"
+                  and args.exchange == "fused")
     cfg = mmn.StepConfig(adamw=adamw, muon=mmn.MuonConfig(), ns_mode=args.ns_mode,
                          grad_dtype=spec["grad"], bf16_param_shadow=is_8b, loss_scaling=is_8b,
                          rank=rank, world_size=world, use_graph=True,
-                         reduce_grads=dp and args.grad_reduce == "fused")
+                         reduce_grads=dp and args.grad_reduce == "fused", scan_shard=shard_scan)
     stream = torch.cuda.current_stream(dev)
     step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg, device=dev,
                              stream=stream.cuda_stream)
@@ -340,6 +344,8 @@ def run_ours(args, rank, world, local_rank):
                 reduces.append((full, full[rank * gl[region]:(rank + 1) * gl[region]]))
 
     def one_step():
+        if shard_scan:
+            step.scan_grads()
         if dp and args.grad_reduce == "fused":
             step.reduce_grads()
         elif reduces:
@@ -417,17 +423,23 @@ def run_ours(args, rank, world, local_rank):
                 off = plan["offset"][k]
                 stepped.append(max(0, min(off + n, (rank + 1) * areg) - max(off, rank * areg)))
         gsz = 2 if spec["grad"] == "bf16" else 4
-        pin_g = [step.grad(k).cpu().pin_memory() if stepped[k] or (is_8b and world > 1) else None
+        full_in = is_8b and world > 1 and not shard_scan  # the scan reads every grad
+        pin_g = [step.grad(k).cpu().pin_memory() if stepped[k] or full_in else None
                  for k in range(len(model))]
         pin_p = [torch.empty(s, dtype=torch.float32).pin_memory() if stepped[k] else None
                  for k, (_, s, _) in enumerate(model)]
-        full_in = is_8b and world > 1  # the non-finite scan reads every grad
+        no_g = [None] * len(model)
         bi = sum((int(np.prod(s)) if full_in else stepped[k]) * gsz
                  for k, (_, s, _) in enumerate(model))
         bo = sum(stepped) * 4
 
         def host_step():
-            step.step_host(pin_g, pin_p, divisor)
+            if shard_scan:
+                # this rank's grads in and scanned, every rank's verdict in, then the step
+                step.scan_grads(pin_g)
+                step.step_host(no_g, pin_p, divisor)
+            else:
+                step.step_host(pin_g, pin_p, divisor)
             if fused:
                 step.exchange_fence()
             if gathers:
@@ -512,7 +524,8 @@ def run_ours(args, rank, world, local_rank):
                 "traffic_unit": "DRAM bytes per launch (ncu: 28 B per param on the 2^28 arena)",
                 "algorithmic_bytes": a_bytes_per * a_elems_rank}
     per_step, per_reduce = step.kernel_launches()
-    launches_per_step = per_step + (per_reduce if dp and args.grad_reduce == "fused" else 0)
+    launches_per_step = per_step + (per_reduce if (dp and args.grad_reduce == "fused") or shard_scan
+                                    else 0)
     line = {
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -532,6 +545,9 @@ def run_ours(args, rank, world, local_rank):
                                     "nccl": "NCCL reduce-scatter of the grad arenas"}
                                    [args.grad_reduce] if dp else
                                    "none (grads already reduced, as the configurations assume)"),
+                   "nonfinite_scan": (("sharded: each rank scans what it steps and sets every "
+                                       "rank's flag (mmn_optim_scan_grads)") if shard_scan else
+                                      "every rank scans every grad") if is_8b else None,
                    "l2": "inputs larger than L2 (no flush needed)"},
         "roofline": roof, "components": comp, "clocks": clk, "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
@@ -583,6 +599,10 @@ def main():
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU parameter exchange: copy-engine pushes over NVLink inside "
                          "the step (CUDA IPC) or an NCCL all-gather after the step")
+    ap.add_argument("--scan", default="shard", choices=["shard", "full"],
+                    help="multi-GPU loss-scaled steps: each rank scans only the grads it "
+                         "steps and sets every rank's skip flag (shard), or every rank scans "
+                         "every grad (full)")
     ap.add_argument("--grad-reduce", default="none", choices=["none", "fused", "nccl"],
                     help="multi-GPU: also time the data-parallel grad reduction before each "
                          "step (fused: mmn_optim_reduce_grads over NVLink; nccl: "

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MMN_OPTIM_ABI_VERSION 2
+#define MMN_OPTIM_ABI_VERSION 3
 
 /* status codes */
 #define MMN_OK 0
@@ -252,6 +252,9 @@ typedef struct {
                                  mmn_optim_reduce_grads sums them across ranks before
                                  each step (data parallelism); the step then takes its
                                  skip decision from that call instead of scanning */
+    int32_t scan_shard;       /* 1 (loss_scaling, world_size > 1, grads replicated): each
+                                 rank scans only what it steps, in mmn_optim_scan_grads,
+                                 and sets every rank's skip flag; the step does not scan */
 } mmn_optim_config;
 
 /* Defaults: AdamW/Muon defaults, hybrid, reference NS, persistent state, f32
@@ -387,6 +390,19 @@ int mmn_optim_connect_peers(mmn_optim_t *h, const void *blobs);
  * all-reduces on the same stream. Asynchronous. */
 int mmn_optim_reduce_grads(mmn_optim_t *h);
 
+/* Non-finite scan of this rank's part of the grads (config.scan_shard = 1,
+ * after mmn_optim_connect_peers), the sharded form of the scan every rank
+ * otherwise runs over every grad inside mmn_optim_step: a non-finite value in
+ * this rank's Muon matrices or AdamW range sets every rank's skip flag
+ * through peer memory, so each rank reads 1/world_size of the grads. `grads`
+ * NULL: the grads are on the device; else host buffers per slot (NULL entries
+ * skipped) of which this rank's parts are copied in first, and the call
+ * returns once they have been read. Order the ranks between this call and the
+ * step that uses the flag (e.g. a one-element all-reduce on the same stream),
+ * as for mmn_optim_reduce_grads; with scan_shard, mmn_optim_step_host takes
+ * null grads (they came in here). No counterpart in the reference. */
+int mmn_optim_scan_grads(mmn_optim_t *h, const void *const *grads);
+
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
 
@@ -395,7 +411,8 @@ int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64
 int mmn_optim_ns_flops(mmn_optim_t *h, double *flops);
 
 /* Kernel launches one mmn_optim_step enqueues on this rank, and one
- * mmn_optim_reduce_grads (0 unless reduce_grads). */
+ * mmn_optim_reduce_grads or mmn_optim_scan_grads (0 unless reduce_grads or
+ * scan_shard). */
 int mmn_optim_kernel_launches(mmn_optim_t *h, int64_t *per_step, int64_t *per_reduce);
 
 /* Per-step device-time breakdown in ms, averaged over the steps enqueued since

@@ -61,7 +61,7 @@ class OptimConfigC(ctypes.Structure):
                 ("loss_scaling", ctypes.c_int32), ("loss_scale_init", ctypes.c_float),
                 ("growth_interval", ctypes.c_int32), ("rank", ctypes.c_int32),
                 ("world_size", ctypes.c_int32), ("use_graph", ctypes.c_int32),
-                ("reduce_grads", ctypes.c_int32)]
+                ("reduce_grads", ctypes.c_int32), ("scan_shard", ctypes.c_int32)]
 
 
 class GatherLayoutC(ctypes.Structure):
@@ -136,6 +136,7 @@ SIGNATURES = {
     "mmn_optim_export_ipc": (_i, [_vp, _vp]),
     "mmn_optim_connect_peers": (_i, [_vp, ctypes.c_char_p]),
     "mmn_optim_reduce_grads": (_i, [_vp]),
+    "mmn_optim_scan_grads": (_i, [_vp, _vp]),
     "mmn_optim_plan": (_i, [_i64p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, _i, _i, _i,
                             ctypes.POINTER(_i), _i64p, _i64p, _i64p]),
     "mmn_optim_ns_flops": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),

@@ -289,6 +289,7 @@ extern "C" mmn_optim_config mmn_optim_config_default(void) {
   c.world_size = 1;
   c.use_graph = 1;
   c.reduce_grads = 0;
+  c.scan_shard = 0;
   return c;
 }
 
@@ -305,6 +306,9 @@ extern "C" int mmn_optim_create(const mmn_optim_config* cfg, int device, void* s
     return fail(MMN_E_INVALID, "grad_dtype must be f32 or bf16");
   if (c.muon.ns_steps < 0) return fail(MMN_E_INVALID, "ns_steps must be >= 0");
   if (c.loss_scaling && !(c.loss_scale_init > 0.0f)) return fail(MMN_E_INVALID, "loss scale <= 0");
+  if (c.scan_shard && (!c.loss_scaling || c.world_size < 2 || c.reduce_grads))
+    return fail(MMN_E_INVALID,
+                "scan_shard needs loss_scaling, world_size > 1 and reduce_grads = 0");
   auto* h = new mmn_optim();
   h->cfg = c;
   int rc = h->ctx.init(device, stream);
@@ -902,7 +906,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       }
       MMN_CUDA_TRY(cudaEventRecord(h->h2d_ev[j], h->h2d));
     }
-    if (h->cfg.loss_scaling && h->cfg.world_size > 1) {
+    if (h->cfg.loss_scaling && h->cfg.world_size > 1 && !h->cfg.scan_shard) {
       // the non-finite scan reads every grad: the peers' parts come in too
       int64_t lo, hi;
       for (size_t i = 0; i < h->slots.size(); ++i) {
@@ -914,10 +918,11 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     MMN_CUDA_TRY(cudaEventRecord(h->h2d_ev.back(), h->h2d));
   }
 
-  if (h->cfg.loss_scaling && !h->cfg.reduce_grads) {
+  if (h->cfg.loss_scaling && !h->cfg.reduce_grads && !h->cfg.scan_shard) {
     // Every rank scans every grad (grads are replicated), so all ranks reach
     // the same skip decision without a collective. (With reduce_grads the
-    // reduction already set the flag on every rank.)
+    // reduction, with scan_shard mmn_optim_scan_grads, already set the flag on
+    // every rank.)
     if (io) MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->h2d_ev.back(), 0));
     MMN_CUDA_TRY(cudaMemsetAsync(h->d_skip, 0, sizeof(int), s));
     const int64_t a_n = h->a_used4 * 4;
@@ -1107,7 +1112,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   t.step_counter = h->d_step;
   t.adamw_calls = h->n_adamw;
   t.skip = h->cfg.loss_scaling ? h->d_skip : nullptr;
-  t.reset_skip = h->cfg.reduce_grads;
+  t.reset_skip = h->cfg.reduce_grads || h->cfg.scan_shard;
   t.grad_scale = h->cfg.loss_scaling ? h->d_scale : nullptr;
   t.good_steps = h->d_good;
   t.growth_interval = h->cfg.growth_interval > 0 ? h->cfg.growth_interval : 2000;
@@ -1167,6 +1172,12 @@ extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
   if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
   if (h->cfg.reduce_grads)
     return fail(MMN_E_UNSUPPORTED, "a step from host memory takes already-reduced grads");
+  if (h->cfg.scan_shard)
+    for (size_t i = 0; i < h->slots.size(); ++i)
+      if (grads[i])
+        return fail(MMN_E_STATE,
+                    "with scan_shard the grads go in through mmn_optim_scan_grads, before "
+                    "the step: pass null grads here");
   DevGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
@@ -1263,9 +1274,10 @@ struct IpcBlob {
   int32_t rank, world;
   int32_t shadow;
   int64_t a_total4, m_total;
-  int32_t grad_dtype, reduce_grads;
+  int32_t grad_dtype, reduce_grads, scan_shard;
   cudaIpcMemHandle_t ap, mp, ap16, mp16;
-  cudaIpcMemHandle_t ga, gm, skip;  // grad arenas and skip flag (reduce_grads)
+  cudaIpcMemHandle_t ga, gm;  // grad arenas (reduce_grads)
+  cudaIpcMemHandle_t skip;    // skip flag (reduce_grads or scan_shard)
 };
 static_assert(sizeof(IpcBlob) <= MMN_IPC_BLOB_BYTES, "IPC blob size");
 constexpr uint32_t kIpcMagic = 0x4D4D4E31u;  // "MMN1"
@@ -1285,6 +1297,7 @@ extern "C" int mmn_optim_export_ipc(mmn_optim_t* h, void* blob) {
   b.m_total = h->m_total;
   b.grad_dtype = h->cfg.grad_dtype;
   b.reduce_grads = h->cfg.reduce_grads;
+  b.scan_shard = h->cfg.scan_shard;
   MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ap, h->ap));
   MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.mp, h->mp));
   if (b.shadow) {
@@ -1294,8 +1307,8 @@ extern "C" int mmn_optim_export_ipc(mmn_optim_t* h, void* blob) {
   if (b.reduce_grads) {
     MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.ga, h->ag));
     MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.gm, h->mg));
-    MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.skip, h->d_skip));
   }
+  if (b.reduce_grads || b.scan_shard) MMN_CUDA_TRY(cudaIpcGetMemHandle(&b.skip, h->d_skip));
   memset(blob, 0, MMN_IPC_BLOB_BYTES);
   memcpy(blob, &b, sizeof(b));
   return MMN_OK;
@@ -1330,7 +1343,7 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     if (b.magic != kIpcMagic || b.rank != r || b.world != W ||
         b.shadow != h->cfg.bf16_param_shadow || b.a_total4 != h->a_total4 ||
         b.m_total != h->m_total || b.grad_dtype != h->cfg.grad_dtype ||
-        b.reduce_grads != h->cfg.reduce_grads) {
+        b.reduce_grads != h->cfg.reduce_grads || b.scan_shard != h->cfg.scan_shard) {
       rc = fail(MMN_E_INVALID, "peer blob does not match this rank's layout");
       break;
     }
@@ -1348,12 +1361,14 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     peer_m[n_peers] = mp;
     ++n_peers;
     if (h->cfg.reduce_grads) {
-      void *ga = nullptr, *gm = nullptr, *sk = nullptr;
-      if ((rc = open(b.ga, &ga)) != MMN_OK || (rc = open(b.gm, &gm)) != MMN_OK ||
-          (rc = open(b.skip, &sk)) != MMN_OK)
-        break;
+      void *ga = nullptr, *gm = nullptr;
+      if ((rc = open(b.ga, &ga)) != MMN_OK || (rc = open(b.gm, &gm)) != MMN_OK) break;
       rank_ga[r] = ga;
       rank_gm[r] = gm;
+    }
+    if (h->cfg.reduce_grads || h->cfg.scan_shard) {
+      void* sk = nullptr;
+      if ((rc = open(b.skip, &sk)) != MMN_OK) break;
       rank_skip[r] = static_cast<int*>(sk);
     }
   }
@@ -1373,7 +1388,7 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
     h->rank_gm[r] = rank_gm[r];
     h->rank_skip[r] = rank_skip[r];
   }
-  h->reduce_ready = h->cfg.reduce_grads != 0;
+  h->reduce_ready = h->cfg.reduce_grads != 0 || h->cfg.scan_shard != 0;
   if (h->graph) {  // the captured step must be re-captured with the peers
     cudaGraphExecDestroy(h->graph);
     h->graph = nullptr;
@@ -1416,6 +1431,52 @@ extern "C" int mmn_optim_reduce_grads(mmn_optim_t* h) {
   return MMN_OK;
 }
 
+extern "C" int mmn_optim_scan_grads(mmn_optim_t* h, const void* const* grads) {
+  NvtxRange range("mmn.scan_grads");
+  if (!h) return fail(MMN_E_INVALID, "null handle");
+  if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
+  if (!h->cfg.scan_shard) return fail(MMN_E_STATE, "create the handle with scan_shard = 1");
+  if (!h->reduce_ready) return fail(MMN_E_STATE, "connect the peers first");
+  DevGuard g(h->ctx.device);
+  const int W = h->cfg.world_size, R = h->cfg.rank;
+  cudaStream_t s = h->ctx.stream;
+  if (grads) {
+    // this rank's parts of the host grads in first, on the copy stream
+    HostIO io{grads, nullptr};
+    MMN_CUDA_TRY(cudaEventRecord(h->in_ev, s));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(h->h2d, h->in_ev, 0));
+    int64_t lo, hi;
+    for (size_t i = 0; i < h->slots.size(); ++i)
+      if (stepped_range(h, h->slots[i], &lo, &hi)) MMN_TRY_RC(grad_in(h, &io, (int)i, lo, hi));
+    MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->h2d));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->out_ev, 0));
+  }
+  RankFlags f{};
+  f.n = W;
+  for (int r = 0; r < W; ++r) f.flag[r] = h->rank_skip[r];
+  const bool bf = h->cfg.grad_dtype == MMN_DTYPE_BF16;
+  const size_t gsz = bf ? 2 : 4;
+  const int64_t alo = std::min<int64_t>(h->a_region4 * R, h->a_used4) * 4;
+  const int64_t ahi = std::min<int64_t>(h->a_region4 * (R + 1), h->a_used4) * 4;
+  const uint8_t* ag = static_cast<const uint8_t*>(h->ag) + (size_t)alo * gsz;
+  const uint8_t* mg = static_cast<const uint8_t*>(h->mg) + (size_t)h->m_own_begin * gsz;
+  const int64_t an = ahi - alo, mn = h->m_own_end - h->m_own_begin;
+  if (bf) {
+    launch_nonfinite_scan_ranks(nullptr, 0, reinterpret_cast<const __nv_bfloat16*>(ag), an, f,
+                                h->ctx.num_sms, s);
+    launch_nonfinite_scan_ranks(nullptr, 0, reinterpret_cast<const __nv_bfloat16*>(mg), mn, f,
+                                h->ctx.num_sms, s);
+  } else {
+    launch_nonfinite_scan_ranks(reinterpret_cast<const float*>(ag), an, nullptr, 0, f,
+                                h->ctx.num_sms, s);
+    launch_nonfinite_scan_ranks(reinterpret_cast<const float*>(mg), mn, nullptr, 0, f,
+                                h->ctx.num_sms, s);
+  }
+  MMN_CUDA_TRY(cudaGetLastError());
+  if (grads) MMN_CUDA_TRY(cudaStreamSynchronize(s));  // the host buffers may be reused
+  return MMN_OK;
+}
+
 extern "C" int mmn_optim_param_counts(mmn_optim_t* h, int64_t* total, int64_t* adamw,
                                       int64_t* muon) {
   if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
@@ -1439,11 +1500,13 @@ extern "C" int mmn_optim_kernel_launches(mmn_optim_t* h, int64_t* per_step,
                      std::min<int64_t>(h->a_region4 * R, h->a_used4);
   const int steps = h->cfg.muon.ns_steps;
   int64_t n = (adamw ? 1 : 0) + 1;  // AdamW, step tail
-  if (h->cfg.loss_scaling && !h->cfg.reduce_grads) n += 2;  // non-finite scans
+  if (h->cfg.loss_scaling && !h->cfg.reduce_grads && !h->cfg.scan_shard)
+    n += 2;  // non-finite scans
   // per chunk: momentum, norms, 3 GEMMs per iteration (or the update kernel)
   n += (int64_t)h->chunk_begin.size() * (2 + (steps >= 1 ? 3 * steps : 1));
   if (per_step) *per_step = n;
-  if (per_reduce) *per_reduce = h->cfg.reduce_grads ? 2 : 0;
+  // mmn_optim_reduce_grads, or mmn_optim_scan_grads: one launch per arena
+  if (per_reduce) *per_reduce = (h->cfg.reduce_grads || h->cfg.scan_shard) ? 2 : 0;
   return MMN_OK;
 }
 

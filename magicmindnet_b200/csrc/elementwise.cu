@@ -496,9 +496,9 @@ __device__ __forceinline__ bool nonfinite_bits(uint32_t u) {
   return (u & 0x7F800000u) == 0x7F800000u;
 }
 
-__global__ void __launch_bounds__(256) nonfinite_kernel(const float* g32, long long n32,
-                                                        const __nv_bfloat16* g16, long long n16,
-                                                        int* flag) {
+// This thread's share of a non-finite scan of g32[0, n32) and g16[0, n16).
+__device__ __forceinline__ bool scan_nonfinite(const float* g32, long long n32,
+                                               const __nv_bfloat16* g16, long long n16) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   bool bad = false;
@@ -527,7 +527,25 @@ __global__ void __launch_bounds__(256) nonfinite_kernel(const float* g32, long l
       bad |= nonfinite_bits(u);
     }
   }
+  return bad;
+}
+
+__global__ void __launch_bounds__(256) nonfinite_kernel(const float* g32, long long n32,
+                                                        const __nv_bfloat16* g16, long long n16,
+                                                        int* flag) {
+  const bool bad = scan_nonfinite(g32, n32, g16, n16);
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+
+// The scan of one rank's part, its verdict stored into every rank's flag.
+__global__ void __launch_bounds__(256) nonfinite_ranks_kernel(const float* g32, long long n32,
+                                                              const __nv_bfloat16* g16,
+                                                              long long n16, const RankFlags f) {
+  const bool bad = scan_nonfinite(g32, n32, g16, n16);
+  if (__syncthreads_or(bad) && threadIdx.x == 0) {
+    for (int r = 0; r < f.n; ++r) *(volatile int*)f.flag[r] = 1;
+    __threadfence_system();
+  }
 }
 
 // fp32: four elements per vector; every rank's vector is loaded before the
@@ -731,6 +749,15 @@ void launch_nonfinite_scan(const float* g32, long long n32, const __nv_bfloat16*
                            long long n16, int* flag, int num_sms, cudaStream_t stream) {
   const long long work = (n32 / 4 > n16 / 8 ? n32 / 4 : n16 / 8) + 1;
   nonfinite_kernel<<<grid_for(work, 256, num_sms, 8), 256, 0, stream>>>(g32, n32, g16, n16, flag);
+}
+
+void launch_nonfinite_scan_ranks(const float* g32, long long n32, const __nv_bfloat16* g16,
+                                 long long n16, const RankFlags& f, int num_sms,
+                                 cudaStream_t stream) {
+  if (f.n < 1 || f.n > kMaxRanks || (n32 <= 0 && n16 <= 0)) return;
+  const long long work = (n32 / 4 > n16 / 8 ? n32 / 4 : n16 / 8) + 1;
+  nonfinite_ranks_kernel<<<grid_for(work, 256, num_sms, 8), 256, 0, stream>>>(g32, n32, g16, n16,
+                                                                              f);
 }
 
 void launch_step_tail(const StepTail& t, cudaStream_t stream) {

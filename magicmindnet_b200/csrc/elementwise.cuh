@@ -112,6 +112,17 @@ struct GradReduceArgs {
 };
 void launch_grad_reduce(const GradReduceArgs& a, int num_sms, cudaStream_t stream);
 
+// Non-finite scan of one rank's part of the grad arenas whose verdict goes to
+// every rank: any non-finite value sets flag[0..n) (this rank's flag and its
+// peers', the latter through IPC mappings). Flags are only ever set here.
+struct RankFlags {
+  int* flag[kMaxRanks];
+  int n;
+};
+void launch_nonfinite_scan_ranks(const float* g32, long long n32, const __nv_bfloat16* g16,
+                                 long long n16, const RankFlags& f, int num_sms,
+                                 cudaStream_t stream);
+
 // End of step: advance the AdamW counter unless skipped; dynamic loss scale.
 struct StepTail {
   long long* step_counter;

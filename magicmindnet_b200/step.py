@@ -72,6 +72,7 @@ class StepConfig:
     world_size: int = 1
     use_graph: bool = True
     reduce_grads: bool = False
+    scan_shard: bool = False
 
     def c(self) -> N.OptimConfigC:
         c = N.lib().mmn_optim_config_default()
@@ -89,6 +90,7 @@ class StepConfig:
         c.world_size = self.world_size
         c.use_graph = int(self.use_graph)
         c.reduce_grads = int(self.reduce_grads)
+        c.scan_shard = int(self.scan_shard)
         return c
 
 
@@ -319,6 +321,30 @@ class OptimizerStep:
 
         dist.all_reduce(self._fence, group=group)
         N.check(N.lib().mmn_optim_reduce_grads(self._h))
+        dist.all_reduce(self._fence, group=group)
+
+    def scan_grads(self, grads=None, group=None) -> None:
+        """Sharded non-finite scan (mmn_optim_scan_grads; needs
+        StepConfig(scan_shard=True, loss_scaling=True) and connect_peers): this
+        rank scans only what it steps and sets every rank's skip flag. `grads`:
+        None when the grads are on the device, else host buffers per slot (None
+        entries skipped) whose parts this rank steps are copied in first; then
+        call step_host with None grads. Fenced on both sides with one-element
+        all-reduces, as the call requires."""
+        import torch.distributed as dist
+
+        gp = None
+        if grads is not None:
+            n = len(self.shapes)
+            if len(grads) != n:
+                raise ValueError(f"need {n} grads (one per slot)")
+            gsz = 2 if self.config.grad_dtype == "bf16" else 4
+            gp = (ctypes.c_void_p * n)()
+            for k in range(n):
+                gp[k] = _host_ptr(grads[k], int(np.prod(self.shapes[k], dtype=np.int64)), gsz,
+                                  "grad", k)
+        dist.all_reduce(self._fence, group=group)
+        N.check(N.lib().mmn_optim_scan_grads(self._h, gp))
         dist.all_reduce(self._fence, group=group)
 
     def param_counts(self):

@@ -33,7 +33,7 @@ def test_abi_version_and_defaults():
     from magicmindnet_b200 import _native as N
 
     L = N.lib()
-    assert L.mmn_abi_version() == 2
+    assert L.mmn_abi_version() == 3
     a = L.mmn_adamw_config_default()
     assert (round(a.lr, 7), round(a.beta1, 6), round(a.beta2, 6), a.eps, round(a.weight_decay, 6)) \
         == (3e-4, 0.9, 0.95, np.float32(1e-8), 0.01)

@@ -430,3 +430,117 @@ def test_sharded_checkpoint_resume_is_bit_exact(tmp_path):
         assert bad == [], (r, bad)
     for p in procs:
         assert p.exitcode == 0
+
+
+# ------------------------------------------------------------------ sharded scan
+def _scan_grads_for(model, it, bad_slot=None):
+    """Replicated bf16 grads of step `it` (seed 700 + it), with a +inf in
+    bad_slot when given."""
+    import torch
+
+    gen = torch.Generator(device="cuda").manual_seed(700 + it)
+    gs = [(torch.empty(s, device="cuda").normal_(0, 1e-3, generator=gen) * 1024.0).bfloat16()
+          for _, s, _ in model]
+    if bad_slot is not None:
+        gs[bad_slot].view(-1)[3] = float("inf")
+    return gs
+
+
+def _scan_worker(rank, world, port, q, bad_slot):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import magicmindnet_b200 as mmn
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        model = _model()
+        step = mmn.OptimizerStep(model, _reduce_cfg(mmn, True, rank=rank, world_size=world,
+                                                    scan_shard=True),
+                                 device=rank, stream=torch.cuda.current_stream(rank).cuda_stream)
+        _fill(step, model, 0)
+        step.connect_peers()
+        for it in range(3):  # step 1 has a +inf in a slot another rank steps
+            gs = _scan_grads_for(model, it, bad_slot if it == 1 else None)
+            if it < 2:
+                for k in range(len(model)):
+                    step.grad(k).copy_(gs[k])
+                step.scan_grads()
+                step.step()
+            else:  # from host memory: this rank's grads in through scan_grads
+                host = [g.cpu() for g in gs]
+                outs = [np.empty(s, np.float32) for _, s, _ in model]
+                step.scan_grads(host)
+                step.step_host([None] * len(model), outs)
+            step.exchange_fence()
+        step.sync()
+        torch.cuda.synchronize()
+        out = [step.param(k).cpu().numpy().copy() for k in range(len(model))]
+        q.put((rank, out, step.loss_scale()))
+        step.close()
+    except Exception as e:  # reported to the parent, which fails at once
+        q.put((rank, f"{type(e).__name__}: {e}", None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_nonfinite_scan_equals_single_gpu(mmn):
+    """Loss-scaled sharded step with the sharded scan (scan_shard): each rank
+    scans only what it steps and sets every rank's flag. A +inf in a slot the
+    last rank steps skips step 1 on every rank and halves every scale; the
+    three steps (the last from host memory) equal one GPU bit for bit."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    model = _model()
+    plan = mmn.shard_plan(model, world)
+    bad_slot = next(k for k, o in enumerate(plan["owner"]) if o == world - 1)
+    single = mmn.OptimizerStep(model, _reduce_cfg(mmn, True), device=0)
+    _fill(single, model, 0)
+    for it in range(3):
+        gs = _scan_grads_for(model, it, bad_slot if it == 1 else None)
+        for k in range(len(model)):
+            single.grad(k).copy_(gs[k])
+        single.step()
+    single.sync()
+    want = [single.param(k).cpu().numpy().copy() for k in range(len(model))]
+    scale = single.loss_scale()
+    single.close()
+    assert scale[1] == 1  # the single-GPU run skipped step 1 too
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_scan_worker, args=(r, world, port, q, bad_slot))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, out, sc = q.get(timeout=900)
+        got[r] = (out, sc)
+    for p in procs:
+        p.join(timeout=120)
+    for r, (out, sc) in got.items():
+        assert not isinstance(out, str), (r, out)
+        assert sc == scale, (r, sc, scale)
+        for k, (a, b) in enumerate(zip(out, want)):
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32),
+                                          err_msg=f"rank {r} slot {k}")
+    for p in procs:
+        assert p.exitcode == 0
