@@ -28,14 +28,17 @@
 // rounded to tf32 (10-bit mantissa, round-to-nearest-even) instead of bf16,
 // and the MMAs issued as kind::tf32. A 128-byte swizzle row then holds 32
 // elements, so a stage covers K = 32 and one MMA K = 8; stage byte sizes and
-// the TMEM layout are the same as in bf16.
+// the TMEM layout are the same as in bf16. MN-major tf32 operands use the
+// 128-byte swizzle with 32-byte atoms, the only layout tcgen05 reads them in.
 //
 // SPLIT = true (with F32) instantiates the fp32 mode: no rounding points at
 // all. Every stored matrix is kept as two tf32 planes, hi = tf32(v) and
 // lo = tf32(v - hi) (batch items 2b and 2b + 1 of the same buffer), and every
-// product is the three-pass hi*hi + hi*lo + lo*hi into one fp32 accumulator,
-// which carries about 21 mantissa bits instead of tf32's 11. Stages hold both
+// product is the three-pass hi*hi + hi*lo + lo*hi, which carries about 21
+// mantissa bits instead of tf32's 11: hi*hi into the main accumulator, the two
+// corrections into a second one, summed in the epilogue. Stages hold both
 // planes of each operand; the symmetric outputs are stored from registers.
+//
 // In the last iteration the Poly epilogue can apply the Muon update
 // p -= lr*sqrt(rows/cols) * X' (lib.rs:169-174) directly instead of storing X'.
 //
