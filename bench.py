@@ -41,7 +41,10 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "hybrid AdamW+Muon step params/s"
+# The benchmark's metric as the configurations name it; `value` is the params/s
+# part (whole job), ms_per_step the step time, components the AdamW GB/s and NS
+# TFLOP/s, and params_per_s_per_gpu the per-GPU rate.
+METRIC = "hybrid AdamW+Muon step ms & params/s/GPU; AdamW HBM GB/s; NS TFLOPS"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per algorithmic Newton-Schulz flop of the GEMM
@@ -528,6 +531,7 @@ def run_ours(args, rank, world, local_rank):
                                     else 0)
     line = {
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
+        "params_per_s_per_gpu": value / world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": ("f32 (NS GEMMs " + {"tf32": "tf32 x tf32", "fp32": "3 x tf32 split fp32"}.get(
