@@ -10,7 +10,10 @@
  * machine, so the reference cannot be run to produce golden outputs, and its own
  * tests pin only the GradAccumulator average (lib.rs:283-293) and the routing
  * table (lib.rs:303-320). Everything else here is pinned by known-answer tests
- * derived from the arithmetic (tests/golden/). Parity is therefore "partially
+ * derived from the arithmetic: tests/golden/known_answers.json, written by
+ * tests/golden/make_golden.py from a numpy restatement of the reference's
+ * operation order that does not use this library, and the closed forms of
+ * tests/test_oracle.py. Parity is therefore "partially
  * pinned": AdamW/momentum/update arithmetic is a literal restatement of the
  * reference's operation order; the Newton-Schulz GEMM summation order of the
  * reference (matrixmultiply 0.3.10 sgemm) is not reproduced.

@@ -1,6 +1,8 @@
 """The CPU oracle against the reference's own known answers and against
 closed forms derived from the arithmetic of crates/mmn-optim/src/lib.rs.
 No GPU needed."""
+import os
+
 import numpy as np
 import pytest
 
@@ -231,3 +233,56 @@ def test_gemm_orders_agree(oracle, order):
     b = rng.normal(0, 1, (53, 71)).astype(np.float32)
     np.testing.assert_allclose(oracle.gemm(a, b, order), a.astype(np.float64) @ b, rtol=1e-4,
                                atol=1e-4)
+
+
+# ------------------------------------------------------------------ golden vectors
+def _golden():
+    import json
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                           "known_answers.json")) as f:
+        return json.load(f)
+
+
+def _f32(hexes):
+    return np.array([int(h, 16) for h in hexes], np.uint32).view(np.float32)
+
+
+def test_oracle_matches_golden_known_answers(oracle):
+    """tests/golden/known_answers.json restates the reference's arithmetic in
+    numpy (tests/golden/make_golden.py); the C oracle must reproduce it bit
+    for bit."""
+    G = _golden()
+    a = G["adamw"]
+    for t in a["tensors"]:
+        p = _f32(t["p"]).copy()
+        m = np.zeros_like(p)
+        v = np.zeros_like(p)
+        oracle.adamw_update(p, m, v, _f32(t["g"]), lr=_f32([a["lr"]])[0],
+                            betas=(_f32([a["beta1"]])[0], _f32([a["beta2"]])[0]),
+                            eps=_f32([a["eps"]])[0], weight_decay=_f32([a["weight_decay"]])[0],
+                            t=t["t"])
+        for name, got in (("p_out", p), ("m_out", m), ("v_out", v)):
+            np.testing.assert_array_equal(got.view(np.uint32), _f32(t[name]).view(np.uint32),
+                                          err_msg=name)
+    mm = G["muon_momentum"]
+    vel = np.zeros(len(mm["g"]), np.float32)
+    u = oracle.muon_momentum(vel, _f32(mm["g"]), momentum=_f32([mm["momentum"]])[0], nesterov=True)
+    np.testing.assert_array_equal(vel.view(np.uint32), _f32(mm["vel_out"]).view(np.uint32))
+    np.testing.assert_array_equal(u.view(np.uint32), _f32(mm["u"]).view(np.uint32))
+    for e in G["muon_scale"]:
+        assert oracle.muon_scale(e["rows"], e["cols"]) == _f32([e["scale"]])[0], e
+    ident = G["ns_scaled_identity"]
+    n, s = ident["n"], _f32([ident["s"]])[0]
+    for name, variant in (("bf16", oracle.NS_REFERENCE), ("tf32", oracle.NS_TF32)):
+        out = oracle.newton_schulz5(np.eye(n, dtype=np.float32) * s, variant=variant)
+        np.testing.assert_array_equal(np.diag(out), np.full(n, _f32([ident["diag"][name]])[0]))
+    acc = G["grad_accumulator"]
+    avg = np.empty(1, np.float32)
+    total = np.array([sum(x[0] for x in acc["micro_batches"])], np.float32)
+    oracle.lib().ref_grad_average(oracle._ptr(total), oracle._ptr(avg), 1,
+                                  len(acc["micro_batches"]))
+    assert avg[0] == _f32(acc["average"])[0]
+    for kind, shapes in G["routing"].items():
+        for shp in shapes:
+            assert oracle.classify_param(tuple(shp)) == kind, shp
