@@ -157,3 +157,27 @@ def test_ns_mode_constants_agree():
     ref_h = open(os.path.join(ROOT, "oracle", "mmn_optim_ref.h")).read()
     assert dict(re.findall(r"REF_NS_(\w+) = (\d)", ref_h)) == {
         "REFERENCE": "0", "BF16": "1", "TF32": "2", "FP32": "3"}
+
+
+def test_optim_config_validation_before_device():
+    """Configuration errors are reported before any device is touched: a
+    sharded scan needs loss scaling, several ranks and no grad reduction, and
+    an unknown Newton-Schulz mode is rejected."""
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+    h = ctypes.c_void_p()
+    c = L.mmn_optim_config_default()
+    assert c.scan_shard == 0 and c.ns_mode == N.NS_REFERENCE
+    c.scan_shard = 1  # without loss scaling and with one rank
+    assert L.mmn_optim_create(ctypes.byref(c), 0, None, ctypes.byref(h)) == N.MMN_E_INVALID
+    assert b"scan_shard" in L.mmn_last_error()
+    c = L.mmn_optim_config_default()
+    c.ns_mode = 4
+    assert L.mmn_optim_create(ctypes.byref(c), 0, None, ctypes.byref(h)) == N.MMN_E_INVALID
+    # the allocation-free entry point rejects the fp32-storage modes before any
+    # pointer is used (the dummy buffers are never read)
+    buf = np.zeros(4, np.float32)
+    for mode in (N.NS_TF32, N.NS_FP32):
+        rc = L.mmn_newton_schulz5_noalloc(buf.ctypes.data, 2, 2, 5, mode, buf.ctypes.data, 0, None)
+        assert rc == N.MMN_E_UNSUPPORTED
