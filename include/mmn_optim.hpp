@@ -10,6 +10,8 @@
  *   GradAccumulator                          lib.rs:212-262
  *   cuda::is_available, require_cuda         crates/mmn-cuda/src/lib.rs:5-12,
  *                                            crates/mmn-core/src/device.rs:29-37
+ *   OptimizerStep (the whole model's step)   crates/mmn-models/src/chatbot.rs:208-227,
+ *                                            crates/mmn-train/src/lib.rs:367-378
  * Parameters and grads are host arrays (ArrayD, the role of ndarray's
  * ArrayD<f32>); the optimizer state lives on the GPU, keyed by the caller's id
  * like the reference's HashMaps. Where the reference panics (a shape that
@@ -302,6 +304,98 @@ class GradAccumulator {
   std::vector<ArrayD> grads_;
   size_t micro_batches_ = 0;
   size_t param_index_ = 0;
+};
+
+// ------------------------------------------------------------ batched step
+// The whole model's step as one device-resident operation: the trainer's call
+// that replaces the per-tensor optim_step_weight loop of a training step
+// (crates/mmn-models/src/chatbot.rs:208-227, call order :1104-1196) and the
+// optimizer construction of crates/mmn-train/src/lib.rs:367-378. Tensors are
+// registered in the reference's call order, which fixes each AdamW tensor's
+// step count.
+class OptimizerStep {
+ public:
+  struct Tensor {
+    uint64_t id;
+    std::vector<int64_t> shape;
+    int route = MMN_ROUTE_AUTO;
+  };
+
+  OptimizerStep(const std::vector<Tensor>& tensors, const mmn_optim_config& cfg, int device = 0)
+      : shapes_() {
+    check(mmn_optim_create(&cfg, device, nullptr, &h_));
+    try {
+      for (const Tensor& t : tensors) {
+        int slot = -1;
+        check(mmn_optim_add_param(h_, t.id, t.shape.data(), (int)t.shape.size(), t.route, &slot));
+        shapes_.push_back(t.shape);
+      }
+      check(mmn_optim_finalize(h_));
+    } catch (...) {
+      mmn_optim_destroy(h_);
+      throw;
+    }
+  }
+  OptimizerStep(const OptimizerStep&) = delete;
+  OptimizerStep& operator=(const OptimizerStep&) = delete;
+  ~OptimizerStep() { mmn_optim_destroy(h_); }
+
+  static mmn_optim_config default_config() { return mmn_optim_config_default(); }
+
+  size_t size() const { return shapes_.size(); }
+
+  void set_param(int slot, const ArrayD& p) {
+    expect(slot, p);
+    check(mmn_optim_set_param(h_, slot, p.data.data(), MMN_MEM_HOST));
+  }
+  ArrayD get_param(int slot) {
+    ArrayD p(shapes_.at((size_t)slot));
+    check(mmn_optim_get_param(h_, slot, p.data.data(), MMN_MEM_HOST));
+    return p;
+  }
+  // fp32 grads (config.grad_dtype == MMN_DTYPE_F32)
+  void set_grad(int slot, const ArrayD& g) {
+    expect(slot, g);
+    check(mmn_optim_set_grad(h_, slot, g.data.data(), MMN_MEM_HOST));
+  }
+
+  // One step over every registered tensor; grad_divisor is the accumulator's
+  // micro-batch count (GradAccumulator::averaged_grad, lib.rs:254-257).
+  void step(float grad_divisor = 1.0f) { check(mmn_optim_step(h_, grad_divisor)); }
+  void sync() { check(mmn_optim_sync(h_)); }
+
+  // One step from host memory: grads in, updated params out (slot order; an
+  // empty array skips that slot's copy). Returns when params hold the result.
+  void step_host(const std::vector<ArrayD>& grads, std::vector<ArrayD>& params,
+                 float grad_divisor = 1.0f) {
+    if (grads.size() != size() || params.size() != size())
+      throw Error(MMN_E_INVALID, "need one grad and one param array per slot");
+    std::vector<const void*> gp(size());
+    std::vector<float*> pp(size());
+    for (size_t k = 0; k < size(); ++k) {
+      gp[k] = grads[k].len() ? grads[k].data.data() : nullptr;
+      if (params[k].len() && params[k].shape != shapes_[k]) params[k] = ArrayD(shapes_[k]);
+      pp[k] = params[k].len() ? params[k].data.data() : nullptr;
+      if (gp[k]) expect((int)k, grads[k]);
+    }
+    check(mmn_optim_step_host(h_, gp.data(), pp.data(), grad_divisor));
+  }
+
+  uint64_t adamw_step() const {
+    uint64_t s = 0;
+    check(mmn_optim_get_adamw_step(h_, &s));
+    return s;
+  }
+
+  mmn_optim_t* handle() const { return h_; }
+
+ private:
+  void expect(int slot, const ArrayD& a) const {
+    if (slot < 0 || (size_t)slot >= shapes_.size() || a.shape != shapes_[(size_t)slot])
+      throw Error(MMN_E_SHAPE, "array shape differs from the registered tensor");
+  }
+  mmn_optim_t* h_ = nullptr;
+  std::vector<std::vector<int64_t>> shapes_;
 };
 
 }  // namespace mmn

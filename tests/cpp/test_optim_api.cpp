@@ -265,6 +265,73 @@ void gpu_tests() {
       EXPECT(r <= tol);
     }
   };
+  // The whole-model step (the trainer's call) on the Chatbot(vocab 512, 2
+  // layers, d_model 64) tensors in the reference's call order
+  // (crates/mmn-models/src/chatbot.rs:1104-1196), routed by the shape rule:
+  // AdamW tensors bit-exact with the per-call counter, Muon within 2e-2; the
+  // step from host memory equals the device-resident step bit for bit.
+  run("optimizer_step_chatbot_vs_oracle", [] {
+    std::vector<std::vector<int64_t>> shapes = {{512, 64}};
+    for (int layer = 1; layer >= 0; --layer) {
+      (void)layer;
+      for (auto s : std::vector<std::vector<int64_t>>{{64, 256}, {256, 64}, {64, 64}, {64, 64},
+                                                      {64, 64}, {64, 64}, {64}, {64}, {64}, {64}})
+        shapes.push_back(s);
+    }
+    shapes.push_back({512, 64});
+    EXPECT(shapes.size() == 22);
+    std::vector<mmn::OptimizerStep::Tensor> ts;
+    for (size_t k = 0; k < shapes.size(); ++k) ts.push_back({k, shapes[k], MMN_ROUTE_AUTO});
+    mmn_optim_config cfg = mmn::OptimizerStep::default_config();
+    cfg.adamw.lr = 1e-3f;
+    cfg.adamw.beta2 = 0.999f;
+    cfg.use_graph = 0;
+    mmn::OptimizerStep dev(ts, cfg), host(ts, cfg);
+    std::mt19937 rng(7);
+    std::vector<ArrayD> p, g;
+    for (auto& s : shapes) {
+      p.push_back(normal(rng, s, 0.02f));
+      g.push_back(normal(rng, s, 1e-3f));
+    }
+    for (size_t k = 0; k < shapes.size(); ++k) {
+      dev.set_param((int)k, p[k]);
+      host.set_param((int)k, p[k]);
+      dev.set_grad((int)k, g[k]);
+    }
+    dev.step();
+    dev.sync();
+    std::vector<ArrayD> out_host(shapes.size());
+    for (size_t k = 0; k < shapes.size(); ++k) out_host[k] = ArrayD(shapes[k]);
+    host.step_host(g, out_host);
+    int64_t t = 0;
+    const mmn::MuonConfig mc;
+    for (size_t k = 0; k < shapes.size(); ++k) {
+      const ArrayD got = dev.get_param((int)k);
+      EXPECT(std::memcmp(got.data.data(), out_host[k].data.data(), got.len() * 4) == 0);
+      std::vector<float> want = p[k].data;
+      const int64_t n = (int64_t)want.size();
+      if (mmn::HybridOptimizer::classify_param(shapes[k]) == mmn::ParamKind::Other) {
+        std::vector<float> m((size_t)n, 0.0f), v((size_t)n, 0.0f);
+        ref_adamw_step(want.data(), m.data(), v.data(), g[k].data.data(), n, cfg.adamw.lr,
+                       cfg.adamw.beta1, cfg.adamw.beta2, cfg.adamw.eps, cfg.adamw.weight_decay,
+                       ++t, 1.0f);
+        EXPECT(std::memcmp(got.data.data(), want.data(), (size_t)n * 4) == 0);
+      } else {
+        std::vector<float> vel((size_t)n, 0.0f), u((size_t)n), o((size_t)n);
+        ref_muon_momentum(vel.data(), g[k].data.data(), u.data(), n, mc.momentum, 1, 1.0f);
+        ref_newton_schulz5(u.data(), shapes[k][0], shapes[k][1], (int)mc.ns_steps, o.data(),
+                           REF_GEMM_F64, REF_NS_REFERENCE, nullptr, 0);
+        ref_muon_apply(want.data(), o.data(), shapes[k][0], shapes[k][1], mc.lr);
+        std::vector<float> du((size_t)n), dw((size_t)n);
+        for (int64_t i = 0; i < n; ++i) {
+          du[(size_t)i] = got.data[(size_t)i] - p[k].data[(size_t)i];
+          dw[(size_t)i] = want[(size_t)i] - p[k].data[(size_t)i];
+        }
+        EXPECT(rel_fro(du, dw) <= 2e-2);
+      }
+    }
+    EXPECT(dev.adamw_step() == (uint64_t)t);  // one count per AdamW tensor
+  });
   run("muon_parity_reference_mode_2e-2", [&] { muon_parity(MMN_NS_REFERENCE, REF_NS_REFERENCE, 2e-2); });
   run("muon_parity_tf32_mode_3e-3", [&] { muon_parity(MMN_NS_TF32, REF_NS_TF32, 3e-3); });
   run("muon_parity_fp32_mode_1e-4", [&] { muon_parity(MMN_NS_FP32, REF_NS_FP32, 1e-4); });
