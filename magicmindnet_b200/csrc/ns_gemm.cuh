@@ -715,7 +715,6 @@ __global__ void __launch_bounds__(320, 1)
       // accumulator columns along X' rows)
       const int lane_dim = kSwap ? args.N : args.M, col_dim = kSwap ? args.M : args.N;
       const bool row_ok = r < lane_dim;
-      const bool rows_full = rw + 32 <= lane_dim;
 #pragma unroll 1
       for (int ch = ch_lo; ch < ch_hi; ++ch) {
         const int c0 = tn * BN + ch * 32;
