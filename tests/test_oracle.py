@@ -286,3 +286,51 @@ def test_oracle_matches_golden_known_answers(oracle):
     for kind, shapes in G["routing"].items():
         for shp in shapes:
             assert oracle.classify_param(tuple(shp)) == kind, shp
+
+
+def _np_round(x, variant, oracle):
+    if variant == oracle.NS_TF32:
+        return oracle.tf32_round(x)
+    if variant == oracle.NS_FP32:
+        return np.asarray(x, np.float32)
+    return oracle.bf16_round(x)
+
+
+def _np_newton_schulz5(g, steps, variant, oracle):
+    """An independent numpy restatement of newton_schulz5 (lib.rs:83-126) with
+    fp64 products rounded once to fp32, the rounding points of each variant,
+    and the reference's sequential fp32 norm (fp64 once for the fp32 mode)."""
+    f = np.float32
+    tr = g.shape[0] > g.shape[1]
+    x = _np_round(g.T if tr else g, variant, oracle).astype(f)
+    if variant == oracle.NS_FP32:
+        s = f(np.sum(x.astype(np.float64) ** 2))
+    else:
+        s = f(0)
+        for v in x.ravel():
+            s = f(s + f(v * v))
+    x = (x / max(f(np.sqrt(s)), f(1e-7))).astype(f)
+    a, b, c = f(3.4445), f(-4.7750), f(2.0315)
+    for _ in range(steps):
+        A = _np_round((x.astype(np.float64) @ x.T.astype(np.float64)).astype(f), variant, oracle)
+        A2 = _np_round((A.astype(np.float64) @ A.astype(np.float64)).astype(f), variant, oracle)
+        B = (A * b + A2 * c).astype(f)
+        if variant == oracle.NS_BF16:
+            B = oracle.bf16_round(B)
+        BX = (B.astype(np.float64) @ x.astype(np.float64)).astype(f)
+        x = _np_round((x * a + BX).astype(f), variant, oracle)
+    return (x.T if tr else x).astype(f)
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+def test_oracle_ns_matches_independent_numpy_restatement(oracle, variant):
+    """The oracle's C recipe (fp64 GEMM order) against the numpy restatement,
+    five iterations, both orientations: bit for bit. With K <= 20 the fp64 sums
+    of fp32 products are exact in both, so every rounding point sees the same
+    value."""
+    rng = np.random.default_rng(40 + variant)
+    for shape in ((12, 20), (20, 12), (16, 16)):
+        g = rng.normal(0, 1e-2, shape).astype(np.float32)
+        got = oracle.newton_schulz5(g, 5, order=oracle.GEMM_F64, variant=variant)
+        want = _np_newton_schulz5(g, 5, variant, oracle)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32), err_msg=str(shape))
