@@ -67,10 +67,10 @@ def _run_chatbot(mmn, oracle, routing, id_scheme, batched, use_graph=True):
     order = [n for n, _ in named]
     p_gpu = {n: v.copy() for n, v in named}
     p_ref = {n: v.copy() for n, v in named}
-    north_star = routing == "north_star"
+    tagged = routing == "tagged"
 
     def route(name, shape):
-        if north_star and (name in ("embed", "lm_head") or len(shape) == 1):
+        if tagged and (name in ("embed", "lm_head") or len(shape) == 1):
             return "adamw"
         return "auto"
 
@@ -120,13 +120,13 @@ def _run_chatbot(mmn, oracle, routing, id_scheme, batched, use_graph=True):
     return worst
 
 
-@pytest.mark.parametrize("routing", ["reference", "north_star"])
+@pytest.mark.parametrize("routing", ["reference", "tagged"])
 @pytest.mark.parametrize("id_scheme", ["stable", "train"])
 def test_chatbot_hybrid_per_call(mmn, oracle, routing, id_scheme):
     _run_chatbot(mmn, oracle, routing, id_scheme, batched=False)
 
 
-@pytest.mark.parametrize("routing", ["reference", "north_star"])
+@pytest.mark.parametrize("routing", ["reference", "tagged"])
 @pytest.mark.parametrize("id_scheme", ["stable", "train"])
 @pytest.mark.parametrize("use_graph", [True, False])
 def test_chatbot_hybrid_batched(mmn, oracle, routing, id_scheme, use_graph):
