@@ -1,7 +1,7 @@
 // The reference's own unit tests of crates/mmn-optim/src/lib.rs:264-382,
 // restated against the C++ mirror of its API (include/mmn_optim.hpp), plus
-// parity checks of the same calls against the CPU oracle (oracle/, linked as
-// the checker only).
+// parity checks of the same calls against the CPU oracle (oracle/, which only
+// this test program links).
 //
 // Usage: test_optim_api [--cpu-only]
 //   --cpu-only runs the tests that need no GPU (routing table, accumulator,
