@@ -44,8 +44,9 @@ def init_linear(rng, out_dim, in_dim):
 
 
 def chatbot_params(rng, vocab=512, n_layer=2, d=64):
-    """Config-1 parameter values in optimizer call order, with the reference's
-    init distributions (Linear U(-s/2,s/2), Embedding U(-1,1), LN gamma=1/beta=0)."""
+    """Chatbot(vocab 512, 2 layers, d_model 64) parameter values in optimizer
+    call order, with the reference's init distributions (Linear U(-s/2,s/2),
+    Embedding U(-1,1), LN gamma=1/beta=0)."""
     from magicmindnet_b200.step import chatbot_param_order
 
     out = []

@@ -92,7 +92,7 @@ def test_step_config_follows_trainer_construction():
         assert not mmn.step_config_for(mmn.TrainConfig(optimizer=opt)).use_hybrid
 
 
-def test_chatbot_param_order_config1():
+def test_chatbot_param_order_vocab512_layers2_d64():
     """22 tensors / 164,352 params; 14 Muon matrices (163,840) under the
     reference rule, in the call order of crates/mmn-models/src/chatbot.rs."""
     import magicmindnet_b200 as mmn

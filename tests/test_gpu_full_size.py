@@ -64,7 +64,7 @@ def test_adamw_arena_2p28_sampled_bitexact(mmn, oracle):
     step.close()
 
 
-CONFIG3 = [(4096, 4096)] * 64 + [(4096, 14336)] * 32
+NS_BATCH_SHAPES = [(4096, 4096)] * 64 + [(4096, 14336)] * 32
 
 
 def _ns_handle(mmn, shapes, seed_of):
@@ -81,21 +81,21 @@ def _ns_handle(mmn, shapes, seed_of):
     return step
 
 
-def test_newton_schulz_config3_deterministic_and_batch_independent(mmn):
+def test_newton_schulz_4096_batch_deterministic_and_batch_independent(mmn):
     import torch
 
-    a = _ns_handle(mmn, CONFIG3, lambda k: 1000 + k)
+    a = _ns_handle(mmn, NS_BATCH_SHAPES, lambda k: 1000 + k)
     a.step()
     a.sync()
-    b = _ns_handle(mmn, CONFIG3, lambda k: 1000 + k)
+    b = _ns_handle(mmn, NS_BATCH_SHAPES, lambda k: 1000 + k)
     b.step()
     b.sync()
-    for k in range(len(CONFIG3)):
+    for k in range(len(NS_BATCH_SHAPES)):
         assert torch.equal(a.param(k), b.param(k)), k
     b.close()
     # the same matrices in other batches (a chunk of their own, other neighbours)
     pick = [0, 37, 63, 64, 80, 95]
-    c = _ns_handle(mmn, [CONFIG3[k] for k in pick], lambda j: 1000 + pick[j])
+    c = _ns_handle(mmn, [NS_BATCH_SHAPES[k] for k in pick], lambda j: 1000 + pick[j])
     c.step()
     c.sync()
     for j, k in enumerate(pick):

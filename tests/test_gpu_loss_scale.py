@@ -1,5 +1,5 @@
 """bf16 grads with fp32 master params, dynamic loss scaling, non-finite skip
-and bf16 parameter copies (the 8B configuration's step) against the oracle's
+and bf16 parameter copies (the step of the 5.36e9-parameter GQA model) against the oracle's
 definition of that behaviour (oracle.LossScaleState)."""
 import numpy as np
 import pytest

@@ -1,5 +1,5 @@
 """Muon::step_matrix, HybridOptimizer::step and the batched whole-model step on
-the GPU against the oracle, on the config-1 Chatbot (vocab 512, 2 layers,
+the GPU against the oracle, on the Chatbot (vocab 512, 2 layers,
 d_model 64) with grads ~ N(0, 1e-3) for three consecutive steps.
 
 Tolerances: AdamW tensors bit-exact; Muon velocity bit-exact; Muon parameter

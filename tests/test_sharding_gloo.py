@@ -145,7 +145,8 @@ def test_two_rank_sharded_step_equals_unsharded(oracle):
 
 
 def test_plan_balances_the_8b_shapes_over_8_ranks():
-    """config 5 shapes: each of 8 ranks gets the same Newton-Schulz work."""
+    """The 5.36e9-parameter GQA shapes (d_model 4096, 32 layers, k/v 1024, FFN
+    14336): each of 8 ranks gets the same Newton-Schulz work."""
     import bench
     from magicmindnet_b200.step import shard_plan
 
