@@ -180,9 +180,13 @@ class OptimizerStep:
         ptr = self._ptrs(slot)[2]
         return None if not ptr else _view(ptr, self.shapes[slot], "bf16", self.device)
 
+    def _numel(self, slot: int) -> int:
+        return int(np.prod(self.shapes[slot], dtype=np.int64))
+
     def set_param(self, slot: int, values: np.ndarray) -> None:
         v = np.ascontiguousarray(values, np.float32)
-        N.check(N.lib().mmn_optim_set_param(self._h, slot, v.ctypes.data, N.MEM_HOST))
+        N.check(N.lib().mmn_optim_set_param(
+            self._h, slot, _host_ptr(v, self._numel(slot), 4, "param", slot), N.MEM_HOST))
 
     def get_param(self, slot: int) -> np.ndarray:
         out = np.empty(self.shapes[slot], np.float32)
@@ -190,13 +194,17 @@ class OptimizerStep:
         return out
 
     def set_grad(self, slot: int, values: np.ndarray) -> None:
+        """fp32 grads, or with grad_dtype "bf16" their 16-bit patterns (uint16)."""
         v = np.ascontiguousarray(values)
-        N.check(N.lib().mmn_optim_set_grad(self._h, slot, v.ctypes.data, N.MEM_HOST))
+        gsz = 2 if self.config.grad_dtype == "bf16" else 4
+        N.check(N.lib().mmn_optim_set_grad(
+            self._h, slot, _host_ptr(v, self._numel(slot), gsz, "grad", slot), N.MEM_HOST))
 
     def set_state(self, slot: int, which: str, values: np.ndarray) -> None:
         v = np.ascontiguousarray(values, np.float32)
         N.check(N.lib().mmn_optim_set_state(self._h, slot, {"m": 0, "v": 1, "velocity": 2}[which],
-                                            v.ctypes.data, N.MEM_HOST))
+                                            _host_ptr(v, self._numel(slot), 4, which, slot),
+                                            N.MEM_HOST))
 
     def get_state(self, slot: int, which: str) -> np.ndarray:
         out = np.empty(self.shapes[slot], np.float32)

@@ -181,3 +181,29 @@ def test_optim_config_validation_before_device():
     for mode in (N.NS_TF32, N.NS_FP32):
         rc = L.mmn_newton_schulz5_noalloc(buf.ctypes.data, 2, 2, 5, mode, buf.ctypes.data, 0, None)
         assert rc == N.MMN_E_UNSUPPORTED
+
+
+def test_host_buffers_checked_before_the_library_reads_them():
+    """Host setters hand the library a pointer only for a contiguous buffer of
+    exactly the slot's element count and element size, so a short or wrongly
+    typed array cannot be read past its end."""
+    import torch
+
+    from magicmindnet_b200.step import _host_ptr
+
+    a = np.zeros(12, np.float32)
+    assert _host_ptr(a, 12, 4, "param", 0) == a.ctypes.data
+    assert _host_ptr(None, 12, 4, "grad", 0) is None
+    for bad, n, isz in ((a[:11], 12, 4), (a, 12, 2), (a[::2], 6, 4),
+                        (np.zeros(12, np.uint16), 12, 4)):
+        with pytest.raises(ValueError):
+            _host_ptr(bad, n, isz, "grad", 3)
+    ro = np.zeros(12, np.float32)
+    ro.flags.writeable = False
+    assert _host_ptr(ro, 12, 4, "grad", 0) == ro.ctypes.data
+    with pytest.raises(ValueError):
+        _host_ptr(ro, 12, 4, "param", 0, writable=True)
+    t = torch.zeros(12, dtype=torch.bfloat16)
+    assert _host_ptr(t, 12, 2, "grad", 0) == t.data_ptr()
+    with pytest.raises(ValueError):
+        _host_ptr(torch.zeros(4, 3).t(), 12, 4, "grad", 0)
