@@ -269,7 +269,9 @@ int mmn_optim_destroy(mmn_optim_t *h);
 int mmn_optim_add_param(mmn_optim_t *h, uint64_t id, const int64_t *shape, int ndim, int route,
                         int *slot);
 
-/* Freeze the layout and allocate every device buffer. */
+/* Freeze the layout and allocate every device buffer. After a failed finalize
+ * (e.g. MMN_E_OOM) the handle only accepts mmn_optim_destroy: further calls
+ * return MMN_E_STATE. */
 int mmn_optim_finalize(mmn_optim_t *h);
 
 /* Device pointers of a slot's fp32 param, its grad (grad_dtype) and its bf16
@@ -292,7 +294,10 @@ int mmn_optim_set_adamw_step(mmn_optim_t *h, uint64_t step);
 int mmn_optim_get_adamw_step(mmn_optim_t *h, uint64_t *step);
 
 /* Enqueue one optimizer step over every slot this rank owns. grad_divisor is
- * GradAccumulator's micro-batch count (1 = none). Asynchronous. */
+ * GradAccumulator's micro-batch count (1 = none). Asynchronous. A handle made
+ * with reduce_grads (scan_shard) returns MMN_E_STATE unless
+ * mmn_optim_reduce_grads (mmn_optim_scan_grads) ran since its last step; the
+ * same holds for mmn_optim_step_host. */
 int mmn_optim_step(mmn_optim_t *h, float grad_divisor);
 
 /* One step from host memory, the batched form of the reference's

@@ -143,7 +143,8 @@ extern "C" int mmn_optim_plan(const int64_t* shapes, const int* ndims, const int
     ts[i].numel = numel;
     ts[i].route = route;
     if (route == MMN_ROUTE_MUON) {
-      if (ndims[i] != 2 || sp[0] < 1 || sp[1] < 1) return fail(MMN_E_SHAPE, "Muon tensors must be 2-D");
+      if (ndims[i] != 2 || sp[0] < 1 || sp[1] < 1 || sp[0] > (1 << 30) || sp[1] > (1 << 30))
+        return fail(MMN_E_SHAPE, "Muon tensors must be 2-D");
       ts[i].rows = (int)sp[0];
       ts[i].cols = (int)sp[1];
     }
@@ -165,6 +166,10 @@ struct mmn_optim {
   mmn_optim_config cfg;
   BiasTable bc;
   bool finalized = false;
+  bool finalize_failed = false;  // a failed finalize leaves a half-built layout
+  // reduce_grads / scan_shard handles: the grads of the coming step went
+  // through mmn_optim_reduce_grads / mmn_optim_scan_grads
+  bool grads_ready = false;
 
   struct Slot {
     uint64_t id = 0;
@@ -392,9 +397,19 @@ extern "C" int mmn_optim_add_param(mmn_optim_t* h, uint64_t id, const int64_t* s
   return MMN_OK;
 }
 
+static int finalize_layout(mmn_optim_t* h);
+
 extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
   if (!h) return fail(MMN_E_INVALID, "null handle");
   if (h->finalized) return MMN_OK;
+  if (h->finalize_failed)
+    return fail(MMN_E_STATE, "an earlier finalize failed: destroy the handle and start again");
+  const int rc = finalize_layout(h);
+  if (rc != MMN_OK) h->finalize_failed = true;
+  return rc;
+}
+
+static int finalize_layout(mmn_optim_t* h) {
   DevGuard g(h->ctx.device);
   const int W = h->cfg.world_size, R = h->cfg.rank;
   const int steps = h->cfg.muon.ns_steps;
@@ -762,6 +777,7 @@ static int state_ptr(mmn_optim_t* h, int slot, int which, float** p) {
 extern "C" int mmn_optim_set_state(mmn_optim_t* h, int slot, int which, const float* src, int mem) {
   int rc = check_slot(h, slot);
   if (rc != MMN_OK) return rc;
+  if (!src) return fail(MMN_E_INVALID, "null src");
   float* p = nullptr;
   if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
   DevGuard g(h->ctx.device);
@@ -773,6 +789,7 @@ extern "C" int mmn_optim_set_state(mmn_optim_t* h, int slot, int which, const fl
 extern "C" int mmn_optim_get_state(mmn_optim_t* h, int slot, int which, float* dst, int mem) {
   int rc = check_slot(h, slot);
   if (rc != MMN_OK) return rc;
+  if (!dst) return fail(MMN_E_INVALID, "null dst");
   float* p = nullptr;
   if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
   DevGuard g(h->ctx.device);
@@ -1123,10 +1140,24 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   return MMN_OK;
 }
 
+// reduce_grads and scan_shard handles step only grads that went through
+// mmn_optim_reduce_grads / mmn_optim_scan_grads since the last step: without
+// it the step would use this rank's unreduced grads, or no rank's non-finite
+// verdict.
+static int take_grads(mmn_optim_t* h) {
+  if (!h->cfg.reduce_grads && !h->cfg.scan_shard) return MMN_OK;
+  if (!h->grads_ready)
+    return fail(MMN_E_STATE, h->cfg.reduce_grads ? "call mmn_optim_reduce_grads before each step"
+                                                 : "call mmn_optim_scan_grads before each step");
+  h->grads_ready = false;
+  return MMN_OK;
+}
+
 extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
   if (!h) return fail(MMN_E_INVALID, "null handle");
   if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
   if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
+  MMN_TRY_RC(take_grads(h));
   DevGuard g(h->ctx.device);
   // The step runs on the handle's own work stream, ordered after everything
   // already queued on the caller's stream and before anything queued there
@@ -1178,6 +1209,7 @@ extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
         return fail(MMN_E_STATE,
                     "with scan_shard the grads go in through mmn_optim_scan_grads, before "
                     "the step: pass null grads here");
+  MMN_TRY_RC(take_grads(h));
   DevGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
@@ -1428,6 +1460,7 @@ extern "C" int mmn_optim_reduce_grads(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaGetLastError());
   MMN_CUDA_TRY(cudaEventRecord(h->out_ev, h->work));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->ctx.stream, h->out_ev, 0));
+  h->grads_ready = true;
   return MMN_OK;
 }
 
@@ -1474,6 +1507,7 @@ extern "C" int mmn_optim_scan_grads(mmn_optim_t* h, const void* const* grads) {
   }
   MMN_CUDA_TRY(cudaGetLastError());
   if (grads) MMN_CUDA_TRY(cudaStreamSynchronize(s));  // the host buffers may be reused
+  h->grads_ready = true;
   return MMN_OK;
 }
 

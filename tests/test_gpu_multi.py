@@ -544,3 +544,35 @@ def test_sharded_nonfinite_scan_equals_single_gpu(mmn):
                                           err_msg=f"rank {r} slot {k}")
     for p in procs:
         assert p.exitcode == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("handoff", ["reduce_grads", "scan_shard"])
+def test_step_needs_the_grad_handoff_first(mmn, handoff):
+    """A reduce_grads (scan_shard) handle refuses a step whose grads did not
+    go through reduce_grads (scan_grads) since the last step, before anything
+    is enqueued: otherwise it would step this rank's unreduced grads, or
+    without any rank's non-finite verdict. One GPU: a rank of two whose peers
+    are never connected, so the hand-off itself is refused too."""
+    model = [(0, (64, 64), "muon"), (1, (64,), "adamw")]
+    cfg = _reduce_cfg(mmn, True, rank=0, world_size=2, **{handoff: True})
+    step = mmn.OptimizerStep(model, cfg, device=0)
+    try:
+        calls = [lambda: step.step()]
+        if handoff == "scan_shard":  # (a reduce_grads handle takes no host-memory step)
+            calls.append(lambda: step.step_host([None, None], [None, None]))
+        for call in calls:
+            with pytest.raises(mmn.MmnError) as e:
+                call()
+            assert e.value.code == -5  # MMN_E_STATE
+            assert ("reduce_grads" if handoff == "reduce_grads" else "scan_grads") in str(e.value)
+        from magicmindnet_b200 import _native as N
+
+        with pytest.raises(mmn.MmnError, match="connect the peers first"):
+            if handoff == "reduce_grads":
+                N.check(N.lib().mmn_optim_reduce_grads(step._h))
+            else:
+                N.check(N.lib().mmn_optim_scan_grads(step._h, None))
+        step.sync()
+    finally:
+        step.close()
