@@ -156,7 +156,9 @@ int mmn_muon_step_matrix(mmn_muon_t *h, uint64_t id, float *param, const float *
                          const int64_t *shape, int ndim, float grad_divisor, int mem);
 
 /* Create the zero velocity of an id without stepping it (lib.rs:150-153 does
- * this lazily on the first step), so that state can be imported first. */
+ * this lazily on the first step), so that state can be imported first. An id
+ * already known with the same shape is left as it is; another shape returns
+ * MMN_E_SHAPE. */
 int mmn_muon_register(mmn_muon_t *h, uint64_t id, const int64_t *shape, int ndim);
 
 /* Velocity state of an id (rows*cols floats). */

@@ -132,6 +132,11 @@ int64_t shape_numel(const int64_t* shape, int ndim, int* err) {
       *err = fail(MMN_E_INVALID, "negative dimension");
       return 0;
     }
+    // elements stay below 2^62 so byte counts of 4-byte elements fit int64
+    if (shape[i] > 0 && n > (int64_t(1) << 62) / shape[i]) {
+      *err = fail(MMN_E_SHAPE, "tensor too large");
+      return 0;
+    }
     n *= shape[i];
   }
   return n;

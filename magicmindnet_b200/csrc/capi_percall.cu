@@ -74,10 +74,15 @@ static int adamw_state(mmn_adamw* h, uint64_t id, const int64_t* shape, int ndim
   st.shape.assign(shape, shape + ndim);
   const size_t bytes = (size_t)((numel + 3) / 4) * 16;
   if (bytes) {
-    MMN_CUDA_TRY(cudaMalloc(&st.m, bytes));
-    MMN_CUDA_TRY(cudaMalloc(&st.v, bytes));
-    MMN_CUDA_TRY(cudaMemsetAsync(st.m, 0, bytes, h->ctx.stream));
-    MMN_CUDA_TRY(cudaMemsetAsync(st.v, 0, bytes, h->ctx.stream));
+    cudaError_t e = cudaMalloc(&st.m, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&st.v, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(st.m, 0, bytes, h->ctx.stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(st.v, 0, bytes, h->ctx.stream);
+    if (e != cudaSuccess) {
+      if (st.m) cudaFree(st.m);
+      if (st.v) cudaFree(st.v);
+      return cuda_fail(e, "AdamW state allocation");
+    }
   }
   *out = &(h->state[id] = st);
   return MMN_OK;
@@ -123,6 +128,7 @@ extern "C" int mmn_adamw_step_param(mmn_adamw_t* h, uint64_t id, float* param, c
                                     const int64_t* shape, int ndim, float grad_divisor, int mem) {
   if (!h || !param || !grad) return fail(MMN_E_INVALID, "null handle, param or grad");
   if (mem != MMN_MEM_HOST && mem != MMN_MEM_DEVICE) return fail(MMN_E_INVALID, "bad mem kind");
+  if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
   int rc;
   const int64_t numel = shape_numel(shape, ndim, &rc);
   if (rc != MMN_OK) return rc;
@@ -359,6 +365,7 @@ extern "C" int mmn_muon_step_matrix(mmn_muon_t* h, uint64_t id, float* param, co
     return fail(MMN_E_SHAPE, "Muon::step_matrix needs a 2-D param (the reference panics otherwise)");
   if (shape[0] < 1 || shape[1] < 1 || shape[0] > (1 << 30) || shape[1] > (1 << 30))
     return fail(MMN_E_SHAPE, "matrix dimensions out of range");
+  if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
   const int rows = (int)shape[0], cols = (int)shape[1];
   const int64_t numel = (int64_t)rows * cols;
   DeviceGuard g(h->ctx.device);
@@ -369,7 +376,11 @@ extern "C" int mmn_muon_step_matrix(mmn_muon_t* h, uint64_t id, float* param, co
     v.rows = rows;
     v.cols = cols;
     MMN_CUDA_TRY(cudaMalloc(&v.vel, (size_t)numel * 4));
-    MMN_CUDA_TRY(cudaMemsetAsync(v.vel, 0, (size_t)numel * 4, s));
+    const cudaError_t e = cudaMemsetAsync(v.vel, 0, (size_t)numel * 4, s);
+    if (e != cudaSuccess) {
+      cudaFree(v.vel);
+      return cuda_fail(e, "cudaMemsetAsync");
+    }
     it = h->vel.emplace(id, v).first;
   } else if (it->second.rows != rows || it->second.cols != cols) {
     return fail(MMN_E_SHAPE, "grad shape differs from the velocity registered for this id");
@@ -424,14 +435,25 @@ extern "C" int mmn_muon_import_velocity(mmn_muon_t* h, uint64_t id, const float*
 // Declares a velocity for an id without stepping (so it can be imported).
 extern "C" int mmn_muon_register(mmn_muon_t* h, uint64_t id, const int64_t* shape, int ndim) {
   if (!h || ndim != 2 || !shape) return fail(MMN_E_INVALID, "2-D shape required");
-  if (h->vel.count(id)) return MMN_OK;
+  if (shape[0] < 1 || shape[1] < 1 || shape[0] > (1 << 30) || shape[1] > (1 << 30))
+    return fail(MMN_E_SHAPE, "matrix dimensions out of range");
+  auto it = h->vel.find(id);
+  if (it != h->vel.end()) {
+    if (it->second.rows != shape[0] || it->second.cols != shape[1])
+      return fail(MMN_E_SHAPE, "shape differs from the velocity registered for this id");
+    return MMN_OK;
+  }
   DeviceGuard g(h->ctx.device);
   mmn_muon::Vel v;
   v.rows = (int)shape[0];
   v.cols = (int)shape[1];
   const size_t bytes = (size_t)v.rows * v.cols * 4;
   MMN_CUDA_TRY(cudaMalloc(&v.vel, bytes));
-  MMN_CUDA_TRY(cudaMemset(v.vel, 0, bytes));
+  const cudaError_t e = cudaMemset(v.vel, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(v.vel);
+    return cuda_fail(e, "cudaMemset");
+  }
   h->vel.emplace(id, v);
   return MMN_OK;
 }
@@ -453,6 +475,8 @@ extern "C" int mmn_newton_schulz5(const float* g, const int64_t* shape, int ndim
     rows = cols = side;
   }
   if (rows < 1 || cols < 1) return fail(MMN_E_SHAPE, "empty matrix");
+  if (rows > (1 << 30) || cols > (1 << 30) || rows * cols < len)
+    return fail(MMN_E_SHAPE, "matrix dimensions out of range");
   mmn_muon_config c = mmn_muon_config_default();
   c.ns_steps = steps;
   mmn_muon_t* h = nullptr;
