@@ -72,8 +72,13 @@ def read_safetensors(path: str):
         if dt is None:
             raise ValueError(f"{name}: unsupported dtype {e['dtype']}")
         b, end = e["data_offsets"]
-        a = np.frombuffer(data, dtype=np.dtype(dt).newbyteorder("<"), count=(end - b) //
-                          np.dtype(dt).itemsize, offset=base + b)
+        isz = np.dtype(dt).itemsize
+        numel = int(np.prod(e["shape"], dtype=np.int64))
+        if not (0 <= b <= end <= len(data) - base) or end - b != numel * isz:
+            raise ValueError(f"{path}: {name}: data_offsets {[b, end]} do not hold shape "
+                             f"{e['shape']} of {e['dtype']} inside the file")
+        a = np.frombuffer(data, dtype=np.dtype(dt).newbyteorder("<"), count=numel,
+                          offset=base + b)
         out[name] = a.astype(dt).reshape(e["shape"])
     return out, meta
 

@@ -89,7 +89,7 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
     return fail(MMN_E_INVALID, "unknown ns_mode");
   if (rows < 1 || cols < 1) return fail(MMN_E_SHAPE, "empty matrix");
   const int64_t n = rows < cols ? rows : cols, m = rows < cols ? cols : rows;
-  if (n > kNoAllocMaxSide || rows * cols > kNoAllocMaxElems)
+  if (n > kNoAllocMaxSide || m > kNoAllocMaxElems / n)  // (rows * cols could overflow)
     return fail(MMN_E_UNSUPPORTED,
                 "matrix exceeds the fixed scratch of mmn_newton_schulz5_noalloc: need "
                 "min(rows, cols) <= 1024 and rows * cols <= 1048576 (use mmn_newton_schulz5)");

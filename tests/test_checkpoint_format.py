@@ -43,3 +43,21 @@ def test_reader_rejects_truncated_files(tmp_path):
     p.write_bytes(b"abc")
     with pytest.raises(ValueError):
         C.read_safetensors(str(p))
+
+
+def test_reader_rejects_offsets_that_do_not_hold_the_shape(tmp_path):
+    """A tensor whose data_offsets reach past the file, run backwards or span
+    another byte count than its shape needs is refused by name."""
+    p = tmp_path / "off.safetensors"
+    C.write_safetensors(str(p), {"x.m": np.ones(4, np.float32)}, {"format": C.FORMAT})
+    raw = p.read_bytes()
+    (n,) = struct.unpack("<Q", raw[:8])
+    header = json.loads(raw[8:8 + n])
+    for offsets, shape in (([0, 32], [8]), ([8, 0], [4]), ([0, 12], [4]), ([-4, 12], [4])):
+        h = dict(header)
+        h["x.m"] = {"dtype": "F32", "shape": shape, "data_offsets": offsets}
+        hb = json.dumps(h).encode()
+        hb += b" " * ((8 - len(hb) % 8) % 8)
+        p.write_bytes(struct.pack("<Q", len(hb)) + hb + raw[8 + n:])
+        with pytest.raises(ValueError, match="x.m"):
+            C.read_safetensors(str(p))
