@@ -142,6 +142,22 @@ int64_t shape_numel(const int64_t* shape, int ndim, int* err) {
   return n;
 }
 
+int check_device_ptr(const void* p, int device, const char* what) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MMN_E_INVALID, std::string(what) + ": not a CUDA pointer");
+  }
+  if (at.type == cudaMemoryTypeManaged) return MMN_OK;
+  if (at.type != cudaMemoryTypeDevice)
+    return fail(MMN_E_INVALID, std::string(what) + ": host memory where device memory is needed");
+  if (at.device != device)
+    return fail(MMN_E_INVALID, std::string(what) + ": memory of device " +
+                                   std::to_string(at.device) + ", handle on device " +
+                                   std::to_string(device));
+  return MMN_OK;
+}
+
 }  // namespace mmn
 
 extern "C" {

@@ -58,6 +58,11 @@ struct BiasTable {
 
 int64_t shape_numel(const int64_t* shape, int ndim, int* err);
 
+// MMN_OK when `p` is device (or managed) memory of `device`, so that kernels
+// launched there may read it; else MMN_E_INVALID naming `what`. Memory of
+// another GPU is refused: kernels here never read a peer's memory.
+int check_device_ptr(const void* p, int device, const char* what);
+
 // fp32 -> tf32 value (10 leading mantissa bits), to nearest with ties to even
 // on the 13 discarded bits; Inf and NaN pass through. The host form of the
 // TF32 mode's rounding point.

@@ -133,6 +133,10 @@ extern "C" int mmn_adamw_step_param(mmn_adamw_t* h, uint64_t id, float* param, c
   const int64_t numel = shape_numel(shape, ndim, &rc);
   if (rc != MMN_OK) return rc;
   DeviceGuard g(h->ctx.device);
+  if (mem == MMN_MEM_DEVICE && numel > 0) {
+    if ((rc = check_device_ptr(param, h->ctx.device, "param")) != MMN_OK) return rc;
+    if ((rc = check_device_ptr(grad, h->ctx.device, "grad")) != MMN_OK) return rc;
+  }
   mmn_adamw::State* st = nullptr;
   if ((rc = adamw_state(h, id, shape, ndim, numel, &st)) != MMN_OK) return rc;
   h->step += 1;  // lib.rs:42, on every call
@@ -369,6 +373,11 @@ extern "C" int mmn_muon_step_matrix(mmn_muon_t* h, uint64_t id, float* param, co
   const int rows = (int)shape[0], cols = (int)shape[1];
   const int64_t numel = (int64_t)rows * cols;
   DeviceGuard g(h->ctx.device);
+  if (mem == MMN_MEM_DEVICE) {
+    int rc0;
+    if ((rc0 = check_device_ptr(param, h->ctx.device, "param")) != MMN_OK) return rc0;
+    if ((rc0 = check_device_ptr(grad, h->ctx.device, "grad")) != MMN_OK) return rc0;
+  }
   cudaStream_t s = h->ctx.stream;
   auto it = h->vel.find(id);
   if (it == h->vel.end()) {

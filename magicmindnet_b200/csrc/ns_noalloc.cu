@@ -112,6 +112,8 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
   DeviceSlot slot;
   int rc = device_setup(device, &slot);
   if (rc != MMN_OK) return rc;
+  if ((rc = check_device_ptr(g, device, "g")) != MMN_OK) return rc;
+  if ((rc = check_device_ptr(out, device, "out")) != MMN_OK) return rc;
 
   // Scratch layout: [Newton-Schulz class][status][partials][descriptor].
   const int ni = (int)n, mi = (int)m, ri = (int)rows, ci = (int)cols;

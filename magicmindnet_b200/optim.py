@@ -28,8 +28,9 @@ def _torch():
         return None
 
 
-def _mem_ptr(x, writable: bool):
-    """(pointer, mem kind, shape) of a float32 numpy array or torch tensor."""
+def _mem_ptr(x, writable: bool, device: int | None = None):
+    """(pointer, mem kind, shape) of a float32 numpy array or torch tensor; a
+    CUDA tensor must live on `device` (the handle's GPU) when one is given."""
     torch = _torch()
     if torch is not None and isinstance(x, torch.Tensor):
         if x.dtype != torch.float32:
@@ -37,6 +38,8 @@ def _mem_ptr(x, writable: bool):
         if not x.is_contiguous():
             raise ValueError("tensor must be contiguous")
         if x.is_cuda:
+            if device is not None and x.device.index != device:
+                raise ValueError(f"tensor on {x.device}, optimizer on cuda:{device}")
             return ctypes.c_void_p(x.data_ptr()), N.MEM_DEVICE, tuple(x.shape)
         x = x.numpy()
     if not isinstance(x, np.ndarray) or x.dtype != np.float32:
@@ -112,6 +115,7 @@ class AdamW:
     def __init__(self, config: AdamWConfig | None = None, device: int = 0, stream=None,
                  _handle=None):
         self.config = config or AdamWConfig()
+        self.device = device
         self._owned = _handle is None
         if _handle is None:
             h = ctypes.c_void_p()
@@ -122,8 +126,8 @@ class AdamW:
         self._h = _handle
 
     def step_param(self, id: int, param, grad, grad_divisor: float = 1.0) -> None:
-        pp, mem, shape = _mem_ptr(param, True)
-        gp, gmem, gshape = _mem_ptr(grad, False)
+        pp, mem, shape = _mem_ptr(param, True, self.device)
+        gp, gmem, gshape = _mem_ptr(grad, False, self.device)
         if gmem != mem or gshape != shape:
             raise N.ShapeError(N.MMN_E_SHAPE, "param and grad must match in shape and memory")
         N.check(N.lib().mmn_adamw_step_param(self._h, id, pp, gp, N.shape_array(shape),
@@ -169,6 +173,7 @@ class Muon:
                  device: int = 0, stream=None, _handle=None):
         self.config = config or MuonConfig()
         self.ns_mode = ns_mode
+        self.device = device
         self._owned = _handle is None
         if _handle is None:
             h = ctypes.c_void_p()
@@ -179,8 +184,8 @@ class Muon:
         self._h = _handle
 
     def step_matrix(self, id: int, param, grad, grad_divisor: float = 1.0) -> None:
-        pp, mem, shape = _mem_ptr(param, True)
-        gp, gmem, gshape = _mem_ptr(grad, False)
+        pp, mem, shape = _mem_ptr(param, True, self.device)
+        gp, gmem, gshape = _mem_ptr(grad, False, self.device)
         if gmem != mem or gshape != shape:
             raise N.ShapeError(N.MMN_E_SHAPE, "param and grad must match in shape and memory")
         N.check(N.lib().mmn_muon_step_matrix(self._h, id, pp, gp, N.shape_array(shape),
@@ -252,8 +257,10 @@ class HybridOptimizer:
         N.check(N.lib().mmn_hybrid_create(ctypes.byref(mcc), ctypes.byref(acc), NS_MODES[ns_mode],
                                           device, _stream_of(device, stream), ctypes.byref(h)))
         self._h = h
-        self.muon = Muon(mc, ns_mode, _handle=ctypes.c_void_p(N.lib().mmn_hybrid_muon(h)))
-        self.adamw = AdamW(ac, _handle=ctypes.c_void_p(N.lib().mmn_hybrid_adamw(h)))
+        self.device = device
+        self.muon = Muon(mc, ns_mode, device,
+                         _handle=ctypes.c_void_p(N.lib().mmn_hybrid_muon(h)))
+        self.adamw = AdamW(ac, device, _handle=ctypes.c_void_p(N.lib().mmn_hybrid_adamw(h)))
 
     @staticmethod
     def classify_param(shape) -> str:
@@ -262,8 +269,8 @@ class HybridOptimizer:
 
     def step(self, id: int, param, grad, route: str | None = None,
              grad_divisor: float = 1.0) -> None:
-        pp, mem, shape = _mem_ptr(param, True)
-        gp, gmem, gshape = _mem_ptr(grad, False)
+        pp, mem, shape = _mem_ptr(param, True, self.device)
+        gp, gmem, gshape = _mem_ptr(grad, False, self.device)
         if gmem != mem or gshape != shape:
             raise N.ShapeError(N.MMN_E_SHAPE, "param and grad must match in shape and memory")
         r = {None: N.ROUTE_AUTO, ParamKind.MATRIX: N.ROUTE_MUON, ParamKind.OTHER: N.ROUTE_ADAMW}[route]

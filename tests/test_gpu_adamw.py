@@ -91,3 +91,32 @@ def test_adamw_reference_unit_test(mmn):
     opt = mmn.AdamW(mmn.AdamWConfig(lr=0.1))
     opt.step_param(0, p, np.array([[0.5]], np.float32))
     assert p[0, 0] != 1.0
+
+
+def test_device_memory_calls_refuse_host_pointers(mmn):
+    """MMN_MEM_DEVICE with a host pointer is refused (MMN_E_INVALID) before
+    any kernel could read it; the state and step counter stay untouched."""
+    import ctypes
+
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+    p = np.ones(8, np.float32)
+    g = np.ones(8, np.float32)
+    shape = N.shape_array((8,))
+    gpu = mmn.AdamW()
+    rc = L.mmn_adamw_step_param(gpu._h, 0, p.ctypes.data, g.ctypes.data, shape, 1, 1.0,
+                                N.MEM_DEVICE)
+    assert rc == N.MMN_E_INVALID and b"host memory" in L.mmn_last_error()
+    assert gpu.step == 0 and (p == 1).all()
+    mu = mmn.Muon()
+    m = np.ones((4, 4), np.float32)
+    rc = L.mmn_muon_step_matrix(mu._h, 0, m.ctypes.data, m.ctypes.data, N.shape_array((4, 4)),
+                                2, 1.0, N.MEM_DEVICE)
+    assert rc == N.MMN_E_INVALID and b"host memory" in L.mmn_last_error()
+    out = np.zeros((4, 4), np.float32)
+    rc = L.mmn_newton_schulz5_noalloc(m.ctypes.data, 4, 4, 5, N.NS_REFERENCE, out.ctypes.data, 0,
+                                      ctypes.c_void_p(0))
+    assert rc == N.MMN_E_INVALID and (out == 0).all()
+    gpu.close()
+    mu.close()
