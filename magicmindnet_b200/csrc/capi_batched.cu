@@ -21,17 +21,6 @@ using namespace mmn;
 
 namespace {
 
-struct DevGuard {
-  int prev = -1;
-  explicit DevGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    cudaSetDevice(dev);
-  }
-  ~DevGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 // NVTX range over one host-side phase (a no-op unless a profiler is attached),
@@ -318,7 +307,7 @@ extern "C" int mmn_optim_create(const mmn_optim_config* cfg, int device, void* s
   h->cfg = c;
   int rc = h->ctx.init(device, stream);
   if (rc == MMN_OK) {
-    DevGuard g(device);
+    DeviceGuard g(device);
     rc = h->bc.build(c.adamw.beta1, c.adamw.beta2);
   }
   if (rc != MMN_OK) {
@@ -332,7 +321,7 @@ extern "C" int mmn_optim_create(const mmn_optim_config* cfg, int device, void* s
 
 extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   if (!h) return MMN_OK;
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   cudaStreamSynchronize(h->ctx.stream);
   if (h->graph) cudaGraphExecDestroy(h->graph);
   for (auto& c : h->classes) ns_class_free(c);
@@ -410,7 +399,7 @@ extern "C" int mmn_optim_finalize(mmn_optim_t* h) {
 }
 
 static int finalize_layout(mmn_optim_t* h) {
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const int W = h->cfg.world_size, R = h->cfg.rank;
   const int steps = h->cfg.muon.ns_steps;
   int rc;
@@ -713,7 +702,7 @@ extern "C" int mmn_optim_set_param(mmn_optim_t* h, int slot, const float* src, i
   int rc = check_slot(h, slot);
   if (rc != MMN_OK) return rc;
   if (!src) return fail(MMN_E_INVALID, "null src");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const auto& s = h->slots[slot];
   float* dst = slot_param(h, s);
   MMN_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)s.numel * 4, kind_in(mem), h->ctx.stream));
@@ -736,7 +725,7 @@ extern "C" int mmn_optim_get_param(mmn_optim_t* h, int slot, float* dst, int mem
   int rc = check_slot(h, slot);
   if (rc != MMN_OK) return rc;
   if (!dst) return fail(MMN_E_INVALID, "null dst");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const auto& s = h->slots[slot];
   MMN_CUDA_TRY(cudaMemcpyAsync(dst, slot_param(h, s), (size_t)s.numel * 4, kind_out(mem),
                                h->ctx.stream));
@@ -748,7 +737,7 @@ extern "C" int mmn_optim_set_grad(mmn_optim_t* h, int slot, const void* src, int
   int rc = check_slot(h, slot);
   if (rc != MMN_OK) return rc;
   if (!src) return fail(MMN_E_INVALID, "null src");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   void* dst = nullptr;
   mmn_optim_slot_ptrs(h, slot, nullptr, &dst, nullptr);
   const size_t gsz = h->cfg.grad_dtype == MMN_DTYPE_BF16 ? 2 : 4;
@@ -780,7 +769,7 @@ extern "C" int mmn_optim_set_state(mmn_optim_t* h, int slot, int which, const fl
   if (!src) return fail(MMN_E_INVALID, "null src");
   float* p = nullptr;
   if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaMemcpyAsync(p, src, (size_t)h->slots[slot].numel * 4, kind_in(mem), h->ctx.stream));
   if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   return MMN_OK;
@@ -792,7 +781,7 @@ extern "C" int mmn_optim_get_state(mmn_optim_t* h, int slot, int which, float* d
   if (!dst) return fail(MMN_E_INVALID, "null dst");
   float* p = nullptr;
   if ((rc = state_ptr(h, slot, which, &p)) != MMN_OK) return rc;
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaMemcpyAsync(dst, p, (size_t)h->slots[slot].numel * 4, kind_out(mem), h->ctx.stream));
   if (mem == MMN_MEM_HOST) MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   return MMN_OK;
@@ -800,7 +789,7 @@ extern "C" int mmn_optim_get_state(mmn_optim_t* h, int slot, int which, float* d
 
 extern "C" int mmn_optim_set_adamw_step(mmn_optim_t* h, uint64_t step) {
   if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const long long v = (long long)step;
   MMN_CUDA_TRY(cudaMemcpyAsync(h->d_step, &v, sizeof(v), cudaMemcpyHostToDevice, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
@@ -809,7 +798,7 @@ extern "C" int mmn_optim_set_adamw_step(mmn_optim_t* h, uint64_t step) {
 
 extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
   if (!h || !h->finalized || !step) return fail(MMN_E_STATE, "finalize first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   long long v = 0;
   MMN_CUDA_TRY(cudaMemcpyAsync(&v, h->d_step, sizeof(v), cudaMemcpyDeviceToHost, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
@@ -1158,7 +1147,7 @@ extern "C" int mmn_optim_step(mmn_optim_t* h, float grad_divisor) {
   if (!h->finalized) return fail(MMN_E_STATE, "finalize before step");
   if (!(grad_divisor > 0.0f)) return fail(MMN_E_INVALID, "grad_divisor must be > 0");
   MMN_TRY_RC(take_grads(h));
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   // The step runs on the handle's own work stream, ordered after everything
   // already queued on the caller's stream and before anything queued there
   // later. Capture therefore never touches the caller's stream (which may be
@@ -1210,7 +1199,7 @@ extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
                     "with scan_shard the grads go in through mmn_optim_scan_grads, before "
                     "the step: pass null grads here");
   MMN_TRY_RC(take_grads(h));
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
   HostIO io{grads, params};
@@ -1230,13 +1219,13 @@ extern "C" int mmn_optim_step_host(mmn_optim_t* h, const void* const* grads,
 
 extern "C" int mmn_optim_sync(mmn_optim_t* h) {
   if (!h) return fail(MMN_E_INVALID, "null handle");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   return h->ctx.check_status();
 }
 
 extern "C" int mmn_optim_loss_scale(mmn_optim_t* h, float* scale, int64_t* skipped_steps) {
   if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   float sc = 0.0f;
   int sk = 0;
@@ -1250,7 +1239,7 @@ extern "C" int mmn_optim_loss_scale(mmn_optim_t* h, float* scale, int64_t* skipp
 extern "C" int mmn_optim_get_loss_state(mmn_optim_t* h, float* scale, int64_t* skipped_steps,
                                         int32_t* good_steps) {
   if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   float sc = 0.0f;
   int sk = 0, gd = 0;
@@ -1268,7 +1257,7 @@ extern "C" int mmn_optim_set_loss_state(mmn_optim_t* h, float scale, int64_t ski
   if (!h || !h->finalized) return fail(MMN_E_STATE, "finalize first");
   if (!(scale > 0.0f) || skipped_steps < 0 || skipped_steps > INT32_MAX || good_steps < 0)
     return fail(MMN_E_INVALID, "bad loss-scaling state");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const int sk = (int)skipped_steps, gd = good_steps;
   MMN_CUDA_TRY(cudaMemcpyAsync(h->d_scale, &scale, sizeof(float), cudaMemcpyHostToDevice,
                                h->ctx.stream));
@@ -1318,7 +1307,7 @@ constexpr uint32_t kIpcMagic = 0x4D4D4E31u;  // "MMN1"
 extern "C" int mmn_optim_export_ipc(mmn_optim_t* h, void* blob) {
   if (!h || !blob) return fail(MMN_E_INVALID, "null argument");
   if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   IpcBlob b;
   memset(&b, 0, sizeof(b));
   b.magic = kIpcMagic;
@@ -1353,7 +1342,7 @@ extern "C" int mmn_optim_connect_peers(mmn_optim_t* h, const void* blobs) {
   constexpr int kMaxPeers = 7;
   if (W - 1 > kMaxPeers) return fail(MMN_E_UNSUPPORTED, "at most 8 ranks share the exchange");
   if (!h->peer_maps.empty()) return fail(MMN_E_STATE, "peers already connected");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const uint8_t* raw = static_cast<const uint8_t*>(blobs);
   int n_peers = 0;
   void* peer_a[8] = {};
@@ -1435,7 +1424,7 @@ extern "C" int mmn_optim_reduce_grads(mmn_optim_t* h) {
   if (!h->cfg.reduce_grads || h->cfg.world_size < 2)
     return fail(MMN_E_STATE, "create the handle with reduce_grads = 1 and world_size > 1");
   if (!h->reduce_ready) return fail(MMN_E_STATE, "connect the peers first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const int W = h->cfg.world_size, R = h->cfg.rank;
   MMN_CUDA_TRY(cudaEventRecord(h->in_ev, h->ctx.stream));
   MMN_CUDA_TRY(cudaStreamWaitEvent(h->work, h->in_ev, 0));
@@ -1470,7 +1459,7 @@ extern "C" int mmn_optim_scan_grads(mmn_optim_t* h, const void* const* grads) {
   if (!h->finalized) return fail(MMN_E_STATE, "finalize first");
   if (!h->cfg.scan_shard) return fail(MMN_E_STATE, "create the handle with scan_shard = 1");
   if (!h->reduce_ready) return fail(MMN_E_STATE, "connect the peers first");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   const int W = h->cfg.world_size, R = h->cfg.rank;
   cudaStream_t s = h->ctx.stream;
   if (grads) {
@@ -1554,7 +1543,7 @@ extern "C" int mmn_optim_enable_timing(mmn_optim_t* h, int enable) {
 extern "C" int mmn_optim_last_timing(mmn_optim_t* h, float* ms5) {
   if (!h || !ms5) return fail(MMN_E_INVALID, "null argument");
   if (!h->timing || h->ev_used == 0) return fail(MMN_E_STATE, "enable timing before the steps");
-  DevGuard g(h->ctx.device);
+  DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   const size_t n = std::min(h->ev_used, mmn_optim::kTimedSteps);
   double acc[5] = {0, 0, 0, 0, 0};

@@ -23,6 +23,20 @@ int cuda_fail(cudaError_t e, const char* what);
     if (_e != cudaSuccess) return cuda_fail(_e, #expr); \
   } while (0)
 
+// Makes `dev` current for a scope and restores the previous device after it.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
 // Device, stream and SM count of a handle.
 struct Ctx {
   int device = 0;

@@ -12,17 +12,6 @@
 
 namespace mmn {
 
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
 // Copies `n` floats between host or device `src` and device `dst` on `s`.
 static cudaError_t copy_in(float* dst, const float* src, int64_t n, int mem, cudaStream_t s) {
   return cudaMemcpyAsync(dst, src, (size_t)n * 4,
