@@ -207,3 +207,23 @@ def test_host_buffers_checked_before_the_library_reads_them():
     assert _host_ptr(t, 12, 2, "grad", 0) == t.data_ptr()
     with pytest.raises(ValueError):
         _host_ptr(torch.zeros(4, 3).t(), 12, 4, "grad", 0)
+
+
+def test_plan_rejects_oversized_shapes_without_a_device():
+    """The host-only plan refuses element counts of 2^62 or more (byte counts
+    would overflow) and Muon dimensions above 2^30, with MMN_E_SHAPE."""
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+
+    def plan(shape, route):
+        shapes = (ctypes.c_int64 * len(shape))(*shape)
+        ndims = (ctypes.c_int * 1)(len(shape))
+        routes = (ctypes.c_int * 1)(route)
+        return L.mmn_optim_plan(shapes, ndims, routes, 1, 1, 5, 1, None, None, None, None)
+
+    assert plan((4, 8), N.ROUTE_MUON) == N.MMN_OK
+    assert plan((1 << 40, 1 << 40), N.ROUTE_ADAMW) == N.MMN_E_SHAPE
+    assert b"too large" in L.mmn_last_error()
+    assert plan(((1 << 31), 2), N.ROUTE_MUON) == N.MMN_E_SHAPE
+    assert plan((-1, 2), N.ROUTE_ADAMW) == N.MMN_E_INVALID
