@@ -227,3 +227,36 @@ def test_plan_rejects_oversized_shapes_without_a_device():
     assert b"too large" in L.mmn_last_error()
     assert plan(((1 << 31), 2), N.ROUTE_MUON) == N.MMN_E_SHAPE
     assert plan((-1, 2), N.ROUTE_ADAMW) == N.MMN_E_INVALID
+
+
+def _header_functions():
+    """{name: parameter count} of every function the C header declares."""
+    text = open(os.path.join(ROOT, "include", "mmn_optim.h")).read()
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(mmn_\w+)\s*\(([^()]*)\)\s*;", text):
+        args = m.group(2).strip()
+        out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_integration_rust_block_matches_the_header():
+    """The Rust extern block a maintainer would add declares
+    only functions of the header, each with the header's parameter count, and
+    its constants carry the header's values."""
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    block = text[text.index('extern "C" {'):]
+    block = block[:block.index("\n}\n")]
+    header = _header_functions()
+    rust = {}
+    for m in re.finditer(r"pub fn (mmn_\w+)\(([^)]*)\)", block, flags=re.S):
+        args = m.group(2).strip()
+        rust[m.group(1)] = 0 if not args else args.count(":")
+    assert len(rust) >= 40
+    for name, n in rust.items():
+        assert name in header, name
+        assert n == header[name], (name, n, header[name])
+    hdr = open(os.path.join(ROOT, "include", "mmn_optim.h")).read()
+    defines = dict(re.findall(r"#define (MMN_\w+) \(?(-?\d+)\)?", hdr))
+    for name, value in re.findall(r"pub const (MMN_\w+): \w+ = (-?\d+);", text):
+        assert defines[name] == value, name
