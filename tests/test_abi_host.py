@@ -25,8 +25,12 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 45
     missing = [n for n in names if not hasattr(L, n)]
     assert not missing, missing
-    # the ctypes table covers exactly the declared functions
+    # the ctypes table covers exactly the declared functions, each with the
+    # header's parameter count
     assert sorted(N.SIGNATURES) == names
+    header = _header_functions()
+    for name, (_, argtypes) in N.SIGNATURES.items():
+        assert len(argtypes) == header[name], (name, len(argtypes), header[name])
 
 
 def test_abi_version_and_defaults():
