@@ -246,7 +246,10 @@ static int muon_class(mmn_muon* h, int n, int m, NsClass** out) {
     NsClass c;
     std::string e =
         ns_class_init(c, n, m, 1, nullptr, ns_elem_bytes(h->ns_mode), ns_planes(h->ns_mode));
-    if (!e.empty()) return fail(MMN_E_CUDA, e);
+    if (!e.empty()) {
+      ns_class_free(c);  // (frees the buffers a failed init may already hold)
+      return fail(MMN_E_CUDA, e);
+    }
     it = h->classes.emplace(key, c).first;
   }
   *out = &it->second;
@@ -525,6 +528,7 @@ extern "C" int mmn_newton_schulz_iteration(const float* x, int64_t n, int64_t m,
   const bool split = ns_mode == MMN_NS_FP32;
   e = ns_class_init(c, (int)n, (int)m, 1, nullptr, ns_elem_bytes(ns_mode), ns_planes(ns_mode));
   if (!e.empty()) {
+    ns_class_free(c);
     ctx.release();
     return fail(MMN_E_OOM, e);
   }
