@@ -49,13 +49,17 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes (read + write) per algorithmic Newton-Schulz flop of the GEMM
 # kernels of one reference-mode optimizer step (5 iterations, the last one fused
-# with the parameter update), from the ncu capture of the 8 x [2048, 8192]
-# profiling case (profiles/ns_gemm_probe_full.md): 5763.1 MB per 6.1848e12 flop.
-# Traffic grows with the flops of a class, so the per-step traffic of a workload
-# is this ratio times its Newton-Schulz flops.
+# with the parameter update): 5763.1 MB of dram__bytes_read.sum +
+# dram__bytes_write.sum per 6.1848e12 flop, summed over the Gram, Square and
+# Poly launches of one step of the 8 x [2048, 8192] case
+# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+#  -k regex:ns_gemm python bench.py --workload ns_probe --steps 1 --warmup 3
+#  --no-e2e --no-cpu-baseline). Traffic grows with the flops of a class, so the
+# per-step traffic of a workload is this ratio times its Newton-Schulz flops.
 NS_DRAM_BYTES_PER_FLOP = 5763.1e6 / 6.1848e12
-# DRAM bytes per element of the isolated AdamW kernel measured by ncu on the
-# 2^28 arena: read p, g, m, v and write p, m, v (profiles/adamw_arena.md).
+# DRAM bytes per element of the isolated AdamW kernel: read p, g, m, v and write
+# p, m, v, as ncu's dram__bytes_read.sum + dram__bytes_write.sum of one
+# adamw_kernel launch on the 2^28 arena gives (7.52 GB per launch).
 ADAMW_DRAM_BYTES_PER_PARAM = 28.0
 
 
@@ -210,60 +214,284 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline(workload: str, model, sample_s: float = 15.0):
+def _ns_flops(n, m, steps=5):
+    return steps * (4.0 * n * n * m + 2.0 * n ** 3)
+
+
+class RefSampler:
     """The oracle (a C port of the reference's CPU step) timed on this host's
-    cores on a bounded sample of the workload, extrapolated to one full step
-    by the sample's share of the step's work. Returns a dict for the JSON line."""
-    import numpy as np
+    cores on a bounded sample of one optimizer step of `model`, extrapolated to
+    the whole step.
 
-    from oracle import reference_optim as R
+    A sample is AdamW over a slice of at most 2^24 elements (scaled by element
+    count) and, for every Newton-Schulz shape class, one matrix shrunk until its
+    flops are at most `sample_flops` (the reference runs every matrix of the
+    class through the same code). Calibration times one full-size matrix of
+    every class whose flops are at most `full_cap` once, so that the sample of
+    that class is scaled by the measured full/sample time ratio; larger classes
+    are scaled by their flop ratio. threads = 0 uses every host thread."""
 
-    cores = R.lib().ref_max_threads()
-    rng = np.random.default_rng(0)
-    n_total = count_params(model)
-    muon = [s for _, s, r in model if r == "muon" or (r == "auto" and R.classify_param(s) == R.MATRIX)]
-    adamw_n = n_total - sum(s[0] * s[1] for s in muon)
-    t_full = 0.0
-    parts = []
-    # AdamW: time a slice, scale by element count.
-    if adamw_n:
-        k = min(adamw_n, 1 << 24)
-        p = rng.normal(0, 0.02, k).astype(np.float32)
-        g = rng.normal(0, 1e-3, k).astype(np.float32)
-        m = np.zeros(k, np.float32)
-        v = np.zeros(k, np.float32)
-        dt = min(R.lib().ref_adamw_step_timed(R._ptr(p), R._ptr(m), R._ptr(v), R._ptr(g), k, 3e-4,
-                                               0.9, 0.95, 1e-8, 0.01, 10, 1.0, 0)
-                 for _ in range(3))
-        t_full += dt * adamw_n / k
-        parts.append(f"AdamW {k} elems x{adamw_n / k:.1f}")
-    # Newton-Schulz: one matrix per shape class, scaled down so the sample stays
-    # bounded, extrapolated by flop count.
-    classes = {}
-    for s in muon:
-        n, mm = min(s), max(s)
-        classes[(n, mm)] = classes.get((n, mm), 0) + 1
-    budget = sample_s / max(len(classes), 1)
-    for (n, mm), cnt in classes.items():
-        f_full = 5 * (4.0 * n * n * mm + 2.0 * n ** 3)
-        sn, sm = n, mm
-        while 5 * (4.0 * sn * sn * sm + 2.0 * sn ** 3) > 5e10 and sn > 64:
-            sn //= 2
-            sm //= 2
-        g = rng.normal(0, 1e-2, (sn, sm)).astype(np.float32)
+    def __init__(self, model, threads=0, sample_flops=5e10, full_cap=1.2e12, calibrate=True):
+        import numpy as np
+
+        from oracle import reference_optim as R
+
+        self.R, self.np = R, np
+        self.threads = threads
+        self.cores = R.lib().ref_max_threads() if threads <= 0 else threads
+        self.rng = np.random.default_rng(0)
+        self.n_total = count_params(model)
+        muon = [s for _, s, r in model
+                if r == "muon" or (r == "auto" and R.classify_param(s) == R.MATRIX)]
+        self.adamw_n = self.n_total - sum(s[0] * s[1] for s in muon)
+        self.k = min(self.adamw_n, 1 << 24)
+        self.classes = {}
+        for s in muon:
+            key = (min(s), max(s))
+            self.classes[key] = self.classes.get(key, 0) + 1
+        self.sample = {}
+        for (n, m) in self.classes:
+            sn, sm = n, m
+            while _ns_flops(sn, sm) > sample_flops and sn > 64:
+                sn //= 2
+                sm //= 2
+            self.sample[(n, m)] = (sn, sm)
+        self.ratio = {c: _ns_flops(*c) / _ns_flops(*self.sample[c]) for c in self.classes}
+        self.calibration = {}
+        if calibrate:
+            for c in self.classes:
+                if _ns_flops(*c) > full_cap or self.sample[c] == c:
+                    continue
+                t_full = self._time_ns(c)
+                t_samp = min(self._time_ns(self.sample[c]) for _ in range(2))
+                self.ratio[c] = t_full / t_samp
+                self.calibration[f"{c[0]}x{c[1]}"] = {
+                    "full_s": round(t_full, 3), "sample_s": round(t_samp, 3),
+                    "flop_ratio": round(_ns_flops(*c) / _ns_flops(*self.sample[c]), 2),
+                    "time_ratio": round(self.ratio[c], 2)}
+
+    def _time_ns(self, shape):
+        g = self.rng.normal(0, 1e-2, shape).astype(self.np.float32)
         t0 = time.perf_counter()
-        R.newton_schulz5(g, 5, order=R.GEMM_F32_FMA)
-        dt = time.perf_counter() - t0
-        f_s = 5 * (4.0 * sn * sn * sm + 2.0 * sn ** 3)
-        t_full += dt * (f_full / f_s) * cnt
-        parts.append(f"NS [{sn},{sm}] for {cnt} x [{n},{mm}] (flop-scaled)")
-        if dt > budget:
-            break
-    return {"value": n_total / t_full if t_full else None, "unit": "params/s", "cores": cores,
-            "kind": "port", "sample": "; ".join(parts), "step_s_extrapolated": t_full}
+        self.R.newton_schulz5(g, 5, order=self.R.GEMM_F32_FMA, threads=self.threads)
+        return time.perf_counter() - t0
+
+    def step(self):
+        """One sampled step: (extrapolated seconds of the whole step, seconds
+        the sample took)."""
+        np, R = self.np, self.R
+        w0 = time.perf_counter()
+        t_full = 0.0
+        if self.adamw_n:
+            k = self.k
+            p = self.rng.normal(0, 0.02, k).astype(np.float32)
+            g = self.rng.normal(0, 1e-3, k).astype(np.float32)
+            m = np.zeros(k, np.float32)
+            v = np.zeros(k, np.float32)
+            dt = R.lib().ref_adamw_step_timed(R._ptr(p), R._ptr(m), R._ptr(v), R._ptr(g), k,
+                                              3e-4, 0.9, 0.95, 1e-8, 0.01, 10, 1.0, self.threads)
+            t_full += dt * self.adamw_n / k
+        for c, cnt in self.classes.items():
+            t_full += self._time_ns(self.sample[c]) * self.ratio[c] * cnt
+        return t_full, time.perf_counter() - w0
+
+    def describe(self):
+        parts = []
+        if self.adamw_n:
+            parts.append(f"AdamW {self.k} of {self.adamw_n} elems")
+        for c, cnt in self.classes.items():
+            how = "time-scaled from a full-size run" if f"{c[0]}x{c[1]}" in self.calibration \
+                else "flop-scaled"
+            parts.append(f"NS [{self.sample[c][0]},{self.sample[c][1]}] for {cnt} x "
+                         f"[{c[0]},{c[1]}] ({how})")
+        return "; ".join(parts)
+
+    def sampled_fraction(self):
+        """Share of the step's work one sample runs (elements for AdamW, flops
+        for Newton-Schulz, each weighted by its extrapolated time share)."""
+        tot = sum(_ns_flops(*c) * cnt for c, cnt in self.classes.items())
+        smp = sum(_ns_flops(*self.sample[c]) for c in self.classes)
+        return {"adamw_elems": self.k / self.adamw_n if self.adamw_n else None,
+                "ns_flops": smp / tot if tot else None}
+
+
+def cpu_baseline(workload: str, model):
+    """The oracle on this host's cores for the JSON line's cpu_baseline: every
+    thread (calibrated on full-size matrices where that is bounded) and one
+    thread (the reference is single-threaded), each one sampled step,
+    extrapolated to the whole step and labelled as such."""
+    allt = RefSampler(model)
+    t_all, w_all = allt.step()
+    one = RefSampler(model, threads=1, sample_flops=1e10, calibrate=False)
+    t_one, w_one = one.step()
+    return {"value": allt.n_total / t_all, "unit": "params/s", "cores": allt.cores,
+            "kind": "port", "extrapolated": True, "sample": allt.describe(),
+            "sample_s": round(w_all, 3), "step_s_extrapolated": t_all,
+            "sampled_fraction": allt.sampled_fraction(), "calibration": allt.calibration,
+            "single_thread": {"value": one.n_total / t_one, "unit": "params/s", "cores": 1,
+                              "extrapolated": True, "sample": one.describe(),
+                              "sample_s": round(w_one, 3), "step_s_extrapolated": t_one}}
 
 
 # --------------------------------------------------------------------- ours
+def fill_workload(step, workload, model, dev):
+    """Seeded synthetic values of a workload, generated on the device in slot
+    order (the same values on every GPU and every rank):
+    params ~ N(0, 0.02); grads ~ N(0, 1e-3) (N(0, 1e-2) for the isolated AdamW
+    and Newton-Schulz workloads; bf16 grads carry the 2^16 loss scale);
+    the isolated AdamW arena also gets m ~ N(0, 1e-3), v ~ |N(0, 1e-4)| and the
+    step count 9 (its first timed step runs at t = 10), the isolated
+    Newton-Schulz batch a velocity ~ N(0, 1e-3)."""
+    import torch
+
+    gen = torch.Generator(device=f"cuda:{dev}").manual_seed(0)
+    for k, (_, s, _) in enumerate(model):
+        step.param(k).normal_(0, 0.02, generator=gen)
+        gv = step.grad(k)
+        if gv.dtype == torch.bfloat16:
+            gv.copy_((torch.randn(s, device=f"cuda:{dev}", generator=gen) * (1e-3 * 65536.0)))
+        else:
+            gv.normal_(0, 1e-2 if workload in ("adamw_arena", "ns_batch") else 1e-3,
+                       generator=gen)
+    if step.config.bf16_param_shadow:
+        for k in range(len(model)):
+            step.param_bf16(k).copy_(step.param(k))
+    if workload == "adamw_arena":
+        n = model[0][1][0]
+        m = torch.empty(n, device=f"cuda:{dev}").normal_(0, 1e-3, generator=gen)
+        step.set_state(0, "m", m)
+        m.normal_(0, 1e-4, generator=gen).abs_()
+        step.set_state(0, "v", m)
+        del m
+        step.adamw_step = 9  # the timed steps run at t = 10, 11, ...
+    if workload == "ns_batch":
+        for k, (_, s, _) in enumerate(model):
+            vel = torch.empty(s, device=f"cuda:{dev}").normal_(0, 1e-3, generator=gen)
+            step.set_state(k, "velocity", vel)
+        del vel
+    torch.cuda.synchronize(dev)
+
+
+def isolated_kernels(dev, pk, pk_kind, ns_modes=("reference", "tf32")):
+    """The configurations' isolated kernel workloads, timed with CUDA events in
+    the same run after the main workload has freed its memory: the fused AdamW
+    over the 2^28-element arena (t = 10, wd 0.1, divisor 4; 28 B per param) and
+    Newton-Schulz on 64 x [4096, 4096] + 32 x [4096, 14336] (velocity ~ N(0,
+    1e-3), 5 iterations) in the reference recipe and in the TF32 mode. 3 warm-up
+    and 3 timed steps each; inputs larger than L2. Fractions are of the measured
+    peaks (HBM copy bandwidth; cuBLAS bf16 burst; the dense TF32 peak measured
+    here, before the timed steps)."""
+    import torch
+
+    import magicmindnet_b200 as mmn
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(workload, cfg, divisor, warmup=3, steps=3):
+        model = WORKLOADS[workload]["model"]()
+        step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg,
+                                 device=dev, stream=stream.cuda_stream)
+        fill_workload(step, workload, model, dev)
+        for _ in range(warmup):
+            step.step(divisor)
+        if workload == "adamw_arena":
+            step.adamw_step = 9  # the timed steps run at t = 10, 11, 12
+        torch.cuda.synchronize(dev)
+        step.enable_timing(True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step.step(divisor)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ph = step.last_timing()
+        flops = step.ns_flops()
+        step.close()
+        torch.cuda.empty_cache()
+        return e0.elapsed_time(e1) / steps, ph, flops
+
+    adamw = mmn.AdamWConfig(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    ms, ph, _ = timed("adamw_arena", mmn.StepConfig(adamw=adamw, use_graph=False), 4.0)
+    byts = ADAMW_DRAM_BYTES_PER_PARAM * (1 << 28)
+    out["adamw_arena"] = {"kernel_ms": ph["adamw"], "step_ms": ms,
+                          "GB/s": byts / (ph["adamw"] / 1e3) / 1e9,
+                          "frac": byts / (ph["adamw"] / 1e3) / 1e9 / pk["hbm_gbs"],
+                          "peak": pk["hbm_gbs"], "peak_source": pk_kind,
+                          "bytes_per_launch": byts}
+    for mode in ns_modes:
+        if mode in ("tf32", "fp32"):
+            tf32 = measure_tf32_peak(dev)
+            peak, src = tf32[0] / (3.0 if mode == "fp32" else 1.0), "measured in this run: " \
+                "cuBLAS tf32 8192^3, best of 10"
+        else:
+            peak, src = pk["bf16_tflops"], pk_kind
+        ms, ph, flops = timed("ns_batch", mmn.StepConfig(ns_mode=mode, use_graph=True), 1.0)
+        tf = flops / (ph["newton_schulz"] / 1e3) / 1e12
+        out[f"ns_batch_{mode}"] = {"ns_ms": ph["newton_schulz"], "step_ms": ms,
+                                   "momentum_ms": ph["muon_momentum"], "flops": flops,
+                                   "TFLOP/s": tf, "peak": peak, "frac": tf / peak,
+                                   "peak_source": src}
+    return out
+
+
+def _param_checksums(step, n_slots):
+    """Per-slot exact checksums of the parameters every rank holds after the
+    exchange (fp32, or the bf16 copies when the fp32 master stays with its
+    owner): the integer sum of the bit patterns and a position-weighted one."""
+    import torch
+
+    rows = []
+    for k in range(n_slots):
+        t = step.param_bf16(k) if step.config.bf16_param_shadow else step.param(k)
+        bits = t.view(torch.int16 if t.dtype == torch.bfloat16 else torch.int32).reshape(-1)
+        b = bits.to(torch.int64)
+        w = torch.arange(b.numel(), device=b.device, dtype=torch.int64) % 4093 + 1
+        rows.append(torch.stack([b.sum(), (b * w).sum()]))
+        del b, w
+    return torch.stack(rows)
+
+
+def parity_vs_single(step, model, cfg, workload, n_steps, inj, divisor, rank, world, dev):
+    """After a sharded run: every rank's parameters against one GPU stepping the
+    same seeded workload unsharded, bit for bit. Each rank checksums every
+    slot; the handles are closed; rank 0 replays the n_steps steps (with the
+    same injected non-finite grads) on its own GPU and compares. Returns the
+    verdict every rank agrees on."""
+    import torch
+    import torch.distributed as dist
+
+    import magicmindnet_b200 as mmn
+
+    cs = _param_checksums(step, len(model))
+    mx, mn = cs.clone(), cs.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+    step.close()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ok = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    if rank == 0:
+        one_cfg = mmn.StepConfig(**{**cfg.__dict__, "rank": 0, "world_size": 1,
+                                    "reduce_grads": False, "scan_shard": False})
+        single = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], one_cfg,
+                                   device=dev, stream=torch.cuda.current_stream(dev).cuda_stream)
+        fill_workload(single, workload, model, dev)
+        g0 = single.grad(0).view(-1)
+        for i in range(n_steps):  # the grad edits and the steps share one stream
+            if i in inj:
+                g0[0] = float("inf")
+            single.step(divisor)
+            if i in inj:
+                g0[0] = 1e-3 * 65536.0
+        single.sync()
+        ref = _param_checksums(single, len(model))
+        single.close()
+        ok[0] = int(torch.equal(mx, mn) and torch.equal(mx, ref))
+    dist.broadcast(ok, 0)
+    return bool(ok.item())
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -294,26 +522,10 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     step = mmn.OptimizerStep([(k, s, r) for k, (_, s, r) in enumerate(model)], cfg, device=dev,
                              stream=stream.cuda_stream)
-    # seeded synthetic values, generated on the device
-    gen = torch.Generator(device=f"cuda:{dev}").manual_seed(0)
-    for k, (_, s, _) in enumerate(model):
-        step.param(k).normal_(0, 0.02, generator=gen)
-        gv = step.grad(k)
-        if gv.dtype == torch.bfloat16:
-            gv.copy_((torch.randn(s, device=f"cuda:{dev}", generator=gen) * (1e-3 * 65536.0)))
-        else:
-            gv.normal_(0, 1e-2 if args.workload in ("adamw_arena", "ns_batch") else 1e-3,
-                       generator=gen)
-    if is_8b:
-        for k in range(len(model)):
-            b = step.param_bf16(k)
-            b.copy_(step.param(k))
-    if args.workload == "adamw_arena":
-        step.set_state(0, "m", np.random.default_rng(0).normal(0, 1e-3, 1 << 28).astype(np.float32))
-        step.set_state(0, "v", np.abs(np.random.default_rng(1).normal(0, 1e-4, 1 << 28)).astype(np.float32))
-        step.adamw_step = 9  # the timed steps run at t = 10, 11, ...
+    fill_workload(step, args.workload, model, dev)
     divisor = 4.0 if args.workload == "adamw_arena" else 1.0
     torch.cuda.synchronize()
+    n_done = 0  # steps taken so far (the multi-GPU parity replay repeats them)
 
     gl = step.gather_layout()
     gathers = []
@@ -369,8 +581,10 @@ def run_ours(args, rank, world, local_rank):
     # region is untouched
     tf32_peak = measure_tf32_peak(dev) if args.ns_mode in ("tf32", "fp32") else None
     inj = []
+    inj_global = []
     for i in range(args.warmup):
         one_step()
+        n_done += 1
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
@@ -389,8 +603,10 @@ def run_ours(args, rank, world, local_rank):
     for i in range(args.steps):
         if is_8b and i % 100 == 50:
             inj.append(i)  # one injected inf grad per 100 steps
+            inj_global.append(n_done)
             step.grad(0).view(-1)[0] = float("inf")
         one_step()
+        n_done += 1
         if is_8b and i % 100 == 50:
             step.grad(0).view(-1)[0] = 1e-3 * 65536.0
     ev1.record(stream)
@@ -454,6 +670,7 @@ def run_ours(args, rank, world, local_rank):
 
         for _ in range(2):
             host_step()
+            n_done += 1
         e_steps = max(1, min(args.steps, 10))
         if world > 1:
             import torch.distributed as dist
@@ -463,6 +680,7 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(e_steps):
             host_step()
         e_ms = (time.perf_counter() - t0) * 1e3 / e_steps
+        n_done += e_steps
         if world > 1:
             import torch.distributed as dist
 
@@ -493,6 +711,7 @@ def run_ours(args, rank, world, local_rank):
                           if med["newton_schulz"] else None},
         "muon_momentum_ms": med["muon_momentum"], "muon_update_ms": med["muon_update"],
         "step_ms_events": med["step"],
+        "exchange_exposed_ms": (ms - med["step"]) if world > 1 else None,
         "note": "phase times are averaged over the timed steps. AdamW runs on a side stream "
                 "concurrently with the Newton-Schulz GEMMs, so in hybrid workloads its event "
                 "time includes waiting for SMs; its kernel rate is the adamw_arena workload's",
@@ -559,30 +778,55 @@ def run_ours(args, rank, world, local_rank):
     if is_8b:
         line["loss_scale"] = dict(zip(("scale", "skipped_steps"), step.loss_scale()))
         line["injected_inf_steps"] = inj
+    if world > 1 and not dp:
+        # the sharded result against one GPU stepping the same workload, bit for bit
+        line["parity_vs_1gpu"] = parity_vs_single(step, model, cfg, args.workload, n_done,
+                                                  set(inj_global), divisor, rank, world, dev)
+        line["parity_steps"] = n_done
+    else:
+        if world > 1:
+            line["parity_vs_1gpu"] = None  # local grads differ per rank under --grad-reduce
+        step.close()
+    if world == 1 and args.kernels and args.workload.startswith("hybrid"):
+        torch.cuda.empty_cache()
+        comp["isolated"] = isolated_kernels(dev, pk, pk_kind)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload, model)
-    step.close()
     return line
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle port of the reference's CPU step on this
+    host's cores (no Rust toolchain exists to build the reference itself). Each
+    of the warm-up and timed steps is one bounded sample of the workload's step
+    (RefSampler), extrapolated to the whole step; ms_per_step is that
+    extrapolated step time and sample_ms_per_step what the samples took."""
     if rank != 0:
         return None
     spec = WORKLOADS[args.workload]
     model = spec["model"]()
-    vals = []
+    smp = RefSampler(model)
+    full, wall = [], []
     for i in range(args.warmup + args.steps):
-        cb = cpu_baseline(args.workload, model, sample_s=2.0)
+        t, w = smp.step()
         if i >= args.warmup:
-            vals.append(cb)
-    v = statistics.median(c["value"] for c in vals)
-    ms = statistics.median(c["step_s_extrapolated"] for c in vals) * 1e3
-    cb = dict(vals[-1])
-    cb["value"] = v
+            full.append(t)
+            wall.append(w)
+    t_med = statistics.median(full)
+    v = smp.n_total / t_med
+    one = RefSampler(model, threads=1, sample_flops=1e10, calibrate=False)
+    t_one, w_one = one.step()
+    cb = {"value": v, "unit": "params/s", "cores": smp.cores, "kind": "port",
+          "extrapolated": True, "sample": smp.describe(),
+          "sampled_fraction": smp.sampled_fraction(), "calibration": smp.calibration,
+          "single_thread": {"value": one.n_total / t_one, "unit": "params/s", "cores": 1,
+                            "extrapolated": True, "sample": one.describe(),
+                            "sample_s": round(w_one, 3), "step_s_extrapolated": t_one}}
     return {"metric": METRIC, "value": v, "unit": "params/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
-            "data": "synthetic (seeded normal params/grads)",
+            "warmup": args.warmup, "ms_per_step": t_med * 1e3,
+            "sample_ms_per_step": statistics.median(wall) * 1e3, "extrapolated": True,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "impl": "reference", "data": "synthetic (seeded normal params/grads)",
             "config": {"workload": args.workload, "desc": spec["desc"],
                        "params": count_params(model)},
             "cpu_baseline": cb,
@@ -600,6 +844,9 @@ def main():
     ap.add_argument("--ns-mode", default="reference", choices=["reference", "bf16", "tf32", "fp32"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", dest="kernels", action="store_false",
+                    help="skip the isolated AdamW-arena and Newton-Schulz-batch timings that "
+                         "a one-GPU hybrid run adds to its components")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU parameter exchange: copy-engine pushes over NVLink inside "
                          "the step (CUDA IPC) or an NCCL all-gather after the step")
@@ -640,6 +887,9 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if line.get("parity_vs_1gpu") is False:
+        print("sharded parameters differ from the one-GPU step", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

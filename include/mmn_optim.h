@@ -186,7 +186,8 @@ int mmn_newton_schulz5(const float *g, const int64_t *shape, int ndim, int steps
  * call on a device resolves that array's device address and should come
  * before any stream capture. All calls on a device share the array, so calls
  * that overlap on the GPU race. Work is enqueued on `stream` (NULL = legacy
- * default stream) and the call returns after it has finished. */
+ * default stream) and the call returns after it has finished; it waits for
+ * that stream only, not for the whole device. */
 int mmn_newton_schulz5_noalloc(const float *g, int64_t rows, int64_t cols, int steps,
                                int ns_mode, float *out, int device, void *stream);
 

@@ -20,7 +20,7 @@ OBJ_DIR = os.path.join(OUT_DIR, "obj")
 LIB_NAME = "libmmn_optim_cuda.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
-SOURCES = ["elementwise.cu", "ns_engine.cu", "capi_common.cu", "capi_percall.cu",
+SOURCES = ["elementwise.cu", "refnorm.cu", "ns_engine.cu", "capi_common.cu", "capi_percall.cu",
            "capi_batched.cu", "ns_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",

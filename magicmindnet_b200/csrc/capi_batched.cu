@@ -1034,13 +1034,14 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       m.tile_begin = h->chunk_tile0[k];
       m.total_tiles = h->chunk_tile0[k + 1] - h->chunk_tile0[k];
     };
-    // momentum, bf16 cast and norms of chunk k
-    auto prologue = [&](size_t k) -> int {
+    // momentum and bf16 cast of chunk k, and its norms unless they come later
+    // for every chunk at once
+    auto prologue = [&](size_t k, bool norms) -> int {
       NvtxRange r("mmn.muon_momentum");
       select(k);
       m.cls = h->d_cls_in;
       launch_muon_momentum(m, h->ctx.num_sms, s);
-      launch_muon_norms(m, s);
+      if (norms) launch_muon_norms(m, s);
       MMN_CUDA_TRY(cudaGetLastError());
       return MMN_OK;
     };
@@ -1077,12 +1078,21 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       for (size_t j = 0; j < h->jobs.size(); ++j) {
         if (h->jobs[j] < 0) continue;
         MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->h2d_ev[j], 0));
-        MMN_TRY_RC(prologue(h->jobs[j]));
+        MMN_TRY_RC(prologue(h->jobs[j], true));
         MMN_TRY_RC(newton_schulz(h->jobs[j]));
       }
     } else {
       for (int k : h->jobs)
-        if (k >= 0) MMN_TRY_RC(prologue(k));
+        if (k >= 0) MMN_TRY_RC(prologue(k, false));
+      // the norms of every matrix in one launch: one CTA per matrix, largest
+      // first, so the long sequential sums of the large matrices run side by side
+      m.mats = h->d_mats;
+      m.nmat = (int)h->mats.size();
+      m.tile_begin = 0;
+      m.total_tiles = h->total_tiles;
+      m.cls = h->d_cls_in;
+      launch_muon_norms(m, s);
+      MMN_CUDA_TRY(cudaGetLastError());
       if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[4], s));
       for (int k : h->jobs)
         if (k >= 0) MMN_TRY_RC(newton_schulz(k));
@@ -1525,8 +1535,10 @@ extern "C" int mmn_optim_kernel_launches(mmn_optim_t* h, int64_t* per_step,
   int64_t n = (adamw ? 1 : 0) + 1;  // AdamW, step tail
   if (h->cfg.loss_scaling && !h->cfg.reduce_grads && !h->cfg.scan_shard)
     n += 2;  // non-finite scans
-  // per chunk: momentum, norms, 3 GEMMs per iteration (or the update kernel)
-  n += (int64_t)h->chunk_begin.size() * (2 + (steps >= 1 ? 3 * steps : 1));
+  // per chunk: momentum, 3 GEMMs per iteration (or the update kernel); the
+  // norms of every chunk in one launch (mmn_optim_step_host: one per chunk)
+  const int64_t chunks = (int64_t)h->chunk_begin.size();
+  n += chunks * (1 + (steps >= 1 ? 3 * steps : 1)) + (chunks ? 1 : 0);
   if (per_step) *per_step = n;
   // mmn_optim_reduce_grads, or mmn_optim_scan_grads: one launch per arena
   if (per_reduce) *per_reduce = (h->cfg.reduce_grads || h->cfg.scan_shard) ? 2 : 0;

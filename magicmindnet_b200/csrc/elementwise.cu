@@ -402,8 +402,12 @@ __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kerne
     if (a.vec_ok && (mm.cols & 3) == 0 && (mm.off & 3) == 0) {
       const float ssv = momentum_tile_vec<BF16G, FRESH, XM>(a, mm, r0, c0, Xv, cp.ld, cp.bstride,
                                                             tile, scale, mu, one_m);
-      const float totv = block_sum_256(ssv, red);
-      if (threadIdx.x == 0) a.partials[t] = totv;
+      if constexpr (XM != 0) {
+        const float totv = block_sum_256(ssv, red);
+        if (threadIdx.x == 0) a.partials[t] = totv;
+      } else if (mm.transposed) {
+        __syncthreads();  // the next tile may overwrite `tile`
+      }
       continue;
     }
     float ss = 0.0f;
@@ -434,8 +438,12 @@ __global__ void __launch_bounds__(256, kMomentumBlocksPerSm) muon_momentum_kerne
           x_store1<XM>(Xv, (long long)c * cp.ld + r, cp.bstride, tile[tx][cc]);
       }
     }
-    const float tot = block_sum_256(ss, red);
-    if (threadIdx.x == 0) a.partials[t] = tot;
+    if constexpr (XM != 0) {
+      const float tot = block_sum_256(ss, red);
+      if (threadIdx.x == 0) a.partials[t] = tot;
+    } else if (mm.transposed) {
+      __syncthreads();  // the next tile may overwrite `tile`
+    }
   }
 }
 
@@ -701,6 +709,10 @@ void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
 
 void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
   if (a.nmat <= 0) return;
+  if (a.x_mode == 0) {
+    launch_ref_norms(a, stream);
+    return;
+  }
   muon_norm_kernel<<<a.nmat < 1024 ? a.nmat : 1024, 256, 0, stream>>>(a);
 }
 

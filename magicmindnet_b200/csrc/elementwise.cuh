@@ -72,7 +72,7 @@ struct MuonArgs {
   int tile_begin;        // mats[0].tile0: the launch covers tiles
   int total_tiles;       // [tile_begin, tile_begin + total_tiles)
   const MuonClassPtr* cls;
-  float* partials;      // one fp32 sum of squares per tile
+  float* partials;      // one fp32 sum of squares per tile (x_mode 1 and 2)
   float* norms;         // clamped Frobenius norms, slot mats[k].norm_idx
   const int* skip;
   const float* grad_scale;
@@ -88,7 +88,13 @@ struct MuonArgs {
 };
 
 void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream);
+// Frobenius norms of the Newton-Schulz inputs of a.mats into a.norms: the
+// reference's sequential fp32 sum reproduced bit for bit (x_mode 0, the
+// reference and bf16 recipes; refnorm.cu), or the fixed-order sum of the
+// momentum kernel's tile partials (x_mode 1 and 2, the TF32 and fp32 modes,
+// which have no reference counterpart and aim at exact Newton-Schulz).
 void launch_muon_norms(const MuonArgs& a, cudaStream_t stream);
+void launch_ref_norms(const MuonArgs& a, cudaStream_t stream);
 void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream);
 
 // Non-finite scan of fp32 and bf16 grad arenas into *flag (flag must be zero).

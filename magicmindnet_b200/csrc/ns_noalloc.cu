@@ -145,6 +145,10 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
   meta.cls[1].x = c.x[steps % 2];
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The tile list and `meta` are pageable host objects of this call. The
+  // runtime stages a pageable source before cudaMemcpyAsync returns, so an
+  // early error return may drop them; on success the call also waits for its
+  // stream before returning, so they outlive their copies either way.
   MMN_CUDA_TRY(cudaMemsetAsync(base, 0, used, s));
   MMN_CUDA_TRY(cudaMemcpyAsync(c.sym_tiles, tile_list.data(), tile_list.size() * sizeof(int2),
                                cudaMemcpyHostToDevice, s));
@@ -176,9 +180,11 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
   a.cls = &dmeta->cls[1];
   launch_muon_apply(a, slot.num_sms, s);
   MMN_CUDA_TRY(cudaGetLastError());
-  MMN_CUDA_TRY(cudaStreamSynchronize(s));
+  // The status word comes back on the caller's stream, so the call waits for
+  // that stream only (a plain cudaMemcpy would wait for the whole device).
   int st = 0;
-  MMN_CUDA_TRY(cudaMemcpy(&st, status, sizeof(int), cudaMemcpyDeviceToHost));
+  MMN_CUDA_TRY(cudaMemcpyAsync(&st, status, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MMN_CUDA_TRY(cudaStreamSynchronize(s));
   if (st != kDevOk)
     return fail(MMN_E_TIMEOUT, "a kernel gave up a bounded wait (device status " +
                                    std::to_string(st) + ")");

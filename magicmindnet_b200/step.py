@@ -200,9 +200,26 @@ class OptimizerStep:
         N.check(N.lib().mmn_optim_set_grad(
             self._h, slot, _host_ptr(v, self._numel(slot), gsz, "grad", slot), N.MEM_HOST))
 
-    def set_state(self, slot: int, which: str, values: np.ndarray) -> None:
+    def set_state(self, slot: int, which: str, values) -> None:
+        """Seed a slot's m, v or velocity from a host array, or from a contiguous
+        fp32 CUDA tensor on the handle's GPU (copied device to device; the call
+        returns once the copy is done)."""
+        kind = {"m": 0, "v": 1, "velocity": 2}[which]
+        if getattr(values, "is_cuda", False):
+            import torch
+
+            if (values.dtype != torch.float32 or not values.is_contiguous()
+                    or values.numel() != self._numel(slot)
+                    or values.device.index != self.device):
+                raise ValueError(f"{which} {slot}: need a contiguous fp32 tensor of "
+                                 f"{self._numel(slot)} elements on cuda:{self.device}")
+            torch.cuda.current_stream(self.device).synchronize()  # values are written
+            N.check(N.lib().mmn_optim_set_state(self._h, slot, kind, values.data_ptr(),
+                                                N.MEM_DEVICE))
+            self.sync()
+            return
         v = np.ascontiguousarray(values, np.float32)
-        N.check(N.lib().mmn_optim_set_state(self._h, slot, {"m": 0, "v": 1, "velocity": 2}[which],
+        N.check(N.lib().mmn_optim_set_state(self._h, slot, kind,
                                             _host_ptr(v, self._numel(slot), 4, which, slot),
                                             N.MEM_HOST))
 

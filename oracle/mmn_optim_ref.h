@@ -44,7 +44,9 @@ enum {
     REF_NS_BF16 = 1,      /* fast variant (no reference counterpart): B rounded to bf16 */
     REF_NS_TF32 = 2,      /* TF32 mode (no reference counterpart): the REF_NS_REFERENCE
                              recipe with every bf16 rounding point of lib.rs:104,115,116,119
-                             replaced by a tf32 rounding (10-bit mantissa, nearest-even) */
+                             replaced by a tf32 rounding (10-bit mantissa, nearest-even),
+                             and the norm's sum of squares rounded to fp32 once, as in
+                             REF_NS_FP32 */
     REF_NS_FP32 = 3       /* fp32 mode (no reference counterpart): the same recipe with no
                              rounding points at all, every value kept in fp32, and the
                              norm's sum of squares rounded to fp32 once */
@@ -98,6 +100,9 @@ double ref_adamw_step_timed(float *p, float *m, float *v, const float *g, int64_
                             int n_threads);
 
 int ref_max_threads(void);
+
+/* ns_round of the variant (bf16, tf32 or none) over n elements; out may equal in. */
+void ref_ns_round_array(const float *in, float *out, int64_t n, int variant);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,11 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libmmn_optim_ref.so")
 
 GEMM_F32_SEQ, GEMM_F32_FMA, GEMM_F64 = 0, 1, 2
+# Newton-Schulz products formed by numpy's float64 matrix multiply (a BLAS
+# dgemm): the GEMM_F64 recipe (fp64 sums rounded once to fp32) with another
+# fp64 summation order, fast enough for the full-size matrices (4096 x 14336)
+# on the host cores. Only newton_schulz5 / ns_iteration accept it.
+GEMM_BLAS64 = 3
 NS_REFERENCE, NS_BF16, NS_TF32, NS_FP32 = 0, 1, 2, 3
 
 _f = ctypes.c_float
@@ -71,6 +76,7 @@ def lib():
         L.ref_bias_correction.argtypes = [_f, _i64]
         L.ref_grad_average.argtypes = [_fp, _fp, _i64, _i64]
         L.ref_max_threads.restype = ctypes.c_int
+        L.ref_ns_round_array.argtypes = [_fp, _fp, _i64, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -145,10 +151,63 @@ def pad_to_square(g: np.ndarray) -> np.ndarray:
     return out.reshape(side, side)
 
 
+_NS_A, _NS_B, _NS_C = np.float32(3.4445), np.float32(-4.7750), np.float32(2.0315)  # lib.rs:84-86
+_NS_EPS = np.float32(1e-7)  # lib.rs:87
+
+
+def _ns_round(x, variant):
+    """The rounding point of a Newton-Schulz variant (ns_round in mmn_optim_ref.c)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if variant == NS_FP32:
+        return x
+    out = np.empty_like(x)
+    lib().ref_ns_round_array(_ptr(x), _ptr(out), x.size, variant)
+    return out
+
+
+def _ns_iteration_blas64(x, variant):
+    """ref_ns_iteration (lib.rs:112-120) with the three products formed in float64
+    by numpy's matmul and rounded once to float32; the elementwise steps are the
+    same float32 operations in the same order."""
+    x64 = x.astype(np.float64)
+    a = _ns_round((x64 @ x64.T).astype(np.float32), variant)               # :114-115
+    a64 = a.astype(np.float64)
+    sq = _ns_round((a64 @ a64).astype(np.float32), variant)                # :116
+    b = a * _NS_B + sq * _NS_C                                              # :117
+    if variant == NS_BF16:
+        b = bf16_round(b)
+    del a, a64, sq
+    bx = (b.astype(np.float64) @ x64).astype(np.float32)
+    return _ns_round(x * _NS_A + bx, variant)                              # :118-119
+
+
+def _newton_schulz5_blas64(g2, steps, variant):
+    """ref_newton_schulz5 (lib.rs:101-126) with GEMM_BLAS64 products: transpose
+    when rows > cols, round, divide by the Frobenius norm (a sequential float32
+    sum of squares, as lib.rs:109; fp64 sum rounded once in NS_TF32 and NS_FP32), iterate,
+    transpose back."""
+    rows, cols = g2.shape
+    transposed = rows > cols
+    x = _ns_round(np.ascontiguousarray(g2.T if transposed else g2), variant)
+    if variant in (NS_FP32, NS_TF32):
+        s = np.float32(np.sum(np.square(x, dtype=np.float64)))
+    else:
+        s = np.cumsum((x * x).reshape(-1), dtype=np.float32)[-1]  # sequential, in order
+    norm = np.fmax(np.sqrt(np.float32(s)), _NS_EPS)  # f32::max: a NaN gives the other
+    x = (x / norm).astype(np.float32)
+    for _ in range(steps):
+        x = _ns_iteration_blas64(x, variant)
+    out = np.ascontiguousarray(x.T if transposed else x)
+    return out, float(norm)
+
+
 def newton_schulz5(g, steps=5, order=GEMM_F32_FMA, variant=NS_REFERENCE, threads=0,
                    return_norm=False):
     """newton_schulz5 (lib.rs:83-126). Output has the (padded) 2-D input shape."""
     g2 = pad_to_square(np.asarray(g, np.float32))
+    if order == GEMM_BLAS64:
+        out, nrm = _newton_schulz5_blas64(g2, steps, variant)
+        return (out, nrm) if return_norm else out
     rows, cols = g2.shape
     out = np.empty((rows, cols), np.float32)
     norm = _f(0.0)
@@ -159,6 +218,8 @@ def newton_schulz5(g, steps=5, order=GEMM_F32_FMA, variant=NS_REFERENCE, threads
 
 def ns_iteration(x, order=GEMM_F64, variant=NS_REFERENCE, threads=0):
     x = np.ascontiguousarray(x, np.float32)
+    if order == GEMM_BLAS64:
+        return _ns_iteration_blas64(x, variant)
     y = np.empty_like(x)
     lib().ref_ns_iteration(_ptr(x), x.shape[0], x.shape[1], _ptr(y), order, variant, threads)
     return y

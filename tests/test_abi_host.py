@@ -242,25 +242,3 @@ def _header_functions():
         args = m.group(2).strip()
         out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
     return out
-
-
-def test_integration_rust_block_matches_the_header():
-    """The Rust extern block a maintainer would add declares
-    only functions of the header, each with the header's parameter count, and
-    its constants carry the header's values."""
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    block = text[text.index('extern "C" {'):]
-    block = block[:block.index("\n}\n")]
-    header = _header_functions()
-    rust = {}
-    for m in re.finditer(r"pub fn (mmn_\w+)\(([^)]*)\)", block, flags=re.S):
-        args = m.group(2).strip()
-        rust[m.group(1)] = 0 if not args else args.count(":")
-    assert len(rust) >= 40
-    for name, n in rust.items():
-        assert name in header, name
-        assert n == header[name], (name, n, header[name])
-    hdr = open(os.path.join(ROOT, "include", "mmn_optim.h")).read()
-    defines = dict(re.findall(r"#define (MMN_\w+) \(?(-?\d+)\)?", hdr))
-    for name, value in re.findall(r"pub const (MMN_\w+): \w+ = (-?\d+);", text):
-        assert defines[name] == value, name

@@ -23,3 +23,6 @@ def test_reference_arm_prints_one_contract_line():
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+    # the value is an extrapolation from bounded samples, and the line says so
+    assert line["extrapolated"] is True and line["sample_ms_per_step"] > 0
+    assert line["cpu_baseline"]["single_thread"]["cores"] == 1

@@ -299,11 +299,12 @@ def _np_round(x, variant, oracle):
 def _np_newton_schulz5(g, steps, variant, oracle):
     """An independent numpy restatement of newton_schulz5 (lib.rs:83-126) with
     fp64 products rounded once to fp32, the rounding points of each variant,
-    and the reference's sequential fp32 norm (fp64 once for the fp32 mode)."""
+    and the reference's sequential fp32 norm (fp64 once for the TF32 and fp32
+    modes)."""
     f = np.float32
     tr = g.shape[0] > g.shape[1]
     x = _np_round(g.T if tr else g, variant, oracle).astype(f)
-    if variant == oracle.NS_FP32:
+    if variant in (oracle.NS_FP32, oracle.NS_TF32):
         s = f(np.sum(x.astype(np.float64) ** 2))
     else:
         s = f(0)
@@ -334,3 +335,25 @@ def test_oracle_ns_matches_independent_numpy_restatement(oracle, variant):
         got = oracle.newton_schulz5(g, 5, order=oracle.GEMM_F64, variant=variant)
         want = _np_newton_schulz5(g, 5, variant, oracle)
         np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32), err_msg=str(shape))
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+def test_blas64_products_equal_the_fp64_order(oracle, variant):
+    """GEMM_BLAS64 (numpy float64 matmul, used for the full-size Newton-Schulz
+    checks) against the oracle's own fp64 GEMM order: five iterations and one
+    iteration bit for bit, both orientations, K up to 1024. Two fp64 sums of
+    bf16 products differ by far less than an fp32 rounding step, so every
+    rounding point sees the same fp32 value."""
+    rng = np.random.default_rng(60 + variant)
+    for shape in ((64, 256), (300, 200), (256, 1024)):
+        g = rng.normal(0, 1e-2, shape).astype(np.float32)
+        a, na = oracle.newton_schulz5(g, 5, order=oracle.GEMM_F64, variant=variant,
+                                      return_norm=True)
+        b, nb = oracle.newton_schulz5(g, 5, order=oracle.GEMM_BLAS64, variant=variant,
+                                      return_norm=True)
+        assert na == nb
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32), err_msg=str(shape))
+        x = g if shape[0] <= shape[1] else np.ascontiguousarray(g.T)
+        x = (oracle._ns_round(x, variant) / np.float32(na)).astype(np.float32)
+        np.testing.assert_array_equal(oracle.ns_iteration(x, oracle.GEMM_F64, variant),
+                                      oracle.ns_iteration(x, oracle.GEMM_BLAS64, variant))

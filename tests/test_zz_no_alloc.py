@@ -3,11 +3,16 @@ cudaMalloc (device memory owned by another allocator or a fixed arena, hosts
 that forbid allocation after start-up, paths that cannot afford cudaMalloc's
 implicit synchronisation). Its scratch is a fixed array inside the library.
 
-Called through the C ABI on device buffers, twice in a row, and compared with
-the allocating entry point mmn_newton_schulz5 within the Newton-Schulz
-tolerance used elsewhere in the suite (2e-2 relative Frobenius; the two paths
-run the same kernels, so they normally agree exactly). This file is named to
-be collected last."""
+Called through the C ABI on device buffers, twice in a row per case, and
+compared with the allocating entry point mmn_newton_schulz5. Both run the same
+kernels on the same input, so the results must agree bit for bit; a scratch
+layout fault (a wrong X ping-pong buffer, overlapping partial sums or
+descriptors, a region left uncleared) would break that. Each case is also held
+to the oracle within the Newton-Schulz tolerance of the suite (2e-2 relative
+Frobenius). The cases cover zero and even step counts (the result then sits in
+the other X buffer, or comes straight from the normalised input), both
+orientations, both arithmetic modes and shapes at the ends of the fixed
+scratch. This file is named to be collected last."""
 import ctypes
 
 import numpy as np
@@ -32,23 +37,40 @@ def _run(fn_name, g, out, steps, mode):
     N.check(rc)
 
 
-@pytest.mark.parametrize("shape,mode", [((256, 1024), 0), ((1024, 256), 0), ((300, 200), 1),
-                                        ((1024, 1024), 0)])
-def test_noalloc_matches_allocating_entry_point(mmn, shape, mode):
+CASES = [
+    ((256, 1024), 0, 5),
+    ((1024, 256), 0, 5),
+    ((300, 200), 1, 5),
+    ((200, 300), 0, 0),
+    ((512, 128), 0, 4),
+    ((128, 512), 1, 4),
+    ((1024, 1024), 0, 5),   # largest square: min side at the limit
+    ((1023, 1025), 0, 5),   # padded strides, scratch nearly full
+    ((1, 1048576), 0, 5),   # rows * cols at the limit
+]
+
+
+@pytest.mark.parametrize("shape,mode,steps", CASES)
+def test_noalloc_matches_allocating_entry_point(mmn, oracle, shape, mode, steps):
     import torch
 
-    rng = np.random.default_rng(123)
+    rng = np.random.default_rng(123 + steps)
     for call in range(2):  # two calls in a row share the fixed scratch
-        g = torch.from_numpy(rng.normal(0, 1e-2, shape).astype(np.float32)).cuda()
+        g_host = rng.normal(0, 1e-2, shape).astype(np.float32)
+        g = torch.from_numpy(g_host).cuda()
         out_fixed = torch.full(shape, float("nan"), device="cuda")
         out_alloc = torch.empty(shape, device="cuda")
-        _run("noalloc", g, out_fixed, 5, mode)
-        _run("alloc", g, out_alloc, 5, mode)
+        _run("noalloc", g, out_fixed, steps, mode)
+        _run("alloc", g, out_alloc, steps, mode)
         torch.cuda.synchronize()
         a = out_fixed.cpu().numpy()
         b = out_alloc.cpu().numpy()
         assert np.isfinite(a).all(), call
-        assert rel_fro(a, b) <= 2e-2, call
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32), err_msg=str(call))
+        if call == 0:
+            variant = oracle.NS_BF16 if mode == 1 else oracle.NS_REFERENCE
+            ref = oracle.newton_schulz5(g_host, steps, order=oracle.GEMM_F64, variant=variant)
+            assert rel_fro(a, ref) <= 2e-2
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(mmn):
@@ -60,4 +82,6 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(mmn):
     assert rc == N.MMN_E_UNSUPPORTED
     assert b"1048576" in L.mmn_last_error()
     rc = L.mmn_newton_schulz5_noalloc(dummy, 1025, 1025, 5, 0, dummy, 0, None)
+    assert rc == N.MMN_E_UNSUPPORTED
+    rc = L.mmn_newton_schulz5_noalloc(dummy, 2, 1048577, 5, 0, dummy, 0, None)
     assert rc == N.MMN_E_UNSUPPORTED
