@@ -292,6 +292,9 @@ class GradAccumulator {
     }
     ++param_index_;
   }
+  // The plain sum of a tensor's grads (no reference counterpart): the batched
+  // GPU step takes the sum and the micro-batch count and divides itself.
+  const ArrayD& sum(size_t index) const { return grads_.at(index); }
   ArrayD averaged_grad(size_t index) const {
     const float n = (float)(micro_batches_ > 0 ? micro_batches_ : 1);
     ArrayD out = grads_.at(index);

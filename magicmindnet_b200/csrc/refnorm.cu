@@ -56,9 +56,9 @@
 namespace mmn {
 namespace {
 
-constexpr int kRnThreads = 512;
+constexpr int kRnThreads = 768;
 constexpr int kRnWarps = kRnThreads / 32;
-constexpr int kRnGroups = 4;                 // 16-byte groups (8 bf16) per thread per tile
+constexpr int kRnGroups = 3;                 // 16-byte groups (8 bf16) per thread per tile
 constexpr int kRnEpt = kRnGroups * 8;        // elements per thread per tile
 constexpr int kRnSat = 1 << 25;              // integers at or above 2^24 mean "left the binade"
 constexpr float kRnBig = 4194304.0f;         // 2^22: larger terms take the exact add
@@ -360,22 +360,23 @@ __device__ __forceinline__ RnMap rn_block_scan(RnMap m, RnShared& sh, RnMap* tot
   return r;
 }
 
-// The composed map of the run's elements from local index `start` on, and the
-// max of their k bit patterns.
+// The composed map of the run's elements and the max of their k bit patterns.
+// A pair without a tie (98% of pairs) adds its two values at once; the branch
+// is taken per pair.
 template <bool TINY>
-__device__ __forceinline__ RnMap rn_run_fold(const RnRun& r, const RnState& st, int start,
-                                             int base, uint32_t* kmax_out) {
+__device__ __forceinline__ RnMap rn_run_fold(const RnRun& r, const RnState& st,
+                                             uint32_t* kmax_out) {
   RnMap m{0, 0, 0};
   uint32_t kmax = 0;
 #pragma unroll
   for (int i = 0; i < kRnEpt / 2; ++i) {
     const RnPair p = rn_pair<TINY>(r.word(i), st);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      if (base + 2 * i + h >= start) {
-        kmax = max(kmax, p.kbits[h]);
-        rn_fold(m, p.val[h], p.tie[h], p.neg[h]);
-      }
+    kmax = max(kmax, max(p.kbits[0], p.kbits[1]));
+    if (!(p.tie[0] | p.tie[1])) {
+      m.A += p.val[0] + p.val[1];
+    } else {
+      rn_fold(m, p.val[0], p.tie[0], p.neg[0]);
+      rn_fold(m, p.val[1], p.tie[1], p.neg[1]);
     }
   }
   *kmax_out = kmax;
@@ -414,8 +415,7 @@ __device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& s
   // fast path: the composed map of the whole tile
   {
     uint32_t kmax;
-    const RnMap m = st.tiny ? rn_run_fold<true>(r, st, 0, base, &kmax)
-                            : rn_run_fold<false>(r, st, 0, base, &kmax);
+    const RnMap m = st.tiny ? rn_run_fold<true>(r, st, &kmax) : rn_run_fold<false>(r, st, &kmax);
     const RnMap tot = rn_block_reduce_fast(rn_fold_sat(m), kmax, sh, st.parity, &kmax);
     st.parity ^= 1;  // the next tile reduces through the other slots
     if (kmax < kRnBigBits) {
