@@ -195,6 +195,9 @@ struct mmn_optim {
   float* d_norms = nullptr;
   NsApply* d_apply = nullptr;   // per owned matrix, indexed like the norms
   std::vector<int64_t> chunk_begin, chunk_end;  // Muon arena range of every NS chunk
+  int norm_cluster = 1;                       // CTAs per matrix of the norm launch (all chunks)
+  int norm_scalar_rows = 0;                     // a matrix's oriented rows are not 8-element groups
+  std::vector<int> chunk_norm_cluster;          // the same for one chunk's launch
   std::vector<int> chunk_mat0, chunk_tile0;     // first matrix / 64x64 tile of every
                                                 // chunk (one past the end appended)
   std::vector<std::vector<int>> chunk_slots;    // slots of every chunk
@@ -504,6 +507,27 @@ static int finalize_layout(mmn_optim_t* h) {
   for (int64_t e : h->chunk_end) h->m_own_end = std::max(h->m_own_end, align_up(e, 64));
   h->chunk_mat0.push_back((int)h->mats.size());
   h->chunk_tile0.push_back(tiles);
+  {
+    // CTAs per matrix of the sequential-norm launches, over every chunk at
+    // once (device steps) and per chunk (steps from host memory)
+    auto elems = [&](const MuonMat& mm) { return (long long)mm.rows * mm.cols; };
+    long long mx = 0, tot = 0;
+    for (const MuonMat& mm : h->mats) {
+      mx = std::max(mx, elems(mm));
+      tot += elems(mm);
+      if (std::max(mm.rows, mm.cols) % 8 != 0) h->norm_scalar_rows = 1;
+    }
+    h->norm_cluster = ref_norm_cluster(mx, tot, (int)h->mats.size(), h->ctx.num_sms);
+    for (size_t k = 0; k + 1 < h->chunk_mat0.size(); ++k) {
+      long long cmx = 0, ctot = 0;
+      for (int i = h->chunk_mat0[k]; i < h->chunk_mat0[k + 1]; ++i) {
+        cmx = std::max(cmx, elems(h->mats[i]));
+        ctot += elems(h->mats[i]);
+      }
+      h->chunk_norm_cluster.push_back(
+          ref_norm_cluster(cmx, ctot, h->chunk_mat0[k + 1] - h->chunk_mat0[k], h->ctx.num_sms));
+    }
+  }
 
   // ---- AdamW parts over this rank's range: at most kChunkElems elements each,
   // and, when the range is large, a small first and last part (2^24 elements)
@@ -1028,6 +1052,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     m.apply_divides_norm = h->cfg.muon.ns_steps == 0;
     m.vec_ok = 1;  // arena bases come from cudaMalloc; offsets are 64-element aligned
     m.x_mode = h->cfg.ns_mode == MMN_NS_FP32 ? 2 : (h->cfg.ns_mode == MMN_NS_TF32 ? 1 : 0);
+    m.norm_scalar_rows = h->norm_scalar_rows;
     auto select = [&](size_t k) {
       m.mats = h->d_mats + h->chunk_mat0[k];
       m.nmat = h->chunk_mat0[k + 1] - h->chunk_mat0[k];
@@ -1041,7 +1066,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       select(k);
       m.cls = h->d_cls_in;
       launch_muon_momentum(m, h->ctx.num_sms, s);
-      if (norms) launch_muon_norms(m, s);
+      if (norms) launch_muon_norms(m, s, h->chunk_norm_cluster[k]);
       MMN_CUDA_TRY(cudaGetLastError());
       return MMN_OK;
     };
@@ -1091,7 +1116,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       m.tile_begin = 0;
       m.total_tiles = h->total_tiles;
       m.cls = h->d_cls_in;
-      launch_muon_norms(m, s);
+      launch_muon_norms(m, s, h->norm_cluster);
       MMN_CUDA_TRY(cudaGetLastError());
       if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[4], s));
       for (int k : h->jobs)

@@ -305,8 +305,10 @@ static int muon_run(mmn_muon* h, float* p, const float* g, float* vel, int rows,
   a.fresh_state = fresh;
   a.apply_divides_norm = steps == 0;
   a.x_mode = h->ns_mode == kNsFp32 ? 2 : (h->ns_mode == kNsTf32 ? 1 : 0);
+  a.norm_scalar_rows = (rows > cols ? rows : cols) % 8 != 0;
   launch_muon_momentum(a, h->ctx.num_sms, s);
-  launch_muon_norms(a, s);
+  const long long numel = (long long)rows * cols;
+  launch_muon_norms(a, s, ref_norm_cluster(numel, numel, 1, h->ctx.num_sms));
   MMN_CUDA_TRY(cudaGetLastError());
   std::string err;
   if (ns_class_run(*c, steps, h->ns_mode, h->ctx.status, h->ctx.num_sms, s, &err) < 0)

@@ -707,10 +707,10 @@ void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream) {
 #undef MMN_MOM
 }
 
-void launch_muon_norms(const MuonArgs& a, cudaStream_t stream) {
+void launch_muon_norms(const MuonArgs& a, cudaStream_t stream, int cluster) {
   if (a.nmat <= 0) return;
   if (a.x_mode == 0) {
-    launch_ref_norms(a, stream);
+    launch_ref_norms(a, cluster, stream);
     return;
   }
   muon_norm_kernel<<<a.nmat < 1024 ? a.nmat : 1024, 256, 0, stream>>>(a);

@@ -83,6 +83,8 @@ struct MuonArgs {
   int apply_divides_norm;  // zero Newton-Schulz steps: O = bf16(u) / norm (lib.rs:110)
   int vec_ok;              // p / g / vel bases are 16-byte aligned: matrices with
                            // cols % 4 == 0 and off % 4 == 0 take the 128-bit path
+  int norm_scalar_rows;    // some matrix has oriented rows that are not a multiple of
+                           // 8 elements (the norm launch adds its element-wise form)
   int x_mode;              // X storage: 0 bf16(u); 1 tf32(u) in fp32 words (TF32
                            // mode); 2 u as hi + lo tf32 planes (fp32 mode)
 };
@@ -93,8 +95,14 @@ void launch_muon_momentum(const MuonArgs& a, int num_sms, cudaStream_t stream);
 // reference and bf16 recipes; refnorm.cu), or the fixed-order sum of the
 // momentum kernel's tile partials (x_mode 1 and 2, the TF32 and fp32 modes,
 // which have no reference counterpart and aim at exact Newton-Schulz).
-void launch_muon_norms(const MuonArgs& a, cudaStream_t stream);
-void launch_ref_norms(const MuonArgs& a, cudaStream_t stream);
+// `cluster` CTAs (1, 2, 4 or 8; see ref_norm_cluster) share each matrix's
+// sequential sum.
+void launch_muon_norms(const MuonArgs& a, cudaStream_t stream, int cluster = 1);
+void launch_ref_norms(const MuonArgs& a, int cluster, cudaStream_t stream);
+// Cluster size for a launch whose largest matrix has max_elems elements out
+// of total_elems: large matrices are split until no CTA's share of the
+// sequential sum is much longer than an even spread over the SMs.
+int ref_norm_cluster(long long max_elems, long long total_elems, int nmat, int num_sms);
 void launch_muon_apply(const MuonArgs& a, int num_sms, cudaStream_t stream);
 
 // Non-finite scan of fp32 and bf16 grad arenas into *flag (flag must be zero).

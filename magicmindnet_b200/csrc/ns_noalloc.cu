@@ -171,8 +171,9 @@ extern "C" int mmn_newton_schulz5_noalloc(const float* g, int64_t rows, int64_t 
   a.grad_divisor = 1.0f;
   a.fresh_state = 1;
   a.apply_divides_norm = steps == 0;
+  a.norm_scalar_rows = m % 8 != 0;
   launch_muon_momentum(a, slot.num_sms, s);
-  launch_muon_norms(a, s);
+  launch_muon_norms(a, s, ref_norm_cluster(rows * cols, rows * cols, 1, slot.num_sms));
   MMN_CUDA_TRY(cudaGetLastError());
   if (ns_class_run(c, steps, ns_mode, status, slot.num_sms, s, &err) < 0)
     return fail(MMN_E_CUDA, err);

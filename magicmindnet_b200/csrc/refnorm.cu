@@ -48,6 +48,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cooperative_groups.h>
+
 #include <climits>
 #include <cstdint>
 
@@ -56,7 +58,7 @@
 namespace mmn {
 namespace {
 
-constexpr int kRnThreads = 768;
+constexpr int kRnThreads = 512;
 constexpr int kRnWarps = kRnThreads / 32;
 constexpr int kRnGroups = 3;                 // 16-byte groups (8 bf16) per thread per tile
 constexpr int kRnEpt = kRnGroups * 8;        // elements per thread per tile
@@ -409,8 +411,7 @@ __device__ __noinline__ RnMap rn_shared_fold(const RnShared& sh, const RnState& 
 // Runs the sequential sum over one tile (this thread's run r), starting from
 // `st`; returns false when the sum became non-finite (s_out holds it; the
 // caller finishes the NaN check).
-__device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& sh,
-                                        float& s_out) {
+__device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& sh, float& s_out) {
   const int base = threadIdx.x * kRnEpt;
   // fast path: the composed map of the whole tile
   {
@@ -485,48 +486,164 @@ __device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& s
   }
 }
 
-// The sequential sum over the whole oriented matrix X (n x m, row stride ld).
+// Cluster-level slots: one composed map per CTA and tile parity, and the
+// state a CTA publishes after walking its part of a slow tile.
+struct RnClusterSlots {
+  RnMap map[2];
+  uint32_t kmax[2];
+  RnMap all;        // the cluster tile's composed map (thread 0's result)
+  uint32_t all_kmax;
+  uint32_t pub_bits;  // running sum after this CTA's part of a slow tile
+  int pub_ok;         // 0: the sum became non-finite there
+};
+
+struct RnSlowResult {
+  RnState st;
+  float s_nf;  // the non-finite sum when ok is false
+  bool ok;
+};
+
+// A cluster tile that leaves the binade: the CTA parts one after another, each
+// from the state its predecessor published.
+__device__ __forceinline__ RnSlowResult rn_slow_cluster_tile(const RnRun& cur, RnState st,
+                                                             RnShared& sh, RnClusterSlots& cs,
+                                                             int C, int crank) {
+  namespace cg = cooperative_groups;
+  RnSlowResult res;
+  res.ok = true;
+  res.s_nf = 0.0f;
+  for (int r = 0; r < C; ++r) {
+    if (crank == r) {
+      float s_nf = 0.0f;
+      const bool ok = rn_tile(cur, st, sh, s_nf);
+      if (threadIdx.x == 0) {
+        cs.pub_ok = ok ? 1 : 0;
+        cs.pub_bits = ok ? __float_as_uint(rn_value(st, st.S)) : __float_as_uint(s_nf);
+      }
+    }
+    const RnClusterSlots* pub = &cs;
+    if (C > 1) {
+      cg::cluster_group cluster = cg::this_cluster();
+      cluster.sync();
+      pub = cluster.map_shared_rank(&cs, r);
+    } else {
+      __syncthreads();
+    }
+    const int ok = pub->pub_ok;
+    const float s = __uint_as_float(pub->pub_bits);
+    __syncthreads();
+    if (!ok) {
+      res.ok = false;
+      res.s_nf = s;
+      break;
+    }
+    rn_set(st, s);
+  }
+  res.st = st;
+  return res;
+}
+
+// The sequential sum over the whole oriented matrix X (n x m, row stride ld),
+// computed by the C CTAs of a cluster (C = 1: one CTA). A cluster tile is C
+// consecutive CTA tiles; CTA r folds the r-th. The CTAs exchange their
+// composed maps through distributed shared memory, and each composes all of
+// them in order, so every CTA holds the same running state. A cluster tile
+// whose composed map leaves the binade (or holds a term of 2^22 grid units or
+// more) is walked one CTA part after another, each part starting from the
+// state its predecessor published.
 template <bool VEC>
 __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, int m,
-                                               long long total, RnShared& sh) {
+                                               long long total, RnShared& sh,
+                                               RnClusterSlots& cs, int C, int crank) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   RnState st;
   rn_set(st, 0.0f);
   st.parity = 0;
   float s_nf = 0.0f;
-  long long done = -1;  // first element of the tile where the sum stopped being finite
+  long long done = -1;  // first element of the cluster tile where the sum stopped being finite
   constexpr long long kTileElems = (long long)kRnThreads * kRnEpt;
-  // this thread's run, advanced by one tile (d_rows rows + d_cols columns)
+  const long long step = kTileElems * C;
+  // this thread's run, advanced by one cluster tile (d_rows rows + d_cols
+  // columns) per step
   RnCursor c;
-  c.e = (long long)threadIdx.x * kRnEpt;
+  c.e = (long long)crank * kTileElems + (long long)threadIdx.x * kRnEpt;
   c.row = c.e / m;
   c.col = (int)(c.e - c.row * m);
-  const long long d_rows = kTileElems / m;
-  const int d_cols = (int)(kTileElems - d_rows * m);
+  const long long d_rows = step / m;
+  const int d_cols = (int)(step - d_rows * m);
   RnRun cur, nxt;
   if (VEC)
     rn_load_vec(cur, X, ld, m, total, c);
   else
     rn_load_scalar(cur, X, ld, m, total, c);
-  for (long long e0 = 0; e0 < total; e0 += kTileElems) {
-    c.e += kTileElems;
+  int cp = 0;
+  for (long long e0 = 0; e0 < total; e0 += step) {
+    c.e += step;
     c.row += d_rows;
     c.col += d_cols;
     if (c.col >= m) {
       c.col -= m;
       ++c.row;
     }
-    if (e0 + kTileElems < total) {  // the next tile's loads fly while this one folds
-      if (VEC)
-        rn_load_vec(nxt, X, ld, m, total, c);
-      else
-        rn_load_scalar(nxt, X, ld, m, total, c);
+    // the next cluster tile's loads fly while this one folds; a part past the
+    // end of the matrix reads as zeros (the loads check every group)
+    if (VEC)
+      rn_load_vec(nxt, X, ld, m, total, c);
+    else
+      rn_load_scalar(nxt, X, ld, m, total, c);
+    // every CTA folds its tile; the cluster composes the C results in order
+    {
+      uint32_t kmax;
+      const RnMap mm = st.tiny ? rn_run_fold<true>(cur, st, &kmax) : rn_run_fold<false>(cur, st, &kmax);
+      const RnMap tot = rn_block_reduce_fast(rn_fold_sat(mm), kmax, sh, st.parity, &kmax);
+      st.parity ^= 1;
+      RnMap all = tot;
+      uint32_t all_kmax = kmax;
+      if (C > 1) {
+        if (threadIdx.x == 0) {
+          cs.map[cp] = tot;
+          cs.kmax[cp] = kmax;
+        }
+        cluster.sync();
+        if (threadIdx.x == 0) {
+          RnMap t{0, 0, 0};
+          uint32_t km = 0;
+          for (int r = 0; r < C; ++r) {
+            const RnClusterSlots* rem = cluster.map_shared_rank(&cs, r);
+            t = rn_compose(t, rem->map[cp]);
+            km = max(km, rem->kmax[cp]);
+          }
+          cs.all = t;
+          cs.all_kmax = km;
+        }
+        __syncthreads();
+        all = cs.all;
+        all_kmax = cs.all_kmax;
+        __syncthreads();
+        cp ^= 1;
+      }
+      if (all_kmax < kRnBigBits) {
+        const int s_end = rn_apply(all, st.S);
+        if (s_end <= (1 << 24) - 1) {
+          st.S = s_end;
+          cur = nxt;
+          continue;
+        }
+      }
     }
-    if (!rn_tile(cur, st, sh, s_nf)) {
+    // slow: the parts in order, each from its predecessor's published state
+    const RnSlowResult res = rn_slow_cluster_tile(cur, st, sh, cs, C, crank);
+    st = res.st;
+    if (!res.ok) {
+      s_nf = res.s_nf;
       done = e0;
       break;
     }
     cur = nxt;
   }
+  // the cluster's CTAs stay resident until every remote read is done
+  if (C > 1) cluster.sync();
   if (done < 0) return rn_value(st, st.S);
   if (isnan(s_nf)) return s_nf;
   // +inf reached: adding the remaining terms keeps it, unless one is NaN
@@ -538,33 +655,65 @@ __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, i
   return __syncthreads_or(nan) ? __int_as_float(0x7fffffff) : s_nf;
 }
 
-__global__ void __launch_bounds__(kRnThreads) refnorm_kernel(const MuonArgs a) {
+// One cluster of C CTAs per matrix (grid = clusters x C), the clusters striding
+// over the launch's matrices. VEC: the matrices whose rows hold whole 16-byte
+// groups (16-byte loads; rows start 16-byte aligned since the class row stride
+// is a multiple of 8 elements); otherwise the others, element by element.
+template <bool VEC>
+__global__ void __launch_bounds__(kRnThreads) refnorm_kernel(const MuonArgs a, int C) {
   __shared__ RnShared sh;
+  __shared__ RnClusterSlots cs;
   if (a.skip && *a.skip) return;
-  for (int k = blockIdx.x; k < a.nmat; k += gridDim.x) {
+  const int crank = C > 1 ? (int)cooperative_groups::this_cluster().block_rank() : 0;
+  const int nclusters = gridDim.x / C;
+  for (int k = blockIdx.x / C; k < a.nmat; k += nclusters) {
     const MuonMat mm = a.mats[k];
     const MuonClassPtr cp = a.cls[mm.xcls];
     const __nv_bfloat16* X =
         static_cast<const __nv_bfloat16*>(cp.x) + (long long)mm.xbatch * cp.bstride;
     const int n = mm.transposed ? mm.cols : mm.rows;
     const int m = mm.transposed ? mm.rows : mm.cols;
-    // 16-byte loads when every row holds whole groups (rows start 16-byte
-    // aligned: the class row stride is a multiple of 8 elements)
-    const float s = (m % 8 == 0) ? rn_matrix_sum<true>(X, cp.ld, m, (long long)n * m, sh)
-                                 : rn_matrix_sum<false>(X, cp.ld, m, (long long)n * m, sh);
-    if (threadIdx.x == 0) a.norms[mm.norm_idx] = fmaxf(__fsqrt_rn(s), 1e-7f);  // lib.rs:109
+    if ((m % 8 == 0) != VEC) continue;  // the other instantiation's matrix
+    const float s = rn_matrix_sum<VEC>(X, cp.ld, m, (long long)n * m, sh, cs, C, crank);
+    if (crank == 0 && threadIdx.x == 0)
+      a.norms[mm.norm_idx] = fmaxf(__fsqrt_rn(s), 1e-7f);  // lib.rs:109
     __syncthreads();
   }
 }
 
 }  // namespace
 
-void launch_ref_norms(const MuonArgs& a, cudaStream_t stream) {
+int ref_norm_cluster(long long max_elems, long long total_elems, int nmat, int num_sms) {
+  // Split the largest matrix until its share is no larger than 1.5 times an
+  // even spread of all the launch's elements over the SMs (at most 8 CTAs,
+  // the portable cluster size): the long sequential sums then no longer set
+  // the launch's length.
+  const long long even = total_elems / (num_sms > 0 ? num_sms : 1) + 1;
+  int c = 1;
+  while (c < 8 && max_elems / c > even + even / 2) c *= 2;
+  (void)nmat;
+  return c;
+}
+
+void launch_ref_norms(const MuonArgs& a, int cluster, cudaStream_t stream) {
   if (a.nmat <= 0) return;
-  // one CTA per matrix (matrices come largest first), all in one wave where
-  // they fit; the grid-stride loop covers the rest
-  const int grid = a.nmat < 4096 ? a.nmat : 4096;
-  refnorm_kernel<<<grid, kRnThreads, 0, stream>>>(a);
+  const int C = cluster == 2 || cluster == 4 || cluster == 8 ? cluster : 1;
+  // clusters stride over the matrices (largest first)
+  const int clusters = a.nmat < 4096 ? a.nmat : 4096;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(clusters * C));
+  cfg.blockDim = dim3(kRnThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, refnorm_kernel<true>, a, C);
+  if (a.norm_scalar_rows) cudaLaunchKernelEx(&cfg, refnorm_kernel<false>, a, C);
 }
 
 }  // namespace mmn
