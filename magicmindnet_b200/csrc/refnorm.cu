@@ -486,164 +486,240 @@ __device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& s
   }
 }
 
-// Cluster-level slots: one composed map per CTA and tile parity, and the
-// state a CTA publishes after walking its part of a slow tile.
+// Cluster-level slots: one composed map per CTA and exchange parity, and the
+// state a CTA publishes after walking its part of a slow cluster step.
+constexpr int kRnTilesPerExchange = 8;  // CTA tiles folded between cluster exchanges
+
 struct RnClusterSlots {
   RnMap map[2];
   uint32_t kmax[2];
-  RnMap all;        // the cluster tile's composed map (thread 0's result)
+  RnMap all;        // the cluster step's composed map (thread 0's result)
   uint32_t all_kmax;
-  uint32_t pub_bits;  // running sum after this CTA's part of a slow tile
+  RnMap tmap[kRnTilesPerExchange];    // this CTA's tile maps of the current step
+  uint32_t tkmax[kRnTilesPerExchange];
+  int bad;            // first tile of this CTA's part whose adds leave the binade
+  int bad_S;          // the running sum (grid units) at that tile's start
+  int first_bad;      // the cluster's first such tile (thread 0's result)
+  uint32_t pub_bits;  // running sum after the exactly walked tile
   int pub_ok;         // 0: the sum became non-finite there
 };
 
-struct RnSlowResult {
-  RnState st;
-  float s_nf;  // the non-finite sum when ok is false
-  bool ok;
-};
+template <bool VEC>
+__device__ __forceinline__ void rn_load(RnRun& r, const __nv_bfloat16* X, int ld, int m,
+                                        long long total, const RnCursor& c) {
+  if (VEC)
+    rn_load_vec(r, X, ld, m, total, c);
+  else
+    rn_load_scalar(r, X, ld, m, total, c);
+}
 
-// A cluster tile that leaves the binade: the CTA parts one after another, each
+__device__ __forceinline__ RnCursor rn_cursor_at(long long e, int m) {
+  RnCursor c;
+  c.e = e;
+  c.row = e / m;
+  c.col = (int)(e - c.row * m);
+  return c;
+}
+
+__device__ __forceinline__ void rn_advance(RnCursor& c, long long d, long long d_rows, int d_cols,
+                                           int m) {
+  c.e += d;
+  c.row += d_rows;
+  c.col += d_cols;
+  if (c.col >= m) {
+    c.col -= m;
+    ++c.row;
+  }
+}
+
+// The sequential sum over the whole oriented matrix X (n x m, row stride ld),
+// computed by the C CTAs of a cluster (C = 1: one CTA). A cluster step is C
+// parts of up to K = kRnTilesPerExchange consecutive CTA tiles; CTA r folds
+// the r-th part, composing its tiles' maps in order. The CTAs then exchange their
+// parts' maps through distributed shared memory, and each composes all of
+// them in order, so every CTA holds the same running state. A cluster step
+// whose composed map leaves the binade (or holds a term of 2^22 grid units or
+// more) is walked part after part and tile after tile, each part starting
 // from the state its predecessor published.
-__device__ __forceinline__ RnSlowResult rn_slow_cluster_tile(const RnRun& cur, RnState st,
-                                                             RnShared& sh, RnClusterSlots& cs,
-                                                             int C, int crank) {
+template <bool VEC>
+__device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, int m,
+                                               long long total, RnShared& sh,
+                                               RnClusterSlots& cs, int C, int crank) {
   namespace cg = cooperative_groups;
-  RnSlowResult res;
-  res.ok = true;
-  res.s_nf = 0.0f;
-  for (int r = 0; r < C; ++r) {
-    if (crank == r) {
-      float s_nf = 0.0f;
-      const bool ok = rn_tile(cur, st, sh, s_nf);
+  constexpr int K = kRnTilesPerExchange;
+  constexpr long long T = (long long)kRnThreads * kRnEpt;  // elements per CTA tile
+  RnState st;
+  rn_set(st, 0.0f);
+  st.parity = 0;
+  float s_nf = 0.0f;
+  long long done = -1;  // first element of the cluster step where the sum stopped being finite
+  const long long own = (long long)threadIdx.x * kRnEpt;
+  // Tiles per part: a restart refolds at most one cluster step, and early on
+  // the sum changes binade whenever it doubles, so parts grow with the
+  // distance covered (one tile at first, K once the sum is past C K tiles).
+  auto tiles_at = [&](long long e) {
+    const long long k = e / (T * C);
+    return (int)(k < 1 ? 1 : (k > K ? K : k));
+  };
+  // this thread's run: one tile further (T) inside the part
+  const long long t_rows = T / m;
+  const int t_cols = (int)(T - t_rows * m);
+  long long e0 = 0;
+  int kt = tiles_at(0);
+  RnCursor c = rn_cursor_at((long long)crank * kt * T + own, m);
+  RnRun cur, nxt;
+  rn_load<VEC>(cur, X, ld, m, total, c);
+  int cp = 0;
+  while (e0 < total) {
+    const long long part = kt * T, step = part * C;
+    const long long part0 = e0 + (long long)crank * part;  // this CTA's part
+    const int kt_next = tiles_at(e0 + step);
+    RnMap acc{0, 0, 0};
+    uint32_t kacc = 0;
+    for (int j = 0; j < kt; ++j) {
+      // the next tile's loads fly while this one folds (zeros past the end)
+      if (j + 1 < kt)
+        rn_advance(c, T, t_rows, t_cols, m);
+      else
+        c = rn_cursor_at(e0 + step + (long long)crank * kt_next * T + own, m);
+      rn_load<VEC>(nxt, X, ld, m, total, c);
+      RnMap tot{0, 0, 0};
+      uint32_t kmax = 0;
+      if (part0 + j * T < total) {  // a tile past the end adds nothing
+        const RnMap mm =
+            st.tiny ? rn_run_fold<true>(cur, st, &kmax) : rn_run_fold<false>(cur, st, &kmax);
+        tot = rn_block_reduce_fast(rn_fold_sat(mm), kmax, sh, st.parity, &kmax);
+        st.parity ^= 1;
+        acc = rn_compose(acc, tot);
+        kacc = max(kacc, kmax);
+      }
+      if (threadIdx.x == 0) {
+        cs.tmap[j] = tot;
+        cs.tkmax[j] = kmax;
+      }
+      cur = nxt;
+    }
+    RnMap all = acc;
+    uint32_t all_kmax = kacc;
+    const int cp_step = cp;
+    if (C > 1) {
+      cg::cluster_group cluster = cg::this_cluster();
+      if (threadIdx.x == 0) {
+        cs.map[cp] = acc;
+        cs.kmax[cp] = kacc;
+      }
+      cluster.sync();
+      if (threadIdx.x == 0) {
+        RnMap t{0, 0, 0};
+        uint32_t km = 0;
+        for (int r = 0; r < C; ++r) {
+          const RnClusterSlots* rem = cluster.map_shared_rank(&cs, r);
+          t = rn_compose(t, rem->map[cp]);
+          km = max(km, rem->kmax[cp]);
+        }
+        cs.all = t;
+        cs.all_kmax = km;
+      }
+      __syncthreads();
+      all = cs.all;
+      all_kmax = cs.all_kmax;
+      __syncthreads();
+      cp ^= 1;
+    }
+    if (all_kmax < kRnBigBits) {
+      const int s_end = rn_apply(all, st.S);
+      if (s_end <= (1 << 24) - 1) {
+        st.S = s_end;
+        e0 += step;
+        kt = kt_next;
+        continue;
+      }
+    }
+    // slow: find the cluster's first tile whose adds leave the binade (or hold
+    // a term of 2^22 units or more), walk that tile exactly, and restart the
+    // cluster step after it (the tiles behind it were folded for the old
+    // binade). Each CTA starts from the composed maps of the parts before its
+    // own and applies its tile maps in order.
+    if (threadIdx.x == 0) {
+      RnMap pre{0, 0, 0};
+      if (C > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        for (int r = 0; r < crank; ++r)
+          pre = rn_compose(pre, cluster.map_shared_rank(&cs, r)->map[cp_step]);
+      }
+      int S = rn_apply(pre, st.S);
+      int bad = INT_MAX;
+      for (int j = 0; j < kt; ++j) {
+        if (part0 + j * T >= total) break;
+        const int next = cs.tkmax[j] >= kRnBigBits ? (1 << 24) : rn_apply(cs.tmap[j], S);
+        if (next >= (1 << 24)) {
+          bad = crank * kt + j;
+          break;
+        }
+        S = next;
+      }
+      cs.bad = bad;
+      cs.bad_S = S;
+    }
+    int first = INT_MAX;
+    if (C > 1) {
+      cg::cluster_group cluster = cg::this_cluster();
+      cluster.sync();
+      if (threadIdx.x == 0) {
+        int b = INT_MAX;
+        for (int r = 0; r < C; ++r) b = min(b, cluster.map_shared_rank(&cs, r)->bad);
+        cs.first_bad = b;
+      }
+      __syncthreads();
+      first = cs.first_bad;
+    } else {
+      __syncthreads();
+      first = cs.bad;
+    }
+    if (first == INT_MAX) first = C * kt - 1;  // not expected: the composed check failed
+    const int r_bad = first / kt, j_bad = first % kt;
+    const long long t_bad = e0 + (long long)r_bad * part + (long long)j_bad * T;
+    if (crank == r_bad) {
+      RnState sb = st;
+      sb.S = cs.bad_S;
+      RnRun tile;
+      rn_load<VEC>(tile, X, ld, m, total, rn_cursor_at(t_bad + own, m));
+      float snf = 0.0f;
+      const bool ok = rn_tile(tile, sb, sh, snf);
+      st.parity = sb.parity;
       if (threadIdx.x == 0) {
         cs.pub_ok = ok ? 1 : 0;
-        cs.pub_bits = ok ? __float_as_uint(rn_value(st, st.S)) : __float_as_uint(s_nf);
+        cs.pub_bits = ok ? __float_as_uint(rn_value(sb, sb.S)) : __float_as_uint(snf);
       }
     }
     const RnClusterSlots* pub = &cs;
     if (C > 1) {
       cg::cluster_group cluster = cg::this_cluster();
       cluster.sync();
-      pub = cluster.map_shared_rank(&cs, r);
+      pub = cluster.map_shared_rank(&cs, r_bad);
     } else {
       __syncthreads();
     }
     const int ok = pub->pub_ok;
-    const float s = __uint_as_float(pub->pub_bits);
-    __syncthreads();
-    if (!ok) {
-      res.ok = false;
-      res.s_nf = s;
-      break;
-    }
-    rn_set(st, s);
-  }
-  res.st = st;
-  return res;
-}
-
-// The sequential sum over the whole oriented matrix X (n x m, row stride ld),
-// computed by the C CTAs of a cluster (C = 1: one CTA). A cluster tile is C
-// consecutive CTA tiles; CTA r folds the r-th. The CTAs exchange their
-// composed maps through distributed shared memory, and each composes all of
-// them in order, so every CTA holds the same running state. A cluster tile
-// whose composed map leaves the binade (or holds a term of 2^22 grid units or
-// more) is walked one CTA part after another, each part starting from the
-// state its predecessor published.
-template <bool VEC>
-__device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, int m,
-                                               long long total, RnShared& sh,
-                                               RnClusterSlots& cs, int C, int crank) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  RnState st;
-  rn_set(st, 0.0f);
-  st.parity = 0;
-  float s_nf = 0.0f;
-  long long done = -1;  // first element of the cluster tile where the sum stopped being finite
-  constexpr long long kTileElems = (long long)kRnThreads * kRnEpt;
-  const long long step = kTileElems * C;
-  // this thread's run, advanced by one cluster tile (d_rows rows + d_cols
-  // columns) per step
-  RnCursor c;
-  c.e = (long long)crank * kTileElems + (long long)threadIdx.x * kRnEpt;
-  c.row = c.e / m;
-  c.col = (int)(c.e - c.row * m);
-  const long long d_rows = step / m;
-  const int d_cols = (int)(step - d_rows * m);
-  RnRun cur, nxt;
-  if (VEC)
-    rn_load_vec(cur, X, ld, m, total, c);
-  else
-    rn_load_scalar(cur, X, ld, m, total, c);
-  int cp = 0;
-  for (long long e0 = 0; e0 < total; e0 += step) {
-    c.e += step;
-    c.row += d_rows;
-    c.col += d_cols;
-    if (c.col >= m) {
-      c.col -= m;
-      ++c.row;
-    }
-    // the next cluster tile's loads fly while this one folds; a part past the
-    // end of the matrix reads as zeros (the loads check every group)
-    if (VEC)
-      rn_load_vec(nxt, X, ld, m, total, c);
+    const float sv = __uint_as_float(pub->pub_bits);
+    // every read of this step's slots precedes the next step's writes
+    if (C > 1)
+      cg::this_cluster().sync();
     else
-      rn_load_scalar(nxt, X, ld, m, total, c);
-    // every CTA folds its tile; the cluster composes the C results in order
-    {
-      uint32_t kmax;
-      const RnMap mm = st.tiny ? rn_run_fold<true>(cur, st, &kmax) : rn_run_fold<false>(cur, st, &kmax);
-      const RnMap tot = rn_block_reduce_fast(rn_fold_sat(mm), kmax, sh, st.parity, &kmax);
-      st.parity ^= 1;
-      RnMap all = tot;
-      uint32_t all_kmax = kmax;
-      if (C > 1) {
-        if (threadIdx.x == 0) {
-          cs.map[cp] = tot;
-          cs.kmax[cp] = kmax;
-        }
-        cluster.sync();
-        if (threadIdx.x == 0) {
-          RnMap t{0, 0, 0};
-          uint32_t km = 0;
-          for (int r = 0; r < C; ++r) {
-            const RnClusterSlots* rem = cluster.map_shared_rank(&cs, r);
-            t = rn_compose(t, rem->map[cp]);
-            km = max(km, rem->kmax[cp]);
-          }
-          cs.all = t;
-          cs.all_kmax = km;
-        }
-        __syncthreads();
-        all = cs.all;
-        all_kmax = cs.all_kmax;
-        __syncthreads();
-        cp ^= 1;
-      }
-      if (all_kmax < kRnBigBits) {
-        const int s_end = rn_apply(all, st.S);
-        if (s_end <= (1 << 24) - 1) {
-          st.S = s_end;
-          cur = nxt;
-          continue;
-        }
-      }
-    }
-    // slow: the parts in order, each from its predecessor's published state
-    const RnSlowResult res = rn_slow_cluster_tile(cur, st, sh, cs, C, crank);
-    st = res.st;
-    if (!res.ok) {
-      s_nf = res.s_nf;
-      done = e0;
+      __syncthreads();
+    if (!ok) {
+      s_nf = sv;
+      done = t_bad;
       break;
     }
-    cur = nxt;
+    rn_set(st, sv);
+    e0 = t_bad + T;
+    kt = tiles_at(e0);
+    c = rn_cursor_at(e0 + (long long)crank * kt * T + own, m);
+    rn_load<VEC>(cur, X, ld, m, total, c);
   }
   // the cluster's CTAs stay resident until every remote read is done
-  if (C > 1) cluster.sync();
+  if (C > 1) cg::this_cluster().sync();
   if (done < 0) return rn_value(st, st.S);
   if (isnan(s_nf)) return s_nf;
   // +inf reached: adding the remaining terms keeps it, unless one is NaN
