@@ -380,6 +380,27 @@ class LossScaleState:
             self.good = 0
 
 
+def grad_allreduce(local_grads, bf16=False) -> np.ndarray:
+    """Data-parallel grad reduction before the step. NEW BEHAVIOUR with no
+    reference counterpart (the reference trains in one process), defined here so
+    the multi-GPU path has something to be checked against:
+      * the ranks' local grads are summed in rank order in fp32: s = g_0, then
+        s = s + g_r for r = 1 .. W-1, each add rounded to nearest even;
+      * bf16 grads are widened to fp32 exactly, summed that way and rounded to
+        bf16 once (round to nearest even).
+    local_grads: one float32 array per rank (bf16 grads as their float32
+    values). Returns the sum as float32 (bf16-rounded values when bf16)."""
+    s = np.asarray(local_grads[0], np.float32).copy()
+    for g in local_grads[1:]:
+        np.add(s, np.asarray(g, np.float32), out=s)
+    return bf16_round(s) if bf16 else s
+
+
+def bf16_from_bits(bits) -> np.ndarray:
+    """float32 values of bf16 bit patterns (uint16 or int16 arrays)."""
+    return (np.asarray(bits).view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
 def bf16_bits(x) -> np.ndarray:
     """uint16 bit patterns of bf16(x) (round to nearest even)."""
     return (bf16_round(x).view(np.uint32) >> 16).astype(np.uint16)

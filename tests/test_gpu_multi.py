@@ -210,6 +210,50 @@ def _local_grads(model, world, bf16):
     return per_rank, sums
 
 
+def _host_values(t):
+    """float32 host values of a device grad (bf16 widened exactly)."""
+    import torch
+
+    if t.dtype == torch.bfloat16:
+        from oracle import reference_optim as R
+
+        return R.bf16_from_bits(t.view(torch.int16).cpu().numpy())
+    return t.cpu().numpy()
+
+
+def _check_reduced_against_oracle(step, model, world, rank, per_rank, bf16):
+    """The parts this rank steps (its Muon matrices, its range of the AdamW
+    arena) must hold the oracle's rank-ordered sum of every rank's local grads,
+    bit for bit. Returns the number of elements compared."""
+    import torch
+
+    import magicmindnet_b200 as mmn
+    from oracle import reference_optim as R
+
+    plan = mmn.shard_plan(model, world)
+    lo, hi = rank * plan["adamw_region"], (rank + 1) * plan["adamw_region"]
+    torch.cuda.synchronize()
+    checked = 0
+    for k, (_, s, _) in enumerate(model):
+        n = int(np.prod(s))
+        if plan["owner"][k] == rank:
+            a, b = 0, n
+        elif plan["owner"][k] == -1:
+            a = min(max(lo - plan["offset"][k], 0), n)
+            b = min(max(hi - plan["offset"][k], 0), n)
+        else:
+            continue
+        if a == b:
+            continue
+        got = _host_values(step.grad(k).reshape(-1)[a:b])
+        want = R.grad_allreduce([_host_values(g.reshape(-1)[a:b]) for g in
+                                 (per_rank[r][k] for r in range(world))], bf16)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32),
+                                      err_msg=f"rank {rank} slot {k} [{a}:{b}]")
+        checked += b - a
+    return checked
+
+
 def _reduce_cfg(mmn, bf16, **kw):
     if bf16:
         return mmn.StepConfig(grad_dtype="bf16", loss_scaling=True, loss_scale_init=1024.0,
@@ -244,6 +288,7 @@ def _reduce_worker(rank, world, port, q, bf16):
             step.grad(k).copy_(per_rank[rank][k])
         step.connect_peers()
         step.reduce_grads()
+        checked = _check_reduced_against_oracle(step, model, world, rank, per_rank, bf16)
         step.step()
         step.exchange_fence()
         out = [step.param(k).cpu().numpy().copy() for k in range(len(model))]
@@ -265,7 +310,7 @@ def _reduce_worker(rank, world, port, q, bf16):
             same = all(torch.equal(step.param(k), before[k]) for k in range(len(model)))
             skipped = (same, step.loss_scale())
         step.sync()
-        q.put((rank, out, skipped))
+        q.put((rank, out, (skipped, checked)))
         step.close()
     except Exception as e:  # reported to the parent, which fails at once
         q.put((rank, f"{type(e).__name__}: {e}", None))
@@ -281,7 +326,9 @@ def test_reduced_grads_step_equals_single_gpu_on_summed_grads(mmn, bf16):
     shard and pushes it to the peers. Every rank's parameters must equal, bit
     for bit, one GPU stepping the rank-ordered sum of the grads. With bf16 grads
     and loss scaling, a +inf in one rank's local grads skips the step on every
-    rank and halves every rank's scale."""
+    rank and halves every rank's scale. Before the step, each rank's reduced
+    parts are compared with the oracle's rank-ordered sum (grad_allreduce) bit
+    for bit."""
     import torch
     import torch.multiprocessing as mp
 
@@ -316,8 +363,11 @@ def test_reduced_grads_step_equals_single_gpu_on_summed_grads(mmn, bf16):
         got[r] = (out, skipped)
     for p in procs:
         p.join(timeout=120)
-    for r, (out, skipped) in got.items():
+    checked = 0
+    for r, (out, extra) in got.items():
         assert not isinstance(out, str), (r, out)
+        skipped, n = extra
+        checked += n
         for k, (a, b) in enumerate(zip(out, want)):
             np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32),
                                           err_msg=f"rank {r} slot {k}")
@@ -325,6 +375,8 @@ def test_reduced_grads_step_equals_single_gpu_on_summed_grads(mmn, bf16):
             same, (scale, nskip) = skipped
             assert same, r
             assert (scale, nskip) == (scale0 / 2, 1), r
+    # the ranks' reduced parts, each equal to the oracle's sum, cover every grad
+    assert checked == sum(int(np.prod(s)) for _, s, _ in model)
     for p in procs:
         assert p.exitcode == 0
 

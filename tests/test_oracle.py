@@ -357,3 +357,37 @@ def test_blas64_products_equal_the_fp64_order(oracle, variant):
         x = (oracle._ns_round(x, variant) / np.float32(na)).astype(np.float32)
         np.testing.assert_array_equal(oracle.ns_iteration(x, oracle.GEMM_F64, variant),
                                       oracle.ns_iteration(x, oracle.GEMM_BLAS64, variant))
+
+
+def test_grad_allreduce_is_the_rank_ordered_fp32_sum(oracle):
+    """The data-parallel reduction the multi-GPU path is checked against: per
+    element, a float32 running sum in rank order (a scalar restatement here),
+    bf16 grads rounded once at the end, non-finite values propagated. The order
+    matters: three ranks with a cancelling pair give another result reversed."""
+    rng = np.random.default_rng(70)
+    world = 3
+    locs = [rng.normal(0, 1e-3, 97).astype(np.float32) for _ in range(world)]
+    locs[0][5], locs[1][5], locs[2][5] = np.float32(1e8), np.float32(-1e8), np.float32(3.0)
+    locs[1][9] = np.inf
+    locs[2][11] = np.nan
+    got = oracle.grad_allreduce(locs)
+    for i in range(97):
+        s = np.float32(locs[0][i])
+        for r in range(1, world):
+            s = np.float32(s + locs[r][i])
+        assert got[i].view(np.uint32) == s.view(np.uint32) or (np.isnan(got[i]) and np.isnan(s)), i
+    assert got[5] == 3.0 and oracle.grad_allreduce(locs[::-1])[5] == 0.0
+    assert np.isposinf(got[9]) and np.isnan(got[11])
+    # bf16: widen, sum in fp32, round once (not after every add)
+    b = [oracle.bf16_round(x * np.float32(1024.0)) for x in locs]
+    got16 = oracle.grad_allreduce(b, bf16=True)
+    np.testing.assert_array_equal(got16.view(np.uint32),
+                                  oracle.bf16_round(oracle.grad_allreduce(b)).view(np.uint32))
+    step = b[0]
+    for x in b[1:]:
+        step = oracle.bf16_round(step + x)
+    assert (oracle.bf16_round(oracle.grad_allreduce(b)) != step)[np.isfinite(step)].any()
+    # bf16 bit patterns read back as float32 values
+    bits = oracle.bf16_bits(b[0])
+    np.testing.assert_array_equal(oracle.bf16_from_bits(bits).view(np.uint32),
+                                  b[0].view(np.uint32))
