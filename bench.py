@@ -429,7 +429,8 @@ def isolated_kernels(dev, pk, pk_kind, ns_modes=("reference", "tf32")):
         ms, ph, flops = timed("ns_batch", mmn.StepConfig(ns_mode=mode, use_graph=True), 1.0)
         tf = flops / (ph["newton_schulz"] / 1e3) / 1e12
         out[f"ns_batch_{mode}"] = {"ns_ms": ph["newton_schulz"], "step_ms": ms,
-                                   "momentum_ms": ph["muon_momentum"], "flops": flops,
+                                   "momentum_ms": ph["muon_momentum"],
+                                   "norm_ms": ph["muon_norm"], "flops": flops,
                                    "TFLOP/s": tf, "peak": peak, "frac": tf / peak,
                                    "peak_source": src}
     return out
@@ -709,7 +710,11 @@ def run_ours(args, rank, world, local_rank):
         "newton_schulz": {"ms": med["newton_schulz"], "flops": ns_flops,
                           "TFLOP/s": (ns_flops / (med["newton_schulz"] / 1e3) / 1e12)
                           if med["newton_schulz"] else None},
-        "muon_momentum_ms": med["muon_momentum"], "muon_update_ms": med["muon_update"],
+        "muon_momentum_ms": med["muon_momentum"],
+        "muon_norm": {"ms": med["muon_norm"], "elems": n_muon / world,
+                      "note": "the sequential fp32 sums of squares of the Newton-Schulz inputs "
+                              "(bf16, 2 B read per element), one launch for every matrix"},
+        "muon_update_ms": med["muon_update"],
         "step_ms_events": med["step"],
         "exchange_exposed_ms": (ms - med["step"]) if world > 1 else None,
         "note": "phase times are averaged over the timed steps. AdamW runs on a side stream "

@@ -430,6 +430,12 @@ int mmn_optim_kernel_launches(mmn_optim_t *h, int64_t *per_step, int64_t *per_re
 int mmn_optim_enable_timing(mmn_optim_t *h, int enable);
 int mmn_optim_last_timing(mmn_optim_t *h, float *ms5);
 
+/* The same breakdown with the Muon momentum pass and the Frobenius norms apart:
+ * [0] AdamW kernel, [1] Muon momentum, [2] Newton-Schulz input norms, [3]
+ * Newton-Schulz GEMMs, [4] Muon update, [5] whole step. On host steps
+ * (mmn_optim_step_host) no events are recorded. */
+int mmn_optim_last_timing_ex(mmn_optim_t *h, float *ms6);
+
 #ifdef __cplusplus
 }
 #endif

@@ -143,6 +143,7 @@ SIGNATURES = {
     "mmn_optim_kernel_launches": (_i, [_vp, _i64p, _i64p]),
     "mmn_optim_enable_timing": (_i, [_vp, _i]),
     "mmn_optim_last_timing": (_i, [_vp, ctypes.POINTER(_f)]),
+    "mmn_optim_last_timing_ex": (_i, [_vp, ctypes.POINTER(_f)]),
 }
 
 _lib = None

@@ -251,10 +251,10 @@ struct mmn_optim {
   cudaGraphExec_t graph = nullptr;
   float graph_divisor = 0.0f;
   bool timing = false;
-  // per-step phase events while timing is on: one set of 8 per step (up to
+  // per-step phase events while timing is on: one set of 9 per step (up to
   // kTimedSteps, then the sets are reused), averaged by mmn_optim_last_timing
   static constexpr size_t kTimedSteps = 4096;
-  std::vector<std::array<cudaEvent_t, 8>> ev_sets;
+  std::vector<std::array<cudaEvent_t, 9>> ev_sets;
   size_t ev_used = 0;
   std::vector<void*> allocs;
 
@@ -913,7 +913,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
   if (tm) {
     const size_t k = h->ev_used % mmn_optim::kTimedSteps;
     if (k == h->ev_sets.size()) {
-      std::array<cudaEvent_t, 8> set{};
+      std::array<cudaEvent_t, 9> set{};
       for (auto& e : set) MMN_CUDA_TRY(cudaEventCreate(&e));
       h->ev_sets.push_back(set);
     }
@@ -1109,6 +1109,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     } else {
       for (int k : h->jobs)
         if (k >= 0) MMN_TRY_RC(prologue(k, false));
+      if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[8], s));
       // the norms of every matrix in one launch: one CTA per matrix, largest
       // first, so the long sequential sums of the large matrices run side by side
       m.mats = h->d_mats;
@@ -1124,6 +1125,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[5], s));
   } else if (tm) {
+    MMN_CUDA_TRY(cudaEventRecord(ev[8], s));
     MMN_CUDA_TRY(cudaEventRecord(ev[4], s));
     MMN_CUDA_TRY(cudaEventRecord(ev[5], s));
   }
@@ -1577,22 +1579,35 @@ extern "C" int mmn_optim_enable_timing(mmn_optim_t* h, int enable) {
   return MMN_OK;
 }
 
-extern "C" int mmn_optim_last_timing(mmn_optim_t* h, float* ms5) {
-  if (!h || !ms5) return fail(MMN_E_INVALID, "null argument");
+// Averages event intervals over the timed steps: out[i] = mean of
+// ev[to[i]] - ev[from[i]].
+static int phase_means(mmn_optim_t* h, const int* from, const int* to, int n_out, float* out) {
   if (!h->timing || h->ev_used == 0) return fail(MMN_E_STATE, "enable timing before the steps");
   DeviceGuard g(h->ctx.device);
   MMN_CUDA_TRY(cudaStreamSynchronize(h->ctx.stream));
   const size_t n = std::min(h->ev_used, mmn_optim::kTimedSteps);
-  double acc[5] = {0, 0, 0, 0, 0};
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   for (size_t k = 0; k < n; ++k) {
     const cudaEvent_t* ev = h->ev_sets[k].data();
-    const int from[5] = {1, 3, 4, 5, 0}, to[5] = {2, 4, 5, 6, 7};
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < n_out; ++i) {
       float ms = 0.0f;
       MMN_CUDA_TRY(cudaEventElapsedTime(&ms, ev[from[i]], ev[to[i]]));
       acc[i] += ms;
     }
   }
-  for (int i = 0; i < 5; ++i) ms5[i] = (float)(acc[i] / (double)n);
+  for (int i = 0; i < n_out; ++i) out[i] = (float)(acc[i] / (double)n);
   return MMN_OK;
+}
+
+extern "C" int mmn_optim_last_timing(mmn_optim_t* h, float* ms5) {
+  if (!h || !ms5) return fail(MMN_E_INVALID, "null argument");
+  const int from[5] = {1, 3, 4, 5, 0}, to[5] = {2, 4, 5, 6, 7};
+  return phase_means(h, from, to, 5, ms5);
+}
+
+extern "C" int mmn_optim_last_timing_ex(mmn_optim_t* h, float* ms6) {
+  if (!h || !ms6) return fail(MMN_E_INVALID, "null argument");
+  // AdamW, momentum, norms, Newton-Schulz, update, step
+  const int from[6] = {1, 3, 8, 4, 5, 0}, to[6] = {2, 8, 4, 5, 6, 7};
+  return phase_means(h, from, to, 6, ms6);
 }

@@ -22,21 +22,25 @@
 // order. The maps S -> S + A and S -> S + A + ((S + B) & 1) are closed under
 // composition (after a tie the running value is even, so a later tie's parity
 // no longer depends on S), which makes the per-element maps an associative
-// monoid: a block reduces (or scans) the maps of its elements in order.
+// monoid: a warp reduces (or scans) the maps of its elements in order.
 //
-// The kernel gives each matrix one CTA, which walks the sequence in tiles of
-// kRnThreads x kRnEpt elements, each thread a run of kRnEpt consecutive ones:
-//   - fast path: compose the tile's element maps in order (thread, warp,
-//     block); if no term was marked for exact handling and the composed map
-//     leaves S <= 2^24 - 1, no add in the tile left the binade (S_i + k_i <=
-//     S_end + 1/2 for every element), and S takes the composed value;
-//   - slow path (a binade change or a term of at least 2^22 units): an
-//     ordered block scan gives every thread the S at its first element;
-//     threads walk their elements to the first one whose add can leave the
-//     binade, that add is done as an fp32 add, and the tile resumes after it
-//     with the new binade.
+// The kernel gives each matrix a cluster of C CTAs, which walks the sequence
+// in cluster steps of consecutive parts, one per CTA; inside a part each warp
+// owns a run of consecutive warp tiles (32 lanes x kRnEpt elements, each lane
+// a run of kRnEpt consecutive ones):
+//   - fast path: compose the element maps in order (lane, warp tile by
+//     shuffles, warp segment, CTA part, cluster step); if no term was marked
+//     for exact handling and the composed map leaves S <= 2^24 - 1, no add in
+//     the step left the binade (S_i + k_i <= S_end + 1/2 for every element),
+//     and S takes the composed value;
+//   - slow path (a binade change or a term of at least 2^22 units): the first
+//     warp tile whose map leaves the binade is walked by its warp: an ordered
+//     warp scan gives every lane the S at its first element, lanes walk their
+//     elements to the first one whose add can leave the binade, that add is
+//     done as an fp32 add, and the walk resumes after it with the new binade;
+//     the cluster step restarts after that warp tile.
 // A binade change happens about log2(N) times per matrix, so nearly every
-// tile takes the fast path; ties (about 1% of the terms of bf16 squares) stay
+// step takes the fast path; ties (about 1% of the terms of bf16 squares) stay
 // on it. The element arithmetic runs on pairs with the packed fp32x2
 // instructions of sm_100. A non-finite running sum ends the walk: fp32
 // addition of the remaining terms (all >= 0 or NaN) then gives NaN if any of
@@ -66,6 +70,7 @@ constexpr int kRnSat = 1 << 25;              // integers at or above 2^24 mean "
 constexpr float kRnBig = 4194304.0f;         // 2^22: larger terms take the exact add
 constexpr uint32_t kRnBigBits = 0x4A800000u; // its bit pattern (NaNs compare above it)
 constexpr float kRnMagic = 12582912.0f;      // 1.5 * 2^23: k + M - M = rint(k) for k < 2^22
+constexpr uint32_t kRnMagicBits = 0x4B400000u;  // its bit pattern
 
 __device__ __forceinline__ int rn_sat(int x) { return x < kRnSat ? x : kRnSat; }
 
@@ -78,38 +83,6 @@ struct RnMap {
   int tie, A, B;
 };
 
-__device__ __forceinline__ RnMap rn_compose(const RnMap a, const RnMap b) {  // a, then b
-  RnMap r;
-  if (!b.tie) {
-    r.tie = a.tie;
-    r.A = rn_sat(a.A + b.A);
-    r.B = a.B;
-  } else if (!a.tie) {
-    r.tie = 1;
-    r.A = rn_sat(a.A + b.A);
-    r.B = rn_sat(a.A + b.B);
-  } else {
-    r.tie = 1;
-    r.A = rn_sat(a.A + b.A + ((a.A + a.B + b.B) & 1));
-    r.B = a.B;
-  }
-  return r;
-}
-
-__device__ __forceinline__ int rn_apply(const RnMap m, int s) {
-  return rn_sat(s + m.A + (m.tie ? ((s + m.B) & 1) : 0));
-}
-
-__device__ __forceinline__ RnMap rn_shfl_down(const RnMap m, int off) {
-  return {__shfl_down_sync(0xffffffffu, m.tie, off), __shfl_down_sync(0xffffffffu, m.A, off),
-          __shfl_down_sync(0xffffffffu, m.B, off)};
-}
-
-__device__ __forceinline__ RnMap rn_shfl_up(const RnMap m, int off) {
-  return {__shfl_up_sync(0xffffffffu, m.tie, off), __shfl_up_sync(0xffffffffu, m.A, off),
-          __shfl_up_sync(0xffffffffu, m.B, off)};
-}
-
 // The binade of the running sum: s = S * 2^(E-23) with S < 2^24 an integer,
 // E >= -126 (the subnormals share the grid of the first normal binade). From
 // the fp32 bit pattern: bits = ((E + 126) << 23) + S.
@@ -120,7 +93,6 @@ struct RnState {
   double scd;  // 2^(23-E)
   bool tiny;   // E < -100: the scale is applied in double (2^(23-E) is beyond
                // the fp32 range); k = t * 2^(23-E) is exact either way
-  int parity;  // shared-slot set of the next fast-path reduction
 };
 
 __device__ __forceinline__ void rn_set(RnState& st, float s) {
@@ -145,6 +117,7 @@ __device__ __forceinline__ float rn_value(const RnState& st, int S) {
 // even; a tie k = q + 1/2 has q = val - neg.
 struct RnPair {
   uint32_t kbits[2];
+  uint32_t ybits[2];  // bit patterns of M + rint(k): val + kRnMagicBits
   int val[2];
   bool tie[2];
   bool neg[2];
@@ -167,8 +140,10 @@ __device__ __forceinline__ RnPair rn_pair(uint32_t w, const RnState& st) {
   RnPair p;
   p.kbits[0] = __float_as_uint(k.x);
   p.kbits[1] = __float_as_uint(k.y);
-  p.val[0] = __float_as_int(y.x) - 0x4B400000;  // rint(k): the low mantissa bits of y
-  p.val[1] = __float_as_int(y.y) - 0x4B400000;
+  p.ybits[0] = __float_as_uint(y.x);
+  p.ybits[1] = __float_as_uint(y.y);
+  p.val[0] = (int)(p.ybits[0] - kRnMagicBits);  // rint(k): the low mantissa bits of y
+  p.val[1] = (int)(p.ybits[1] - kRnMagicBits);
   p.tie[0] = fabsf(d.x) == 0.5f;
   p.tie[1] = fabsf(d.y) == 0.5f;
   p.neg[0] = d.x < 0.0f;
@@ -274,235 +249,91 @@ __device__ __forceinline__ void rn_load_scalar(RnRun& r, const __nv_bfloat16* X,
   }
 }
 
-struct RnShared {
-  uint4 run[kRnGroups][kRnThreads];  // the tile's runs, for the slow path
-  RnMap warp[kRnWarps];
-  RnMap total;
-  int stop;          // first tile-local element needing the exact add
-  uint32_t s_bits;   // running sum after that add
-  // fast-path reduction, double-buffered by tile parity so that a tile needs
-  // two barriers: warp results in, block result out
-  RnMap fwarp[2][kRnWarps];
-  uint32_t fmax[2][kRnWarps];
-  RnMap ftotal[2];
-  uint32_t ftmax[2];
+// Warp form of a map: B < 0 when the map holds no tie (B >= 0 otherwise), so a
+// map crosses a shuffle as two words and composes without branches.
+struct RnWMap {
+  int A, B;
 };
 
-// Fast path: ordered composition of the block's per-thread maps and the max of
-// their k bit patterns, in two barriers (shared slots alternate by tile).
-__device__ __forceinline__ RnMap rn_block_reduce_fast(RnMap m, uint32_t kmax, RnShared& sh,
-                                                      int p, uint32_t* kmax_out) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const RnMap o = rn_shfl_down(m, off);
-    const uint32_t ko = __shfl_down_sync(0xffffffffu, kmax, off);
-    if (lane + off < 32) {
-      m = rn_compose(m, o);
-      kmax = max(kmax, ko);
-    }
-  }
-  if (lane == 0) {
-    sh.fwarp[p][w] = m;
-    sh.fmax[p][w] = kmax;
-  }
-  __syncthreads();
-  if (w == 0) {
-    RnMap t = lane < kRnWarps ? sh.fwarp[p][lane] : RnMap{0, 0, 0};
-    uint32_t km = lane < kRnWarps ? sh.fmax[p][lane] : 0u;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const RnMap o = rn_shfl_down(t, off);
-      const uint32_t ko = __shfl_down_sync(0xffffffffu, km, off);
-      if (lane + off < 32) {
-        t = rn_compose(t, o);
-        km = max(km, ko);
-      }
-    }
-    if (lane == 0) {
-      sh.ftotal[p] = t;
-      sh.ftmax[p] = km;
-    }
-  }
-  __syncthreads();
-  *kmax_out = sh.ftmax[p];
-  return sh.ftotal[p];
+__device__ __forceinline__ RnWMap rn_wmap(const RnMap m) {
+  return {rn_sat(m.A), m.tie ? rn_sat(m.B) : -1};
 }
 
-// Ordered exclusive scan of the per-thread maps (prefix of the threads before
-// this one) and the block total.
-__device__ __forceinline__ RnMap rn_block_scan(RnMap m, RnShared& sh, RnMap* total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  RnMap inc = m;
+__device__ __forceinline__ RnWMap rn_wcompose(const RnWMap a, const RnWMap b) {  // a, then b
+  const bool at = a.B >= 0, bt = b.B >= 0;
+  int A = a.A + b.A;
+  if (at && bt) A += (a.A + a.B + b.B) & 1;
+  const int B = at ? a.B : (bt ? a.A + b.B : -1);
+  return {rn_sat(A), rn_sat(B)};
+}
+
+__device__ __forceinline__ int rn_wapply(const RnWMap m, int s) {
+  return rn_sat(s + m.A + (m.B >= 0 ? ((s + m.B) & 1) : 0));
+}
+
+constexpr int kRnWarpTile = 32 * kRnEpt;  // elements of a warp tile: its lanes' runs in order
+
+// Ordered composition of the lanes' maps; lane 0 receives lanes 0..31 in order
+// (the other lanes' results are partial and unused).
+__device__ __forceinline__ RnWMap rn_warp_reduce(RnWMap m) {
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const RnMap o = rn_shfl_up(inc, off);
-    if (lane >= off) inc = rn_compose(o, inc);
+    const RnWMap o{__shfl_down_sync(0xffffffffu, m.A, off),
+                   __shfl_down_sync(0xffffffffu, m.B, off)};
+    m = rn_wcompose(m, o);
   }
-  RnMap exc = rn_shfl_up(inc, 1);
-  if (lane == 0) exc = RnMap{0, 0, 0};
-  if (lane == 31) sh.warp[w] = inc;
-  __syncthreads();
-  if (w == 0) {
-    RnMap t = lane < kRnWarps ? sh.warp[lane] : RnMap{0, 0, 0};
+  return m;
+}
+
+// Ordered inclusive scan of the lanes' maps.
+__device__ __forceinline__ RnWMap rn_warp_scan(RnWMap m) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const RnMap o = rn_shfl_up(t, off);
-      if (lane >= off) t = rn_compose(o, t);
-    }
-    RnMap te = rn_shfl_up(t, 1);
-    if (lane == 0) te = RnMap{0, 0, 0};
-    if (lane < kRnWarps) sh.warp[lane] = te;  // exclusive prefix of warp `lane`
-    if (lane == kRnWarps - 1) sh.total = t;
+  for (int off = 1; off < 32; off <<= 1) {
+    const RnWMap o{__shfl_up_sync(0xffffffffu, m.A, off), __shfl_up_sync(0xffffffffu, m.B, off)};
+    if (lane >= off) m = rn_wcompose(o, m);
   }
-  __syncthreads();
-  const RnMap r = rn_compose(sh.warp[w], exc);
-  *total = sh.total;
-  __syncthreads();
-  return r;
+  return m;
 }
 
 // The composed map of the run's elements and the max of their k bit patterns.
-// A pair without a tie (98% of pairs) adds its two values at once; the branch
-// is taken per pair.
+// A pair without a tie (98% of pairs) adds the bit patterns of its two M +
+// rint(k) at once (one three-input add); the sum carries kRnMagicBits per
+// element folded so far, modulo 2^32, and loses it at the end. The branch is
+// taken per pair. (A term of 2^22 units or more, or a NaN, leaves A
+// meaningless; kmax sends such a run to the exact walk.)
 template <bool TINY>
 __device__ __forceinline__ RnMap rn_run_fold(const RnRun& r, const RnState& st,
                                              uint32_t* kmax_out) {
   RnMap m{0, 0, 0};
+  uint32_t biased = 0;  // A + (elements folded) * kRnMagicBits, modulo 2^32
   uint32_t kmax = 0;
 #pragma unroll
   for (int i = 0; i < kRnEpt / 2; ++i) {
     const RnPair p = rn_pair<TINY>(r.word(i), st);
     kmax = max(kmax, max(p.kbits[0], p.kbits[1]));
     if (!(p.tie[0] | p.tie[1])) {
-      m.A += p.val[0] + p.val[1];
+      biased += p.ybits[0] + p.ybits[1];
     } else {
-      rn_fold(m, p.val[0], p.tie[0], p.neg[0]);
-      rn_fold(m, p.val[1], p.tie[1], p.neg[1]);
+      RnMap t{m.tie, (int)(biased - (uint32_t)(2 * i) * kRnMagicBits), m.B};
+      rn_fold(t, p.val[0], p.tie[0], p.neg[0]);
+      rn_fold(t, p.val[1], p.tie[1], p.neg[1]);
+      m.tie = t.tie;
+      m.B = t.B;
+      biased = (uint32_t)t.A + (uint32_t)(2 * i + 2) * kRnMagicBits;
     }
   }
+  m.A = (int)(biased - (uint32_t)kRnEpt * kRnMagicBits);
   *kmax_out = kmax;
   return m;
 }
 
-// The word of elements 2i, 2i + 1 of this thread's run, from its shared copy.
-__device__ __forceinline__ uint32_t rn_shared_word(const RnShared& sh, int i) {
-  const uint4 v = sh.run[i / 4][threadIdx.x];
-  const int j = i % 4;
-  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+// The fold while the sum is below 2^-100 (its scale applied in double): out of
+// line, so that its registers stay out of the main loop's.
+__device__ __noinline__ RnMap rn_run_fold_tiny(const RnRun& r, const RnState& st,
+                                               uint32_t* kmax_out) {
+  return rn_run_fold<true>(r, st, kmax_out);
 }
-
-// Slow-path form of rn_run_fold: the run from its shared copy, one pair at a
-// time.
-template <bool TINY>
-__device__ __noinline__ RnMap rn_shared_fold(const RnShared& sh, const RnState& st, int start,
-                                             int base) {
-  RnMap m{0, 0, 0};
-#pragma unroll 1
-  for (int i = 0; i < kRnEpt / 2; ++i) {
-    const RnPair p = rn_pair<TINY>(rn_shared_word(sh, i), st);
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (base + 2 * i + h >= start) rn_fold(m, p.val[h], p.tie[h], p.neg[h]);
-  }
-  return m;
-}
-
-// Runs the sequential sum over one tile (this thread's run r), starting from
-// `st`; returns false when the sum became non-finite (s_out holds it; the
-// caller finishes the NaN check).
-__device__ __forceinline__ bool rn_tile(const RnRun& r, RnState& st, RnShared& sh, float& s_out) {
-  const int base = threadIdx.x * kRnEpt;
-  // fast path: the composed map of the whole tile
-  {
-    uint32_t kmax;
-    const RnMap m = st.tiny ? rn_run_fold<true>(r, st, &kmax) : rn_run_fold<false>(r, st, &kmax);
-    const RnMap tot = rn_block_reduce_fast(rn_fold_sat(m), kmax, sh, st.parity, &kmax);
-    st.parity ^= 1;  // the next tile reduces through the other slots
-    if (kmax < kRnBigBits) {
-      const int s_end = rn_apply(tot, st.S);
-      if (s_end <= (1 << 24) - 1) {
-        st.S = s_end;
-        return true;
-      }
-    }
-  }
-  // slow path: walk to each add that can leave the binade (or has a term of
-  // 2^22 units or more), do it as an fp32 add, resume after it. The runs go
-  // to shared memory so that the rarely taken walk needs no registers of its
-  // own.
-#pragma unroll
-  for (int u = 0; u < kRnGroups; ++u) sh.run[u][threadIdx.x] = r.g[u];
-  int start = 0;
-  while (true) {
-    const RnMap m = st.tiny ? rn_shared_fold<true>(sh, st, start, base)
-                            : rn_shared_fold<false>(sh, st, start, base);
-    RnMap total;
-    const RnMap pre = rn_block_scan(rn_fold_sat(m), sh, &total);
-    if (threadIdx.x == 0) sh.stop = INT_MAX;
-    __syncthreads();
-    int S = rn_apply(pre, st.S);
-    int cand = INT_MAX;
-    uint32_t cand_bits = 0;
-#pragma unroll 1
-    for (int i = 0; i < kRnEpt / 2; ++i) {
-      if (cand == INT_MAX) {
-        const uint32_t w = rn_shared_word(sh, i);
-        const RnPair p = st.tiny ? rn_pair<true>(w, st) : rn_pair<false>(w, st);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (cand == INT_MAX && base + 2 * i + h >= start) {
-            // room below the binade's top, less 1/2 (exact where k can reach it)
-            const float room = __fsub_rn((float)((1 << 24) - S), 0.5f);
-            if (p.kbits[h] >= kRnBigBits || !(__uint_as_float(p.kbits[h]) < room)) {
-              const float xv = __uint_as_float(h ? (w & 0xFFFF0000u) : (w << 16));
-              cand = base + 2 * i + h;
-              cand_bits = __float_as_uint(__fadd_rn(rn_value(st, S), __fmul_rn(xv, xv)));
-            } else {
-              S = rn_step(p.val[h], p.tie[h], p.neg[h], S);
-            }
-          }
-        }
-      }
-    }
-    if (cand != INT_MAX) atomicMin(&sh.stop, cand);
-    __syncthreads();
-    const int stop = sh.stop;
-    if (stop == INT_MAX) {
-      st.S = rn_apply(total, st.S);
-      __syncthreads();
-      return true;
-    }
-    if (cand == stop) sh.s_bits = cand_bits;
-    __syncthreads();
-    const float s = __uint_as_float(sh.s_bits);
-    __syncthreads();
-    if (!isfinite(s)) {
-      s_out = s;
-      return false;
-    }
-    rn_set(st, s);
-    start = stop + 1;
-  }
-}
-
-// Cluster-level slots: one composed map per CTA and exchange parity, and the
-// state a CTA publishes after walking its part of a slow cluster step.
-constexpr int kRnTilesPerExchange = 8;  // CTA tiles folded between cluster exchanges
-
-struct RnClusterSlots {
-  RnMap map[2];
-  uint32_t kmax[2];
-  RnMap all;        // the cluster step's composed map (thread 0's result)
-  uint32_t all_kmax;
-  RnMap tmap[kRnTilesPerExchange];    // this CTA's tile maps of the current step
-  uint32_t tkmax[kRnTilesPerExchange];
-  int bad;            // first tile of this CTA's part whose adds leave the binade
-  int bad_S;          // the running sum (grid units) at that tile's start
-  int first_bad;      // the cluster's first such tile (thread 0's result)
-  uint32_t pub_bits;  // running sum after the exactly walked tile
-  int pub_ok;         // 0: the sum became non-finite there
-};
 
 template <bool VEC>
 __device__ __forceinline__ void rn_load(RnRun& r, const __nv_bfloat16* X, int ld, int m,
@@ -532,131 +363,277 @@ __device__ __forceinline__ void rn_advance(RnCursor& c, long long d, long long d
   }
 }
 
+// Walks one warp tile (the 32 runs from element t0) exactly, on one warp: an
+// ordered warp scan gives every lane the running sum at its first element, the
+// lanes walk their elements to the first add that can leave the binade (or has
+// a term of 2^22 units or more), that add is done as an fp32 add, and the walk
+// resumes after it in the new binade. Returns false when the sum became
+// non-finite (s_out holds it). Taken about log2(length) times per matrix, so
+// it reloads its elements rather than holding registers for them.
+template <bool VEC>
+__device__ __forceinline__ bool rn_warp_walk(const __nv_bfloat16* X, int ld, int m, long long total,
+                                          long long t0, RnState& st, float& s_out) {
+  const int lane = threadIdx.x & 31;
+  const int base = lane * kRnEpt;
+  RnRun r;
+  rn_load<VEC>(r, X, ld, m, total, rn_cursor_at(t0 + base, m));
+  int start = 0;
+  while (true) {
+    // this lane's map over its elements from `start` on (values clamped so a
+    // non-finite or huge term cannot overflow it; the walk stops there anyway)
+    RnMap mm{0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < kRnEpt / 2; ++i) {
+      const RnPair p = st.tiny ? rn_pair<true>(r.word(i), st) : rn_pair<false>(r.word(i), st);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (base + 2 * i + h >= start) rn_fold(mm, min(p.val[h], kRnSat), p.tie[h], p.neg[h]);
+    }
+    const RnWMap inc = rn_warp_scan(rn_wmap(rn_fold_sat(mm)));
+    RnWMap exc{__shfl_up_sync(0xffffffffu, inc.A, 1), __shfl_up_sync(0xffffffffu, inc.B, 1)};
+    if (lane == 0) exc = RnWMap{0, -1};
+    const RnWMap all{__shfl_sync(0xffffffffu, inc.A, 31), __shfl_sync(0xffffffffu, inc.B, 31)};
+    int S = rn_wapply(exc, st.S);
+    int cand = INT_MAX;
+    uint32_t cand_bits = 0;
+#pragma unroll
+    for (int i = 0; i < kRnEpt / 2; ++i) {
+      const uint32_t w = r.word(i);
+      const RnPair p = st.tiny ? rn_pair<true>(w, st) : rn_pair<false>(w, st);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (cand == INT_MAX && base + 2 * i + h >= start) {
+          // room below the binade's top, less 1/2 (exact where k can reach it)
+          const float room = __fsub_rn((float)((1 << 24) - S), 0.5f);
+          if (p.kbits[h] >= kRnBigBits || !(__uint_as_float(p.kbits[h]) < room)) {
+            const float xv = __uint_as_float(h ? (w & 0xFFFF0000u) : (w << 16));
+            cand = base + 2 * i + h;
+            cand_bits = __float_as_uint(__fadd_rn(rn_value(st, S), __fmul_rn(xv, xv)));
+          } else {
+            S = rn_step(p.val[h], p.tie[h], p.neg[h], S);
+          }
+        }
+      }
+    }
+    // lanes after a stop may hold a meaningless S; their candidates come later
+    const int stop = __reduce_min_sync(0xffffffffu, cand);
+    if (stop == INT_MAX) {
+      st.S = rn_wapply(all, st.S);
+      return true;
+    }
+    const float s = __uint_as_float(__shfl_sync(0xffffffffu, cand_bits, stop / kRnEpt));
+    if (!isfinite(s)) {
+      s_out = s;
+      return false;
+    }
+    rn_set(st, s);
+    start = stop + 1;
+  }
+}
+
+// Warp tiles a warp folds between cluster exchanges (at most).
+constexpr int kRnTilesPerExchange = 16;
+
+// Per-CTA slots: each warp's tile maps of the current cluster step and the
+// composed map of its segment.
+struct RnWarpSlots {
+  RnWMap tile[kRnWarps][kRnTilesPerExchange];
+  uint32_t tkmax[kRnWarps][kRnTilesPerExchange];
+  RnWMap seg[kRnWarps];
+  uint32_t skmax[kRnWarps];
+};
+
+// Cluster-level slots: one composed map per CTA and exchange parity, and the
+// state a CTA publishes after walking the cluster step's first bad warp tile.
+struct RnClusterSlots {
+  RnWMap map[2];
+  uint32_t kmax[2];
+  RnWMap all;         // the cluster step's composed map (thread 0's result)
+  uint32_t all_kmax;
+  int bad;            // first warp tile of this CTA's part whose adds leave the binade
+  int bad_S;          // the running sum (grid units) at that warp tile's start
+  int first_bad;      // the cluster's first such warp tile (thread 0's result)
+  uint32_t pub_bits;  // running sum after the exactly walked warp tile
+  int pub_ok;         // 0: the sum became non-finite there
+};
+
 // The sequential sum over the whole oriented matrix X (n x m, row stride ld),
 // computed by the C CTAs of a cluster (C = 1: one CTA). A cluster step is C
-// parts of up to K = kRnTilesPerExchange consecutive CTA tiles; CTA r folds
-// the r-th part, composing its tiles' maps in order. The CTAs then exchange their
-// parts' maps through distributed shared memory, and each composes all of
-// them in order, so every CTA holds the same running state. A cluster step
-// whose composed map leaves the binade (or holds a term of 2^22 grid units or
-// more) is walked part after part and tile after tile, each part starting
-// from the state its predecessor published.
+// consecutive parts of kt CTA tiles each (kt <= kRnTilesPerExchange); inside
+// CTA r's part, warp w owns the w-th of kRnWarps consecutive segments of kt
+// warp tiles and composes its tiles' maps in order with shuffles alone, so
+// the warps run independently between exchanges. At the end of the step the
+// CTA composes its warps' maps, the CTAs exchange their parts' maps through
+// distributed shared memory, and each composes all of them in order, so every
+// CTA holds the same running state. A cluster step whose composed map leaves
+// the binade (or holds a term of 2^22 grid units or more) is resolved at warp
+// tile granularity: its first bad warp tile is walked exactly by one warp, and
+// the cluster restarts after that warp tile (the tiles behind it were folded
+// for the old binade).
 template <bool VEC>
 __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, int m,
-                                               long long total, RnShared& sh,
+                                               long long total, RnWarpSlots& ws,
                                                RnClusterSlots& cs, int C, int crank) {
   namespace cg = cooperative_groups;
   constexpr int K = kRnTilesPerExchange;
   constexpr long long T = (long long)kRnThreads * kRnEpt;  // elements per CTA tile
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   RnState st;
   rn_set(st, 0.0f);
-  st.parity = 0;
   float s_nf = 0.0f;
-  long long done = -1;  // first element of the cluster step where the sum stopped being finite
-  const long long own = (long long)threadIdx.x * kRnEpt;
-  // Tiles per part: a restart refolds at most one cluster step, and early on
-  // the sum changes binade whenever it doubles, so parts grow with the
-  // distance covered (one tile at first, K once the sum is past C K tiles).
-  auto tiles_at = [&](long long e) {
-    const long long k = e / (T * C);
-    return (int)(k < 1 ? 1 : (k > K ? K : k));
+  long long done = -1;  // first element of the warp tile where the sum stopped being finite
+  // Tiles per part. A step that leaves the binade is refolded from the warp
+  // tile after the change, so steps are sized to end before the binade's top:
+  // early on the sum changes binade whenever it doubles, so parts grow with
+  // the distance covered (one tile at first, K once the sum is past C K
+  // tiles); after that, with the growth per element of the last fast step
+  // (rate, in value units), a step covers at most 3/4 of the elements expected
+  // to fit in the room left above S (one tile per part near the top). Every
+  // CTA of the cluster computes the same sizes from the same state.
+  float rate = 0.0f;
+  auto tiles_for = [&](long long e, float s_at) {
+    const long long k0 = e / (T * C);
+    int k = (int)(k0 < 1 ? 1 : (k0 > K ? K : k0));
+    if (rate > 0.0f && !st.tiny) {
+      const float fit = 0.75f * ((float)((1 << 24) - 1) - s_at) / (rate * st.scf) /
+                        (float)(T * C);
+      if (fit < (float)k) k = fit < 1.0f ? 1 : (int)fit;
+    }
+    return k;
   };
-  // this thread's run: one tile further (T) inside the part
-  const long long t_rows = T / m;
-  const int t_cols = (int)(T - t_rows * m);
+  // this thread's first run in the cluster step that starts at e
+  auto run_at = [&](long long e, int kt) {
+    return rn_cursor_at(e + ((long long)crank * kRnWarps + w) * kt * kRnWarpTile +
+                            (long long)lane * kRnEpt,
+                        m);
+  };
+  // one warp tile further inside the warp's segment
+  const long long wt_rows = kRnWarpTile / m;
+  const int wt_cols = (int)(kRnWarpTile - wt_rows * m);
   long long e0 = 0;
-  int kt = tiles_at(0);
-  RnCursor c = rn_cursor_at((long long)crank * kt * T + own, m);
+  int kt = tiles_for(0, 0.0f);
+  RnCursor c = run_at(0, kt);
   RnRun cur, nxt;
   rn_load<VEC>(cur, X, ld, m, total, c);
   int cp = 0;
   while (e0 < total) {
     const long long part = kt * T, step = part * C;
-    const long long part0 = e0 + (long long)crank * part;  // this CTA's part
-    const int kt_next = tiles_at(e0 + step);
-    RnMap acc{0, 0, 0};
+    const long long seg0 = e0 + ((long long)crank * kRnWarps + w) * kt * kRnWarpTile;
+    // the next step's first loads are issued before this step's sum is known:
+    // it is sized from the sum this step is expected to reach
+    const float s_pred = (float)st.S + (st.tiny ? 0.0f : rate * st.scf * (float)step);
+    const int kt_next = tiles_for(e0 + step, s_pred);
+    RnWMap acc{0, -1};
     uint32_t kacc = 0;
     for (int j = 0; j < kt; ++j) {
-      // the next tile's loads fly while this one folds (zeros past the end)
+      // the next warp tile's loads fly while this one folds (zeros past the end)
       if (j + 1 < kt)
-        rn_advance(c, T, t_rows, t_cols, m);
+        rn_advance(c, kRnWarpTile, wt_rows, wt_cols, m);
       else
-        c = rn_cursor_at(e0 + step + (long long)crank * kt_next * T + own, m);
+        c = run_at(e0 + step, kt_next);
       rn_load<VEC>(nxt, X, ld, m, total, c);
-      RnMap tot{0, 0, 0};
+      RnWMap tot{0, -1};
       uint32_t kmax = 0;
-      if (part0 + j * T < total) {  // a tile past the end adds nothing
+      if (seg0 + (long long)j * kRnWarpTile < total) {  // warp-uniform: past the end adds nothing
         const RnMap mm =
-            st.tiny ? rn_run_fold<true>(cur, st, &kmax) : rn_run_fold<false>(cur, st, &kmax);
-        tot = rn_block_reduce_fast(rn_fold_sat(mm), kmax, sh, st.parity, &kmax);
-        st.parity ^= 1;
-        acc = rn_compose(acc, tot);
+            st.tiny ? rn_run_fold_tiny(cur, st, &kmax) : rn_run_fold<false>(cur, st, &kmax);
+        tot = rn_warp_reduce(rn_wmap(mm));
+        kmax = __reduce_max_sync(0xffffffffu, kmax);
+        acc = rn_wcompose(acc, tot);
         kacc = max(kacc, kmax);
       }
-      if (threadIdx.x == 0) {
-        cs.tmap[j] = tot;
-        cs.tkmax[j] = kmax;
+      if (lane == 0) {
+        ws.tile[w][j] = tot;
+        ws.tkmax[w][j] = kmax;
       }
       cur = nxt;
     }
-    RnMap all = acc;
-    uint32_t all_kmax = kacc;
+    if (lane == 0) {
+      ws.seg[w] = acc;
+      ws.skmax[w] = kacc;
+    }
+    __syncthreads();
+    if (w == 0) {  // the CTA's part: its warps' segments in order
+      RnWMap t = lane < kRnWarps ? ws.seg[lane] : RnWMap{0, -1};
+      uint32_t km = lane < kRnWarps ? ws.skmax[lane] : 0u;
+      t = rn_warp_reduce(t);
+      km = __reduce_max_sync(0xffffffffu, km);
+      if (lane == 0) {
+        cs.map[cp] = t;
+        cs.kmax[cp] = km;
+      }
+    }
+    RnWMap all;
+    uint32_t all_kmax;
     const int cp_step = cp;
     if (C > 1) {
       cg::cluster_group cluster = cg::this_cluster();
-      if (threadIdx.x == 0) {
-        cs.map[cp] = acc;
-        cs.kmax[cp] = kacc;
-      }
       cluster.sync();
-      if (threadIdx.x == 0) {
-        RnMap t{0, 0, 0};
+      if (w == 0) {  // lane r reads CTA r's part; the lanes compose them in order
+        RnWMap t{0, -1};
         uint32_t km = 0;
-        for (int r = 0; r < C; ++r) {
-          const RnClusterSlots* rem = cluster.map_shared_rank(&cs, r);
-          t = rn_compose(t, rem->map[cp]);
-          km = max(km, rem->kmax[cp]);
+        if (lane < C) {
+          const RnClusterSlots* rem = cluster.map_shared_rank(&cs, lane);
+          t = rem->map[cp];
+          km = rem->kmax[cp];
         }
-        cs.all = t;
-        cs.all_kmax = km;
+        t = rn_warp_reduce(t);
+        km = __reduce_max_sync(0xffffffffu, km);
+        if (lane == 0) {
+          cs.all = t;
+          cs.all_kmax = km;
+        }
       }
       __syncthreads();
       all = cs.all;
       all_kmax = cs.all_kmax;
-      __syncthreads();
       cp ^= 1;
+    } else {
+      __syncthreads();
+      all = cs.map[0];
+      all_kmax = cs.kmax[0];
     }
     if (all_kmax < kRnBigBits) {
-      const int s_end = rn_apply(all, st.S);
+      const int s_end = rn_wapply(all, st.S);
       if (s_end <= (1 << 24) - 1) {
+        if (!st.tiny) rate = (float)(s_end - st.S) / (st.scf * (float)step);
         st.S = s_end;
         e0 += step;
         kt = kt_next;
         continue;
       }
     }
-    // slow: find the cluster's first tile whose adds leave the binade (or hold
-    // a term of 2^22 units or more), walk that tile exactly, and restart the
-    // cluster step after it (the tiles behind it were folded for the old
-    // binade). Each CTA starts from the composed maps of the parts before its
-    // own and applies its tile maps in order.
+    // slow: the cluster's first warp tile whose adds leave the binade (or hold
+    // a term of 2^22 units or more). Each CTA starts from the composed maps of
+    // the parts before its own and applies its warps' segment maps, then the
+    // failing segment's tile maps, in order.
+    const int units = kRnWarps * kt;  // warp tiles per part
+    RnWMap pre{0, -1};
+    if (C > 1 && w == 0) {  // the parts before this CTA's, composed across lanes
+      if (lane < crank) pre = cg::this_cluster().map_shared_rank(&cs, lane)->map[cp_step];
+      pre = rn_warp_reduce(pre);
+    }
     if (threadIdx.x == 0) {
-      RnMap pre{0, 0, 0};
-      if (C > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
-        for (int r = 0; r < crank; ++r)
-          pre = rn_compose(pre, cluster.map_shared_rank(&cs, r)->map[cp_step]);
-      }
-      int S = rn_apply(pre, st.S);
+      int S = rn_wapply(pre, st.S);
       int bad = INT_MAX;
-      for (int j = 0; j < kt; ++j) {
-        if (part0 + j * T >= total) break;
-        const int next = cs.tkmax[j] >= kRnBigBits ? (1 << 24) : rn_apply(cs.tmap[j], S);
-        if (next >= (1 << 24)) {
-          bad = crank * kt + j;
-          break;
+      const long long p0 = e0 + (long long)crank * part;
+      for (int ww = 0; ww < kRnWarps && bad == INT_MAX; ++ww) {
+        if (ws.skmax[ww] < kRnBigBits) {
+          const int nx = rn_wapply(ws.seg[ww], S);
+          if (nx < (1 << 24)) {
+            S = nx;
+            continue;
+          }
         }
-        S = next;
+        for (int j = 0; j < kt; ++j) {
+          if (p0 + ((long long)ww * kt + j) * kRnWarpTile >= total) break;
+          const int next = ws.tkmax[ww][j] >= kRnBigBits ? (1 << 24) : rn_wapply(ws.tile[ww][j], S);
+          if (next >= (1 << 24)) {
+            bad = crank * units + ww * kt + j;
+            break;
+          }
+          S = next;
+        }
       }
       cs.bad = bad;
       cs.bad_S = S;
@@ -665,10 +642,10 @@ __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, i
     if (C > 1) {
       cg::cluster_group cluster = cg::this_cluster();
       cluster.sync();
-      if (threadIdx.x == 0) {
-        int b = INT_MAX;
-        for (int r = 0; r < C; ++r) b = min(b, cluster.map_shared_rank(&cs, r)->bad);
-        cs.first_bad = b;
+      if (w == 0) {
+        const int b = __reduce_min_sync(
+            0xffffffffu, lane < C ? cluster.map_shared_rank(&cs, lane)->bad : INT_MAX);
+        if (lane == 0) cs.first_bad = b;
       }
       __syncthreads();
       first = cs.first_bad;
@@ -676,18 +653,15 @@ __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, i
       __syncthreads();
       first = cs.bad;
     }
-    if (first == INT_MAX) first = C * kt - 1;  // not expected: the composed check failed
-    const int r_bad = first / kt, j_bad = first % kt;
-    const long long t_bad = e0 + (long long)r_bad * part + (long long)j_bad * T;
-    if (crank == r_bad) {
+    if (first == INT_MAX) first = C * units - 1;  // not expected: the composed check failed
+    const int r_bad = first / units, u_bad = first % units;
+    const long long t_bad = e0 + (long long)r_bad * part + (long long)u_bad * kRnWarpTile;
+    if (crank == r_bad && w == u_bad / kt) {
       RnState sb = st;
       sb.S = cs.bad_S;
-      RnRun tile;
-      rn_load<VEC>(tile, X, ld, m, total, rn_cursor_at(t_bad + own, m));
       float snf = 0.0f;
-      const bool ok = rn_tile(tile, sb, sh, snf);
-      st.parity = sb.parity;
-      if (threadIdx.x == 0) {
+      const bool ok = rn_warp_walk<VEC>(X, ld, m, total, t_bad, sb, snf);
+      if (lane == 0) {
         cs.pub_ok = ok ? 1 : 0;
         cs.pub_bits = ok ? __float_as_uint(rn_value(sb, sb.S)) : __float_as_uint(snf);
       }
@@ -713,9 +687,9 @@ __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, i
       break;
     }
     rn_set(st, sv);
-    e0 = t_bad + T;
-    kt = tiles_at(e0);
-    c = rn_cursor_at(e0 + (long long)crank * kt * T + own, m);
+    e0 = t_bad + kRnWarpTile;
+    kt = tiles_for(e0, (float)st.S);
+    c = run_at(e0, kt);
     rn_load<VEC>(cur, X, ld, m, total, c);
   }
   // the cluster's CTAs stay resident until every remote read is done
@@ -737,7 +711,7 @@ __device__ __forceinline__ float rn_matrix_sum(const __nv_bfloat16* X, int ld, i
 // is a multiple of 8 elements); otherwise the others, element by element.
 template <bool VEC>
 __global__ void __launch_bounds__(kRnThreads) refnorm_kernel(const MuonArgs a, int C) {
-  __shared__ RnShared sh;
+  __shared__ RnWarpSlots ws;
   __shared__ RnClusterSlots cs;
   if (a.skip && *a.skip) return;
   const int crank = C > 1 ? (int)cooperative_groups::this_cluster().block_rank() : 0;
@@ -750,7 +724,7 @@ __global__ void __launch_bounds__(kRnThreads) refnorm_kernel(const MuonArgs a, i
     const int n = mm.transposed ? mm.cols : mm.rows;
     const int m = mm.transposed ? mm.rows : mm.cols;
     if ((m % 8 == 0) != VEC) continue;  // the other instantiation's matrix
-    const float s = rn_matrix_sum<VEC>(X, cp.ld, m, (long long)n * m, sh, cs, C, crank);
+    const float s = rn_matrix_sum<VEC>(X, cp.ld, m, (long long)n * m, ws, cs, C, crank);
     if (crank == 0 && threadIdx.x == 0)
       a.norms[mm.norm_idx] = fmaxf(__fsqrt_rn(s), 1e-7f);  // lib.rs:109
     __syncthreads();

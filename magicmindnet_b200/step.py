@@ -299,10 +299,13 @@ class OptimizerStep:
         N.check(N.lib().mmn_optim_enable_timing(self._h, int(on)))
 
     def last_timing(self) -> dict:
-        ms = (ctypes.c_float * 5)()
-        N.check(N.lib().mmn_optim_last_timing(self._h, ms))
-        return dict(zip(("adamw", "muon_momentum", "newton_schulz", "muon_update", "step"),
-                        list(ms)))
+        """Mean per-step device time (ms) of each phase over the timed steps:
+        AdamW kernel, Muon momentum pass, Newton-Schulz input norms, Newton-
+        Schulz GEMMs, Muon update, whole step."""
+        ms = (ctypes.c_float * 6)()
+        N.check(N.lib().mmn_optim_last_timing_ex(self._h, ms))
+        return dict(zip(("adamw", "muon_momentum", "muon_norm", "newton_schulz", "muon_update",
+                         "step"), list(ms)))
 
     def gather_layout(self) -> dict:
         g = N.GatherLayoutC()
