@@ -327,15 +327,22 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
     }
     return;
   }
+  // The parameters are read in full before the first store: a store through
+  // args.p (or args.p_bf16) may alias a later load as far as the compiler can
+  // tell, so interleaved loads and stores would wait out one memory round trip
+  // each.
   const NsApply ap = args.apply[b];
   const float ls = ap.lr_scale;
   if (!ap.transposed) {
     const long long base = ap.off + (long long)r * args.N + c0;
     float* prow = args.p + base;
     if (row_ok && cols_full && (base & 3) == 0) {
+      float4 pin[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) pin[q] = *reinterpret_cast<const float4*>(prow + q * 4);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float4 pv = *reinterpret_cast<float4*>(prow + q * 4);
+        float4 pv = pin[q];
         pv.x = __fsub_rn(pv.x, __fmul_rn(ls, v[q * 4 + 0]));
         pv.y = __fsub_rn(pv.y, __fmul_rn(ls, v[q * 4 + 1]));
         pv.z = __fsub_rn(pv.z, __fmul_rn(ls, v[q * 4 + 2]));
@@ -359,11 +366,15 @@ __device__ __forceinline__ void poly_finish(const NsGemmArgs& args, int b, int r
     }
   } else if (row_ok) {
     // Parameter element (c, r): consecutive lanes touch consecutive r.
+    float pin[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      pin[j] = c0 + j < args.N ? args.p[ap.off + (long long)(c0 + j) * args.M + r] : 0.0f;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (c0 + j < args.N) {
         const long long idx = ap.off + (long long)(c0 + j) * args.M + r;
-        const float pn = __fsub_rn(args.p[idx], __fmul_rn(ls, v[j]));
+        const float pn = __fsub_rn(pin[j], __fmul_rn(ls, v[j]));
         args.p[idx] = pn;
         if (args.p_bf16) args.p_bf16[idx] = __float2bfloat16_rn(pn);
       }
@@ -385,6 +396,64 @@ __device__ __forceinline__ void ns_mma(uint32_t d, uint64_t da, uint64_t db, uin
     else
       tc_mma_bf16(d, da, db, idesc, accum);
   }
+}
+
+// The fused Muon update of the transposed bf16 Poly for a parameter laid out
+// like X' (not transposed). v[j] is X' element (c0 + j, rw + lane); the warp's
+// 32 x 32 block goes through its shared-memory stage so that eight lanes cover
+// one row, four consecutive columns each: every load and store of X (4 bf16)
+// and of the fp32 parameters (a float4) is then vectorised, and one warp
+// instruction touches four whole 128-byte lines. Same arithmetic as
+// poly_finish. Only full, 16-byte-aligned blocks come here.
+// The caller has staged the block (tst[j * 33 + lane] = v[j]) and passes the
+// fields it needs by value; out of line, so that its registers stay out of the
+// epilogue's. xb: X of this batch item; p: the parameter's first element.
+static __device__ __noinline__ void poly_update_rows(const __nv_bfloat16* xb, int aux_ld, float* p,
+                                              __nv_bfloat16* p_bf16, int N, float coef_a,
+                                              float ls, int c0, int rw, float s,
+                                              const float* tst) {
+  const int lane = threadIdx.x & 31;
+  const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+  // Two halves of four rounds; in each, every load comes before the first
+  // store (a store may alias a later load as far as the compiler can tell).
+#pragma unroll
+  for (int h = 0; h < 8; h += 4) {
+    uint2 xin[4];
+    float4 pin[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int row = c0 + (h + q) * 4 + rsub;
+      xin[q] = *reinterpret_cast<const uint2*>(xb + (long long)row * aux_ld + rw + c4);
+      pin[q] =
+          *reinterpret_cast<const float4*>(p + (long long)row * N + rw + c4);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int rl = (h + q) * 4 + rsub;  // row in the block
+      const long long base = (long long)(c0 + rl) * N + rw + c4;
+      const __nv_bfloat162 x01 = *reinterpret_cast<const __nv_bfloat162*>(&xin[q].x);
+      const __nv_bfloat162 x23 = *reinterpret_cast<const __nv_bfloat162*>(&xin[q].y);
+      const float xv[4] = {__low2float(x01), __high2float(x01), __low2float(x23),
+                           __high2float(x23)};
+      float pv[4] = {pin[q].x, pin[q].y, pin[q].z, pin[q].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float vv = tst[rl * 33 + c4 + i];
+        const float x0 = s != 1.0f ? __fdiv_rn(xv[i], s) : xv[i];
+        const float bs = s != 1.0f ? __fdiv_rn(vv, s) : vv;
+        const float o = op_round<false>(__fadd_rn(__fmul_rn(x0, coef_a), bs));
+        pv[i] = __fsub_rn(pv[i], __fmul_rn(ls, o));
+      }
+      *reinterpret_cast<float4*>(p + base) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+      if (p_bf16) {
+        uint2 u;
+        u.x = pack_bf16x2(pv[0], pv[1]);
+        u.y = pack_bf16x2(pv[2], pv[3]);
+        *reinterpret_cast<uint2*>(p_bf16 + base) = u;
+      }
+    }
+  }
+  __syncwarp();  // the stage is rewritten by the next chunk
 }
 
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false, bool SPLIT = false>
@@ -851,6 +920,22 @@ __global__ void __launch_bounds__(320, 1)
           for (int j = 0; j < 32; ++j)
             if (DUAL) v[j] = __fadd_rn(__fmul_rn(args.coef_b, v[j]), __fmul_rn(args.coef_c, w[j]));
           if (kSwap) {
+            if constexpr (!F32) {
+              if (args.p && !args.apply[b].transposed && c0 + 32 <= args.M &&
+                  rw + 32 <= args.N && ((args.apply[b].off | args.N) & 3) == 0) {
+                float* tst = reinterpret_cast<float*>(epi_stage) + (warp - 2) * 32 * 33;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) tst[j * 33 + lane] = v[j];
+                __syncwarp();
+                const NsApply ap = args.apply[b];
+                poly_update_rows(static_cast<const __nv_bfloat16*>(args.aux) +
+                                     (long long)b * args.aux_bstride,
+                                 args.aux_ld, args.p + ap.off,
+                                 args.p_bf16 ? args.p_bf16 + ap.off : nullptr, args.N,
+                                 args.coef_a, ap.lr_scale, c0, rw, s, tst);
+                continue;
+              }
+            }
             // v[j] is X' element (c0 + j, r): transpose the warp's 32 x 32 block
             // through shared memory so that lane L holds row c0 + L, columns
             // rw .. rw + 31, and finish it like the row-major Poly.
