@@ -456,6 +456,44 @@ static __device__ __noinline__ void poly_update_rows(const __nv_bfloat16* xb, in
   __syncwarp();  // the stage is rewritten by the next chunk
 }
 
+// X' of a full block of the transposed bf16 Poly (no fused update), from the
+// warp's stage (tst[j * 33 + lane] = v[j], v[j] being X' element (c0 + j, rw +
+// lane)): four lanes cover one row, eight consecutive columns each, so X is
+// read and X' written as 16-byte vectors, eight whole rows per instruction.
+// Same arithmetic as poly_finish.
+static __device__ __noinline__ void poly_store_rows(const __nv_bfloat16* xb, __nv_bfloat16* ob,
+                                                    int ld, float coef_a, int c0, int rw, float s,
+                                                    const float* tst) {
+  const int lane = threadIdx.x & 31;
+  const int rsub = lane >> 2, c8 = (lane & 3) * 8;
+  uint4 xin[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    xin[q] = *reinterpret_cast<const uint4*>(xb + (long long)(c0 + q * 8 + rsub) * ld + rw + c8);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int rl = q * 8 + rsub;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xin[q]);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162*>(&xw[i / 2]);
+      const float xv = (i & 1) ? __high2float(x2) : __low2float(x2);
+      const float vv = tst[rl * 33 + c8 + i];
+      const float x0 = s != 1.0f ? __fdiv_rn(xv, s) : xv;
+      const float bs = s != 1.0f ? __fdiv_rn(vv, s) : vv;
+      o[i] = op_round<false>(__fadd_rn(__fmul_rn(x0, coef_a), bs));
+    }
+    uint4 u;
+    u.x = pack_bf16x2(o[0], o[1]);
+    u.y = pack_bf16x2(o[2], o[3]);
+    u.z = pack_bf16x2(o[4], o[5]);
+    u.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(ob + (long long)(c0 + rl) * ld + rw + c8) = u;
+  }
+  __syncwarp();  // the stage is rewritten by the next chunk
+}
+
 template <int BN, bool DUAL, bool B_MN, int EPI, bool PAIR, bool F32 = false, bool SPLIT = false>
 __global__ void __launch_bounds__(320, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1,
@@ -933,6 +971,19 @@ __global__ void __launch_bounds__(320, 1)
                                  args.aux_ld, args.p + ap.off,
                                  args.p_bf16 ? args.p_bf16 + ap.off : nullptr, args.N,
                                  args.coef_a, ap.lr_scale, c0, rw, s, tst);
+                continue;
+              }
+              if (!args.p && c0 + 32 <= args.M && rw + 32 <= args.N &&
+                  args.aux_ld == args.out_ld && args.aux_bstride == args.out_bstride) {
+                float* tst = reinterpret_cast<float*>(epi_stage) + (warp - 2) * 32 * 33;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) tst[j * 33 + lane] = v[j];
+                __syncwarp();
+                poly_store_rows(static_cast<const __nv_bfloat16*>(args.aux) +
+                                    (long long)b * args.aux_bstride,
+                                static_cast<__nv_bfloat16*>(args.out) +
+                                    (long long)b * args.out_bstride,
+                                args.out_ld, args.coef_a, c0, rw, s, tst);
                 continue;
               }
             }
