@@ -176,7 +176,8 @@ cudaError_t launch(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorM
   cfg.gridDim = dim3(grid, 1, 1);
   // Programmatic dependent launch: this grid may be scheduled while the previous
   // kernel on the stream drains (its CTAs take SMs as the previous ones exit);
-  // the kernel's first instruction waits until that kernel has completed.
+  // each CTA sets up its barriers and TMEM, then waits until that kernel has
+  // completed before it touches global memory.
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.numAttrs = 2;

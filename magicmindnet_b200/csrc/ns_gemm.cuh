@@ -518,14 +518,6 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 6);
   uint8_t* epi_stage = smem + STAGES * S::kStageBytes + S::kBarBytes;
 
-  // Launched as a programmatic dependent: nothing of the previous kernel's output
-  // (X, A, A2, the skip flag) is read before it has completed. The next kernel
-  // may then be scheduled; it waits the same way.
-  griddep_wait();
-  griddep_launch_dependents();
-  // A skipped step (non-finite grads) leaves every buffer untouched. Both CTAs
-  // of a pair read the same flag, so both leave before any cluster barrier.
-  if (args.skip && *args.skip) return;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
@@ -565,6 +557,30 @@ __global__ void __launch_bounds__(320, 1)
   if (PAIR) cluster_sync_all();  // peer barriers initialised, both TMEM allocations done
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  // Launched as a programmatic dependent: the setup above touches only this
+  // CTA's shared memory, its TMEM and the tensor-map parameters, so it overlaps
+  // the previous kernel's last tiles (a CTA is placed on an SM only once the
+  // previous kernel's CTA there has left, shared memory and TMEM included).
+  // Nothing in global memory is read or written before the previous kernel has
+  // completed. The next kernel may then be scheduled; it waits the same way.
+  griddep_wait();
+  griddep_launch_dependents();
+  // A skipped step (non-finite grads) leaves every buffer untouched. The flag
+  // is the same for every CTA, so both CTAs of a pair take this path together.
+  if (args.skip && *args.skip) {
+    tc_fence_before();
+    __syncthreads();
+    if (PAIR) cluster_sync_all();
+    if (warp == 1) {
+      tc_fence_after();
+      if (PAIR)
+        tmem_dealloc_pair(tmem_base, S::kTmemCols);
+      else
+        tmem_dealloc(tmem_base, S::kTmemCols);
+    }
+    return;
+  }
   const int num_kb = (args.K + kBK - 1) / kBK;
 
   auto decode = [&](int tile, int& b, int& tm, int& tn) {
