@@ -578,6 +578,19 @@ static int finalize_layout(mmn_optim_t* h) {
     std::stable_sort(ck.begin(), ck.end(), [&](int a, int b) { return per_elem(a) > per_elem(b); });
     std::vector<int> zig;
     for (int lo = 0, hi = nck - 1, front = 1; lo <= hi; front ^= 1) zig.push_back(front ? ck[lo++] : ck[hi--]);
+    if (W > 1 && zig.size() > 1) {
+      // with peers, the last chunk's push is the one no compute hides: the
+      // chunk with the fewest elements goes last (ties keep the later chunk,
+      // so equal chunks keep their order)
+      size_t small = 0;
+      for (size_t i = 1; i < zig.size(); ++i)
+        if (h->chunk_end[zig[i]] - h->chunk_begin[zig[i]] <=
+            h->chunk_end[zig[small]] - h->chunk_begin[zig[small]])
+          small = i;
+      const int last = zig[small];
+      zig.erase(zig.begin() + (long)small);
+      zig.push_back(last);
+    }
     const int P = (int)h->apart_begin4.size();
     std::vector<std::vector<int>> before(zig.size() + 1);  // AdamW parts placed before zig[i]
     for (int p = 0; p < P; ++p) {
