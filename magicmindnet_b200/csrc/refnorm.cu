@@ -151,20 +151,23 @@ __device__ __forceinline__ RnPair rn_pair(uint32_t w, const RnState& st) {
   return p;
 }
 
-// Appends an element to a thread's running map (at most kRnEpt elements of at
-// most 2^22 units each, so no value reaches 2^31 before rn_fold_sat). Ties are
-// about 1% of bf16 squares: they take the branch.
+// Appends an element to a thread's running map. The sums wrap modulo 2^32:
+// with terms below 2^22 units (at most kRnEpt of them) nothing wraps, and a
+// run holding a larger term or a NaN leaves A meaningless, its k bit patterns
+// sending it to the exact walk. Ties are about 1% of bf16 squares: they take
+// the branch.
 __device__ __forceinline__ void rn_fold(RnMap& m, int val, bool tie, bool neg) {
+  const uint32_t a = (uint32_t)m.A, v = (uint32_t)val;
   if (!tie) {
-    m.A += val;
+    m.A = (int)(a + v);
   } else {
-    const int q = val - (neg ? 1 : 0);
+    const uint32_t q = v - (neg ? 1u : 0u);
     if (!m.tie) {
       m.tie = 1;
-      m.A += q;
+      m.A = (int)(a + q);
       m.B = m.A;
     } else {
-      m.A += q + ((m.A + m.B + q) & 1);
+      m.A = (int)(a + q + ((a + (uint32_t)m.B + q) & 1u));
     }
   }
 }
