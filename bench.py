@@ -694,6 +694,33 @@ def run_ours(args, rank, world, local_rank):
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
                "api": "mmn_optim_step_host (pinned host buffers, synchronous)",
                "timing": "host wall clock per step, max over ranks"}
+        if world == 1:
+            # The PCIe floor on this box: the same per-slot copies (grads in on
+            # one stream, params out on another, pinned buffers), no compute.
+            # The grads copied in are the values already there; params are only read.
+            h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+            def copies():
+                for k in range(len(model)):
+                    if pin_g[k] is not None:
+                        with torch.cuda.stream(h2d):
+                            step.grad(k).copy_(pin_g[k], non_blocking=True)
+                    if pin_p[k] is not None:
+                        with torch.cuda.stream(d2h):
+                            pin_p[k].copy_(step.param(k), non_blocking=True)
+                h2d.synchronize()
+                d2h.synchronize()
+
+            torch.cuda.synchronize(dev)
+            copies()
+            t0 = time.perf_counter()
+            for _ in range(3):
+                copies()
+            floor = (time.perf_counter() - t0) * 1e3 / 3
+            e2e["copy_floor_ms"] = floor
+            e2e["vs_copy_floor"] = e_ms / floor
+            e2e["copy_floor"] = ("the same host<->device copies alone, both directions at once "
+                                 "on two streams, host wall clock, mean of 3")
 
     pk, pk_kind = peaks()
     med = {k: (statistics.median(v) if v else 0.0) for k, v in phase.items()}
