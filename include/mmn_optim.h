@@ -411,6 +411,24 @@ int mmn_optim_reduce_grads(mmn_optim_t *h);
  * null grads (they came in here). No counterpart in the reference. */
 int mmn_optim_scan_grads(mmn_optim_t *h, const void *const *grads);
 
+/* The reduction of mmn_optim_reduce_grads on buffers the caller owns, for a
+ * trainer that keeps its grads outside a handle: dst[i] = src[0][i] +
+ * src[1][i] + ... + src[nsrc-1][i] for i in [0, numel), accumulated in fp32 in
+ * source order (MMN_DTYPE_BF16: bf16 inputs, the fp32 sum rounded to bf16
+ * once), the same kernels and arithmetic as the handle's rank-ordered sum.
+ * 2 <= nsrc <= 8. Every pointer is a 16-byte aligned device pointer. dst is
+ * memory of `device`, and either equals one source (an in-place sum) or
+ * overlaps none. A source is memory of `device` or of another GPU that
+ * `device` can reach over NVLink (a peer allocation or a cudaIpcOpenMemHandle
+ * mapping); the call enables peer access to that GPU first. When
+ * nonfinite_flag (an int on `device`) is not NULL, a non-finite sum sets it to
+ * 1; it is never cleared here. Enqueued on `stream` (NULL = legacy default
+ * stream); returns without synchronising. The reference trains on one process
+ * and has no counterpart; this is the data-parallel sum that runs before
+ * crates/mmn-optim/src/lib.rs:41-60 / :141-175 on each rank. */
+int mmn_grad_reduce(const void *const *src, int nsrc, void *dst, int64_t numel, int dtype,
+                    int *nonfinite_flag, int device, void *stream);
+
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
 

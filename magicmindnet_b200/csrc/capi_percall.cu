@@ -663,3 +663,92 @@ extern "C" int mmn_hybrid_step(mmn_hybrid_t* h, uint64_t id, float* param, const
 
 extern "C" mmn_adamw_t* mmn_hybrid_adamw(mmn_hybrid_t* h) { return h ? h->adamw : nullptr; }
 extern "C" mmn_muon_t* mmn_hybrid_muon(mmn_hybrid_t* h) { return h ? h->muon : nullptr; }
+
+// ============================================== grad reduction, caller's buffers
+namespace {
+
+// A source of mmn_grad_reduce: device (or managed) memory of `device`, or of a
+// peer GPU that `device` can reach, with peer access enabled here.
+int check_reduce_source(const void* p, int device, int k) {
+  const std::string what = "src[" + std::to_string(k) + "]";
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MMN_E_INVALID, what + ": not a CUDA pointer");
+  }
+  if (at.type == cudaMemoryTypeManaged) return MMN_OK;
+  if (at.type != cudaMemoryTypeDevice)
+    return fail(MMN_E_INVALID, what + ": host memory where device memory is needed");
+  if (at.device == device) return MMN_OK;
+  int can = 0;
+  if (cudaDeviceCanAccessPeer(&can, device, at.device) != cudaSuccess || !can) {
+    cudaGetLastError();
+    return fail(MMN_E_INVALID, what + ": memory of device " + std::to_string(at.device) +
+                                   ", which device " + std::to_string(device) + " cannot reach");
+  }
+  const cudaError_t e = cudaDeviceEnablePeerAccess(at.device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+  } else if (e != cudaSuccess) {
+    return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+  }
+  return MMN_OK;
+}
+
+}  // namespace
+
+extern "C" int mmn_grad_reduce(const void* const* src, int nsrc, void* dst, int64_t numel,
+                               int dtype, int* nonfinite_flag, int device, void* stream) {
+  if (!src || !dst) return fail(MMN_E_INVALID, "null source list or destination");
+  if (nsrc < 2 || nsrc > kMaxRanks) return fail(MMN_E_INVALID, "nsrc must lie in [2, 8]");
+  if (dtype != MMN_DTYPE_F32 && dtype != MMN_DTYPE_BF16)
+    return fail(MMN_E_INVALID, "unknown dtype");
+  if (numel < 0 || numel > (int64_t(1) << 60)) return fail(MMN_E_INVALID, "numel out of range");
+  for (int k = 0; k < nsrc; ++k)
+    if (!src[k]) return fail(MMN_E_INVALID, "null source pointer");
+  const uintptr_t d0 = reinterpret_cast<uintptr_t>(dst);
+  if (d0 % 16) return fail(MMN_E_INVALID, "dst is not 16-byte aligned");
+  const uintptr_t bytes = (uintptr_t)numel * (dtype == MMN_DTYPE_BF16 ? 2u : 4u);
+  for (int k = 0; k < nsrc; ++k) {
+    const uintptr_t s0 = reinterpret_cast<uintptr_t>(src[k]);
+    if (s0 % 16) return fail(MMN_E_INVALID, "a source is not 16-byte aligned");
+    if (s0 != d0 && s0 < d0 + bytes && d0 < s0 + bytes)
+      return fail(MMN_E_INVALID, "dst overlaps a source it does not equal");
+  }
+  if (nonfinite_flag && reinterpret_cast<uintptr_t>(nonfinite_flag) % 4)
+    return fail(MMN_E_INVALID, "nonfinite_flag is not 4-byte aligned");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(MMN_E_NO_DEVICE, "GPU missing, but CUDA was requested.");
+  }
+  if (device < 0 || device >= count) return fail(MMN_E_INVALID, "device ordinal out of range");
+  int major = 0, minor = 0, sms = 0;
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  if (major != 10 || minor != 0)
+    return fail(MMN_E_NO_DEVICE, "this library is built for sm_100a (B200) devices only");
+  DeviceGuard guard(device);
+  int rc;
+  if ((rc = check_device_ptr(dst, device, "dst")) != MMN_OK) return rc;
+  if (nonfinite_flag && (rc = check_device_ptr(nonfinite_flag, device, "nonfinite_flag")) != MMN_OK)
+    return rc;
+  for (int k = 0; k < nsrc; ++k)
+    if ((rc = check_reduce_source(src[k], device, k)) != MMN_OK) return rc;
+  if (numel == 0) return MMN_OK;
+  GradReduceArgs a{};
+  a.world = nsrc;
+  a.bf16 = dtype == MMN_DTYPE_BF16;
+  a.scan = nonfinite_flag != nullptr;
+  for (int k = 0; k < nsrc; ++k) {
+    a.src[k] = src[k];
+    a.skip_flags[k] = nonfinite_flag;  // one flag: every "rank" slot points at it
+  }
+  a.dst = dst;
+  a.begin = 0;
+  a.end = numel;
+  launch_grad_reduce(a, sms, static_cast<cudaStream_t>(stream));
+  MMN_CUDA_TRY(cudaGetLastError());
+  return MMN_OK;
+}
