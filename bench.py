@@ -372,15 +372,16 @@ def fill_workload(step, workload, model, dev):
     torch.cuda.synchronize(dev)
 
 
-def isolated_kernels(dev, pk, pk_kind, ns_modes=("reference", "tf32")):
+def isolated_kernels(dev, pk, pk_kind, ns_modes=("reference", "tf32", "fp32")):
     """The configurations' isolated kernel workloads, timed with CUDA events in
     the same run after the main workload has freed its memory: the fused AdamW
     over the 2^28-element arena (t = 10, wd 0.1, divisor 4; 28 B per param) and
     Newton-Schulz on 64 x [4096, 4096] + 32 x [4096, 14336] (velocity ~ N(0,
-    1e-3), 5 iterations) in the reference recipe and in the TF32 mode. 3 warm-up
-    and 3 timed steps each; inputs larger than L2. Fractions are of the measured
-    peaks (HBM copy bandwidth; cuBLAS bf16 burst; the dense TF32 peak measured
-    here, before the timed steps)."""
+    1e-3), 5 iterations) in the reference recipe, the TF32 mode and the fp32 mode
+    (the one within 1e-4 of exact Newton-Schulz). 3 warm-up and 3 timed steps
+    each; inputs larger than L2. Fractions are of the measured peaks (HBM copy
+    bandwidth; cuBLAS bf16 burst; the dense TF32 peak measured here, before the
+    timed steps, and a third of it for the fp32 mode's three tf32 products)."""
     import torch
 
     import magicmindnet_b200 as mmn
@@ -419,9 +420,10 @@ def isolated_kernels(dev, pk, pk_kind, ns_modes=("reference", "tf32")):
                           "frac": byts / (ph["adamw"] / 1e3) / 1e9 / pk["hbm_gbs"],
                           "peak": pk["hbm_gbs"], "peak_source": pk_kind,
                           "bytes_per_launch": byts}
+    tf32 = None
     for mode in ns_modes:
         if mode in ("tf32", "fp32"):
-            tf32 = measure_tf32_peak(dev)
+            tf32 = tf32 or measure_tf32_peak(dev)
             peak, src = tf32[0] / (3.0 if mode == "fp32" else 1.0), "measured in this run: " \
                 "cuBLAS tf32 8192^3, best of 10"
         else:
