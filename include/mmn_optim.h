@@ -429,6 +429,20 @@ int mmn_optim_scan_grads(mmn_optim_t *h, const void *const *grads);
 int mmn_grad_reduce(const void *const *src, int nsrc, void *dst, int64_t numel, int dtype,
                     int *nonfinite_flag, int device, void *stream);
 
+/* The sharded non-finite scan of mmn_optim_scan_grads on a buffer the caller
+ * owns: when any of grads[0, numel) (fp32, or bf16 for MMN_DTYPE_BF16) is Inf
+ * or NaN, every flags[k] (k < nflags, 1 <= nflags <= 8) is set to 1; flags are
+ * never cleared here. Each rank scans only its own part of the grads and
+ * raises its peers' flags as well as its own, so the ranks reach one skip
+ * decision while each reads 1/world_size of the grads. grads is a 16-byte
+ * aligned device pointer on `device`; a flag is an int of `device` or of a
+ * peer GPU that `device` can reach (peer access is enabled first). Enqueued on
+ * `stream`; returns without synchronising. The reference checks no grads for
+ * non-finite values and has no counterpart (the loss-scaled step skips on one,
+ * see mmn_optim_step). */
+int mmn_grad_nonfinite_scan(const void *grads, int64_t numel, int dtype, int *const *flags,
+                            int nflags, int device, void *stream);
+
 /* Parameter counts: total registered, stepped by AdamW, stepped by Muon. */
 int mmn_optim_param_counts(mmn_optim_t *h, int64_t *total, int64_t *adamw, int64_t *muon);
 

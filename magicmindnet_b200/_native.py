@@ -138,6 +138,7 @@ SIGNATURES = {
     "mmn_optim_reduce_grads": (_i, [_vp]),
     "mmn_optim_scan_grads": (_i, [_vp, _vp]),
     "mmn_grad_reduce": (_i, [ctypes.POINTER(_vp), _i, _vp, _i64, _i, _vp, _i, _vp]),
+    "mmn_grad_nonfinite_scan": (_i, [_vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _vp]),
     "mmn_optim_plan": (_i, [_i64p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, _i, _i, _i,
                             ctypes.POINTER(_i), _i64p, _i64p, _i64p]),
     "mmn_optim_ns_flops": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),

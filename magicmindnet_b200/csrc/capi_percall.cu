@@ -667,10 +667,10 @@ extern "C" mmn_muon_t* mmn_hybrid_muon(mmn_hybrid_t* h) { return h ? h->muon : n
 // ============================================== grad reduction, caller's buffers
 namespace {
 
-// A source of mmn_grad_reduce: device (or managed) memory of `device`, or of a
-// peer GPU that `device` can reach, with peer access enabled here.
-int check_reduce_source(const void* p, int device, int k) {
-  const std::string what = "src[" + std::to_string(k) + "]";
+// Device (or managed) memory of `device`, or of a peer GPU that `device` can
+// reach, with peer access enabled here: a source of mmn_grad_reduce or a flag
+// of mmn_grad_nonfinite_scan.
+int check_reachable(const void* p, int device, const std::string& what) {
   cudaPointerAttributes at;
   if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
     cudaGetLastError();
@@ -692,6 +692,23 @@ int check_reduce_source(const void* p, int device, int k) {
   } else if (e != cudaSuccess) {
     return cuda_fail(e, "cudaDeviceEnablePeerAccess");
   }
+  return MMN_OK;
+}
+
+// The device checks of the caller-buffer entry points: a usable sm_100 GPU.
+int percall_device(int device, int* sms) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(MMN_E_NO_DEVICE, "GPU missing, but CUDA was requested.");
+  }
+  if (device < 0 || device >= count) return fail(MMN_E_INVALID, "device ordinal out of range");
+  int major = 0, minor = 0;
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+  MMN_CUDA_TRY(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, device));
+  if (major != 10 || minor != 0)
+    return fail(MMN_E_NO_DEVICE, "this library is built for sm_100a (B200) devices only");
   return MMN_OK;
 }
 
@@ -717,25 +734,15 @@ extern "C" int mmn_grad_reduce(const void* const* src, int nsrc, void* dst, int6
   }
   if (nonfinite_flag && reinterpret_cast<uintptr_t>(nonfinite_flag) % 4)
     return fail(MMN_E_INVALID, "nonfinite_flag is not 4-byte aligned");
-  int count = 0;
-  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
-    cudaGetLastError();
-    return fail(MMN_E_NO_DEVICE, "GPU missing, but CUDA was requested.");
-  }
-  if (device < 0 || device >= count) return fail(MMN_E_INVALID, "device ordinal out of range");
-  int major = 0, minor = 0, sms = 0;
-  MMN_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
-  MMN_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
-  MMN_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-  if (major != 10 || minor != 0)
-    return fail(MMN_E_NO_DEVICE, "this library is built for sm_100a (B200) devices only");
+  int sms = 0, rc;
+  if ((rc = percall_device(device, &sms)) != MMN_OK) return rc;
   DeviceGuard guard(device);
-  int rc;
   if ((rc = check_device_ptr(dst, device, "dst")) != MMN_OK) return rc;
   if (nonfinite_flag && (rc = check_device_ptr(nonfinite_flag, device, "nonfinite_flag")) != MMN_OK)
     return rc;
   for (int k = 0; k < nsrc; ++k)
-    if ((rc = check_reduce_source(src[k], device, k)) != MMN_OK) return rc;
+    if ((rc = check_reachable(src[k], device, "src[" + std::to_string(k) + "]")) != MMN_OK)
+      return rc;
   if (numel == 0) return MMN_OK;
   GradReduceArgs a{};
   a.world = nsrc;
@@ -749,6 +756,38 @@ extern "C" int mmn_grad_reduce(const void* const* src, int nsrc, void* dst, int6
   a.begin = 0;
   a.end = numel;
   launch_grad_reduce(a, sms, static_cast<cudaStream_t>(stream));
+  MMN_CUDA_TRY(cudaGetLastError());
+  return MMN_OK;
+}
+
+extern "C" int mmn_grad_nonfinite_scan(const void* grads, int64_t numel, int dtype,
+                                       int* const* flags, int nflags, int device, void* stream) {
+  if (!grads || !flags) return fail(MMN_E_INVALID, "null grads or flag list");
+  if (nflags < 1 || nflags > kMaxRanks) return fail(MMN_E_INVALID, "nflags must lie in [1, 8]");
+  if (dtype != MMN_DTYPE_F32 && dtype != MMN_DTYPE_BF16)
+    return fail(MMN_E_INVALID, "unknown dtype");
+  if (numel < 0 || numel > (int64_t(1) << 60)) return fail(MMN_E_INVALID, "numel out of range");
+  if (reinterpret_cast<uintptr_t>(grads) % 16) return fail(MMN_E_INVALID, "grads is not 16-byte aligned");
+  for (int k = 0; k < nflags; ++k) {
+    if (!flags[k]) return fail(MMN_E_INVALID, "null flag pointer");
+    if (reinterpret_cast<uintptr_t>(flags[k]) % 4)
+      return fail(MMN_E_INVALID, "a flag is not 4-byte aligned");
+  }
+  int sms = 0, rc;
+  if ((rc = percall_device(device, &sms)) != MMN_OK) return rc;
+  DeviceGuard guard(device);
+  if ((rc = check_device_ptr(grads, device, "grads")) != MMN_OK) return rc;
+  for (int k = 0; k < nflags; ++k)
+    if ((rc = check_reachable(flags[k], device, "flags[" + std::to_string(k) + "]")) != MMN_OK)
+      return rc;
+  if (numel == 0) return MMN_OK;
+  RankFlags f{};
+  f.n = nflags;
+  for (int k = 0; k < nflags; ++k) f.flag[k] = flags[k];
+  const bool bf = dtype == MMN_DTYPE_BF16;
+  launch_nonfinite_scan_ranks(bf ? nullptr : static_cast<const float*>(grads), bf ? 0 : numel,
+                              bf ? static_cast<const __nv_bfloat16*>(grads) : nullptr,
+                              bf ? numel : 0, f, sms, static_cast<cudaStream_t>(stream));
   MMN_CUDA_TRY(cudaGetLastError());
   return MMN_OK;
 }

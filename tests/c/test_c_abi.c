@@ -54,6 +54,11 @@ int main(void) {
   CHECK(strlen(mmn_last_error()) > 0);
   CHECK(mmn_optim_step(NULL, 1.0f) == MMN_E_INVALID);
   CHECK(mmn_optim_destroy(NULL) == MMN_OK);
+  const void *srcs[1] = {NULL};
+  CHECK(mmn_grad_reduce(srcs, 1, (void *)srcs, 16, MMN_DTYPE_F32, NULL, 0, NULL) ==
+        MMN_E_INVALID);
+  int *flags[1] = {NULL};
+  CHECK(mmn_grad_nonfinite_scan(NULL, 16, MMN_DTYPE_F32, flags, 1, 0, NULL) == MMN_E_INVALID);
 
   if (failures) {
     fprintf(stderr, "%d check(s) failed\n", failures);

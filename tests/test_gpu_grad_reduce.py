@@ -1,12 +1,15 @@
-"""mmn_grad_reduce: the data-parallel grad reduction (the step before the
-optimizer on each rank) on caller-owned buffers, through the C ABI.
+"""mmn_grad_reduce and mmn_grad_nonfinite_scan: the data-parallel grad
+reduction and the sharded non-finite scan (the steps before the optimizer on
+each rank) on caller-owned buffers, through the C ABI.
 
 The sources stand in for the ranks' local grads. On one GPU they are buffers of
 that GPU, which runs the same kernels that mmn_optim_reduce_grads runs over
 NVLink mappings; the sum must equal the oracle's rank-ordered sum
 (oracle.grad_allreduce) bit for bit, fp32 and bf16, ragged lengths included.
 The non-finite flag is checked both ways, and bad arguments are refused before
-any kernel runs. With two GPUs one source also lives on the peer GPU.
+any kernel runs. The scan raises every rank's flag (here: words of one GPU)
+on one Inf or NaN and none on finite grads. With two GPUs one source, and one
+flag, also live on the peer GPU.
 """
 import ctypes
 
@@ -142,3 +145,82 @@ def test_peer_source_on_a_second_gpu(mmn, oracle):
                     dst.data_ptr(), n, False))
     torch.cuda.synchronize(0)
     np.testing.assert_array_equal(_host(dst, oracle).view(np.uint32), want.view(np.uint32))
+
+
+def _scan(grads, numel, bf16, flags, device=0):
+    import torch
+
+    from magicmindnet_b200 import _native as N
+
+    arr = (ctypes.c_void_p * len(flags))(*[ctypes.c_void_p(p) for p in flags])
+    return N.lib().mmn_grad_nonfinite_scan(
+        ctypes.c_void_p(grads), numel, N.DTYPE_BF16 if bf16 else N.DTYPE_F32, arr, len(flags),
+        device, ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+
+
+@pytest.mark.parametrize("bf16", [False, True], ids=["f32", "bf16"])
+@pytest.mark.parametrize("n", [1, 13, 4096, (1 << 22) + 7])
+def test_sharded_scan_raises_every_rank_flag(mmn, bf16, n):
+    """The sharded scan's kernel (each rank scans its part and raises all ranks'
+    flags), with the ranks' flags as words of one GPU: a clean part raises
+    none, one Inf or NaN anywhere (vector body or scalar tail) raises all."""
+    import torch
+
+    from magicmindnet_b200 import _native as N
+
+    dt = torch.bfloat16 if bf16 else torch.float32
+    g = torch.empty(n, device="cuda", dtype=dt).normal_(0, 1e-3)
+    flags = torch.zeros(8, dtype=torch.int32, device="cuda")
+    ptrs = [flags.data_ptr() + 4 * k for k in range(8)]
+    N.check(_scan(g.data_ptr(), n, bf16, ptrs))
+    torch.cuda.synchronize()
+    assert int(flags.sum().item()) == 0
+    for pos, bad in [(n - 1, float("inf")), (n // 2, float("nan")), (0, float("-inf"))]:
+        g2 = g.clone()
+        g2[pos] = bad
+        flags.zero_()
+        N.check(_scan(g2.data_ptr(), n, bf16, ptrs[:5]))
+        torch.cuda.synchronize()
+        assert flags.cpu().tolist() == [1] * 5 + [0] * 3, (pos, bad)
+    # the largest finite values are not flagged
+    g.fill_(torch.finfo(dt).max)
+    flags.zero_()
+    N.check(_scan(g.data_ptr(), n, bf16, ptrs))
+    torch.cuda.synchronize()
+    assert int(flags.sum().item()) == 0
+
+
+def test_sharded_scan_refuses_bad_arguments(mmn):
+    import torch
+
+    from magicmindnet_b200 import _native as N
+
+    g = torch.zeros(64, device="cuda")
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    f = [flags.data_ptr(), flags.data_ptr() + 4]
+    assert _scan(g.data_ptr() + 4, 32, False, f) == N.MMN_E_INVALID  # misaligned grads
+    assert _scan(g.data_ptr(), 32, False, []) == N.MMN_E_INVALID
+    assert _scan(g.data_ptr(), 32, False, f * 5) == N.MMN_E_INVALID  # ten flags
+    assert _scan(g.data_ptr(), 32, False, [flags.data_ptr() + 2]) == N.MMN_E_INVALID
+    host = np.zeros(8, np.int32)
+    assert _scan(g.data_ptr(), 32, False, [host.ctypes.data]) == N.MMN_E_INVALID
+    assert _scan(g.data_ptr(), -1, False, f) == N.MMN_E_INVALID
+    N.check(_scan(g.data_ptr(), 0, False, f))
+    torch.cuda.synchronize()
+    assert int(flags.sum().item()) == 0
+
+
+def test_sharded_scan_raises_a_peer_flag(mmn):
+    import torch
+
+    from magicmindnet_b200 import _native as N
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    g = torch.zeros(1000, device="cuda:0")
+    g[999] = float("nan")
+    mine = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    peer = torch.zeros(1, dtype=torch.int32, device="cuda:1")
+    N.check(_scan(g.data_ptr(), 1000, False, [mine.data_ptr(), peer.data_ptr()]))
+    torch.cuda.synchronize(0)
+    assert int(mine.item()) == 1 and int(peer.item()) == 1
