@@ -242,3 +242,32 @@ def _header_functions():
         args = m.group(2).strip()
         out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
     return out
+
+
+def test_caller_buffer_reduction_checks_arguments_before_the_device():
+    """mmn_grad_reduce / mmn_grad_nonfinite_scan refuse bad arguments before
+    touching a device, and without a GPU a well-formed call reports the CUDA
+    gate's error (CUDAError), never a CPU result."""
+    from magicmindnet_b200 import _native as N
+
+    L = N.lib()
+    vp = ctypes.c_void_p
+    two = (vp * 2)(vp(0x10000), vp(0x20000))
+    assert L.mmn_grad_reduce(two, 1, vp(0x30000), 64, N.DTYPE_F32, None, 0, None) == \
+        N.MMN_E_INVALID  # one source
+    assert L.mmn_grad_reduce(two, 2, vp(0x30004), 64, N.DTYPE_F32, None, 0, None) == \
+        N.MMN_E_INVALID  # misaligned destination
+    assert L.mmn_grad_reduce(two, 2, vp(0x10010), 64, N.DTYPE_F32, None, 0, None) == \
+        N.MMN_E_INVALID  # overlaps the first source
+    assert L.mmn_grad_reduce(two, 2, vp(0x30000), 64, 7, None, 0, None) == N.MMN_E_INVALID
+    # well formed: the CUDA gate without a GPU; with one, the made-up addresses
+    # are refused as not CUDA memory before any kernel is launched
+    gate = N.MMN_E_INVALID if L.mmn_cuda_is_available() else N.MMN_E_NO_DEVICE
+    rc = L.mmn_grad_reduce(two, 2, vp(0x30000), 64, N.DTYPE_BF16, None, 0, None)
+    assert rc == gate and L.mmn_last_error()
+    flags = (vp * 1)(vp(0x40000))
+    assert L.mmn_grad_nonfinite_scan(vp(0x10008), 64, N.DTYPE_F32, flags, 1, 0, None) == \
+        N.MMN_E_INVALID  # misaligned grads
+    assert L.mmn_grad_nonfinite_scan(vp(0x10000), 64, N.DTYPE_F32, flags, 0, 0, None) == \
+        N.MMN_E_INVALID  # no flags
+    assert L.mmn_grad_nonfinite_scan(vp(0x10000), 64, N.DTYPE_F32, flags, 1, 0, None) == gate
