@@ -229,9 +229,12 @@ struct mmn_optim {
   int* rank_skip[8] = {};
   bool reduce_ready = false;
   int64_t m_own_begin = 0, m_own_end = 0;
-  cudaStream_t xfer = nullptr;
+  // one transfer stream per peer (and its end-of-step event), so that the
+  // pushes to the peers run on several copy engines at once
+  cudaStream_t xfer[mmn::kMaxRanks - 1] = {};
+  cudaEvent_t xfer_done[mmn::kMaxRanks - 1] = {};
   std::vector<cudaEvent_t> chunk_ev;
-  cudaEvent_t adamw_ev = nullptr, xfer_done = nullptr;
+  cudaEvent_t adamw_ev = nullptr;
   std::vector<int> cls_base;    // first norm / apply slot of every class
   int total_tiles = 0;
   double ns_flops = 0.0;
@@ -336,7 +339,8 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   if (h->fork) cudaEventDestroy(h->fork);
   if (h->join) cudaEventDestroy(h->join);
   if (h->side) cudaStreamDestroy(h->side);
-  if (h->xfer) cudaStreamDestroy(h->xfer);
+  for (auto st : h->xfer)
+    if (st) cudaStreamDestroy(st);
   if (h->h2d) cudaStreamDestroy(h->h2d);
   if (h->d2h) cudaStreamDestroy(h->d2h);
   for (auto e : h->chunk_ev)
@@ -346,7 +350,8 @@ extern "C" int mmn_optim_destroy(mmn_optim_t* h) {
   for (auto e : h->apart_ev)
     if (e) cudaEventDestroy(e);
   if (h->adamw_ev) cudaEventDestroy(h->adamw_ev);
-  if (h->xfer_done) cudaEventDestroy(h->xfer_done);
+  for (auto e : h->xfer_done)
+    if (e) cudaEventDestroy(e);
   if (h->d2h_done) cudaEventDestroy(h->d2h_done);
   if (h->work) cudaStreamDestroy(h->work);
   if (h->in_ev) cudaEventDestroy(h->in_ev);
@@ -684,11 +689,13 @@ static int finalize_layout(mmn_optim_t* h) {
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->out_ev, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->fork, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->join, cudaEventDisableTiming));
-  MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->xfer, cudaStreamNonBlocking));
+  for (int r = 0; r + 1 < h->cfg.world_size && r < mmn::kMaxRanks - 1; ++r) {
+    MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->xfer[r], cudaStreamNonBlocking));
+    MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->xfer_done[r], cudaEventDisableTiming));
+  }
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->h2d, cudaStreamNonBlocking));
   MMN_CUDA_TRY(cudaStreamCreateWithFlags(&h->d2h, cudaStreamNonBlocking));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->adamw_ev, cudaEventDisableTiming));
-  MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->xfer_done, cudaEventDisableTiming));
   MMN_CUDA_TRY(cudaEventCreateWithFlags(&h->d2h_done, cudaEventDisableTiming));
   h->chunk_ev.assign(h->chunk_begin.size(), nullptr);
   for (auto& e : h->chunk_ev) MMN_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -843,16 +850,21 @@ extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
   return MMN_OK;
 }
 
-// Copies elements [lo, hi) of a local parameter arena (fp32, or bf16 when the
-// copies are kept) into the same range of every peer's arena on the transfer
-// stream (copy engines over NVLink through the IPC mappings).
-static int copy_to_peers(mmn_optim_t* h, void* local, void* const* peers, int64_t lo, int64_t hi) {
+// Once `ready` has completed, copies elements [lo, hi) of a local parameter
+// arena (fp32, or bf16 when the copies are kept) into the same range of every
+// peer's arena (copy engines over NVLink through the IPC mappings). Each peer
+// has a transfer stream of its own: the copies to the peers run side by side
+// on several copy engines, where one stream would run them one after another.
+static int copy_to_peers(mmn_optim_t* h, cudaEvent_t ready, void* local, void* const* peers,
+                         int64_t lo, int64_t hi) {
   if (hi <= lo) return MMN_OK;
   const size_t es = h->cfg.bf16_param_shadow ? 2 : 4;
   const uint8_t* src = static_cast<const uint8_t*>(local) + (size_t)lo * es;
-  for (int r = 0; r < h->n_peers; ++r)
+  for (int r = 0; r < h->n_peers; ++r) {
+    MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer[r], ready, 0));
     MMN_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(peers[r]) + (size_t)lo * es, src,
-                                 (size_t)(hi - lo) * es, cudaMemcpyDeviceToDevice, h->xfer));
+                                 (size_t)(hi - lo) * es, cudaMemcpyDeviceToDevice, h->xfer[r]));
+  }
   return MMN_OK;
 }
 
@@ -1023,10 +1035,8 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
         launch_adamw(a, h->ctx.num_sms, h->side);
         MMN_CUDA_TRY(cudaGetLastError());
         MMN_CUDA_TRY(cudaEventRecord(h->apart_ev[p], h->side));
-        if (h->n_peers) {
-          MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->apart_ev[p], 0));
-          MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
-        }
+        if (h->n_peers)
+          MMN_TRY_RC(copy_to_peers(h, h->apart_ev[p], a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
       }
     } else {
       a.begin4 = std::min<long long>(h->a_region4 * R, h->a_used4);
@@ -1036,8 +1046,7 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       if (h->n_peers) {
         // this rank's AdamW range goes to every peer while the Muon work runs
         MMN_CUDA_TRY(cudaEventRecord(h->adamw_ev, h->side));
-        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->adamw_ev, 0));
-        MMN_TRY_RC(copy_to_peers(h, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
+        MMN_TRY_RC(copy_to_peers(h, h->adamw_ev, a_src, h->peer_a, a.begin4 * 4, a.end4 * 4));
       }
     }
     if (tm) MMN_CUDA_TRY(cudaEventRecord(ev[2], h->side));
@@ -1106,8 +1115,8 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
       if (h->n_peers) {
         // the chunk's parameters are final: copy engines push them over NVLink
         // while the next chunk computes
-        MMN_CUDA_TRY(cudaStreamWaitEvent(h->xfer, h->chunk_ev[k], 0));
-        MMN_TRY_RC(copy_to_peers(h, h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
+        MMN_TRY_RC(copy_to_peers(h, h->chunk_ev[k],
+                                 h->cfg.bf16_param_shadow ? (void*)h->mp16 : (void*)h->mp,
                                  h->peer_m, h->chunk_begin[k], h->chunk_end[k]));
       }
       return MMN_OK;
@@ -1160,9 +1169,9 @@ static int enqueue_step(mmn_optim_t* h, float divisor, const HostIO* io) {
     MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->d2h_done, 0));
   }
   MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->join, 0));
-  if (h->n_peers) {
-    MMN_CUDA_TRY(cudaEventRecord(h->xfer_done, h->xfer));
-    MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->xfer_done, 0));
+  for (int r = 0; r < h->n_peers; ++r) {
+    MMN_CUDA_TRY(cudaEventRecord(h->xfer_done[r], h->xfer[r]));
+    MMN_CUDA_TRY(cudaStreamWaitEvent(s, h->xfer_done[r], 0));
   }
   StepTail t{};
   t.step_counter = h->d_step;
