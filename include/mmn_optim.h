@@ -365,8 +365,8 @@ int mmn_optim_plan(const int64_t *shapes, const int *ndims, const int *routes, i
 /* Parameter exchange fused into the step (world_size > 1), in place of a
  * post-step all-gather. After mmn_optim_connect_peers the step pushes each
  * finished piece of this rank's regions into every peer's arena at the same
- * offset, over NVLink through CUDA IPC mappings, on a transfer stream of its
- * own: the AdamW range once its kernel ends, and the Newton-Schulz matrices in
+ * offset, over NVLink through CUDA IPC mappings, on transfer streams of its
+ * own (one per peer): the AdamW range once its kernel ends, and the Newton-Schulz matrices in
  * chunks (runs of at most 16 matrices of one shape, largest first), each as
  * soon as its last iteration ends, so the copies overlap the chunks still
  * computing. fp32 params are sent, or only the bf16 copies when

@@ -229,8 +229,8 @@ struct mmn_optim {
   int* rank_skip[8] = {};
   bool reduce_ready = false;
   int64_t m_own_begin = 0, m_own_end = 0;
-  // one transfer stream per peer (and its end-of-step event), so that the
-  // pushes to the peers run on several copy engines at once
+  // one transfer stream per peer (and its end-of-step event): no peer's push
+  // waits behind another's
   cudaStream_t xfer[mmn::kMaxRanks - 1] = {};
   cudaEvent_t xfer_done[mmn::kMaxRanks - 1] = {};
   std::vector<cudaEvent_t> chunk_ev;
@@ -853,8 +853,9 @@ extern "C" int mmn_optim_get_adamw_step(mmn_optim_t* h, uint64_t* step) {
 // Once `ready` has completed, copies elements [lo, hi) of a local parameter
 // arena (fp32, or bf16 when the copies are kept) into the same range of every
 // peer's arena (copy engines over NVLink through the IPC mappings). Each peer
-// has a transfer stream of its own: the copies to the peers run side by side
-// on several copy engines, where one stream would run them one after another.
+// has a transfer stream of its own, so the copies to the peers may run side by
+// side. (On 8 B200s this measured the same as one stream for all peers: the
+// copy-engine pushes reach about 400 GB/s of egress per rank either way.)
 static int copy_to_peers(mmn_optim_t* h, cudaEvent_t ready, void* local, void* const* peers,
                          int64_t lo, int64_t hi) {
   if (hi <= lo) return MMN_OK;
